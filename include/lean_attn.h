@@ -1,0 +1,155 @@
+/*
+ * lean_attn.h — C ABI of the B200 (sm_100a) paged-attention backend for the
+ * lean-infer Qwen3 engine.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, and
+ * the CUDA stream to launch on; none allocates device memory, synchronises the
+ * host or calls exit/abort. Each returns LA_OK or an la_status code; argument
+ * errors are reported before anything is launched. Conditions that can only be
+ * seen on the device (a block id outside the pool, a sequence longer than its
+ * block table, a bounded wait that ran out) are recorded in the caller's
+ * optional device error word (`dev_error`, one int32 in device memory; the
+ * first non-zero code wins) and the offending access is skipped.
+ *
+ * Layout contract (reference: leaninfer/engine/cache_manager.py:53-60, 63-76):
+ *   k_cache / v_cache : [num_blocks, block_size, num_kv_heads, head_dim] bf16,
+ *                       head_dim contiguous; the block/token/head strides are
+ *                       passed explicitly so a layer slice of the engine's
+ *                       [L, NB, BS, Hkv, D] pool can be used in place.
+ *   block_table       : [batch, max_blocks_per_seq] int32, logical block ->
+ *                       physical block id. Block 0 is the engine's trash block.
+ *   cache_seqlens     : [batch] int32, number of valid keys per sequence.
+ *
+ * Graph capture: all launches are asynchronous on `stream`, use a grid that
+ * does not depend on device data, and take their scratch from the caller, so
+ * a sequence of calls can be captured in a CUDA graph. Call la_init() for the
+ * device once before the first capture.
+ */
+#ifndef LEAN_ATTN_H_
+#define LEAN_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LA_VERSION 1
+
+typedef enum {
+  LA_OK = 0,
+  LA_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, inconsistent shapes */
+  LA_ERR_UNSUPPORTED = 2,      /* a shape the kernels are not built for (e.g. head_dim != 128) */
+  LA_ERR_ALIGNMENT = 3,        /* pointer or stride not aligned as TMA / vector loads need */
+  LA_ERR_WORKSPACE = 4,        /* workspace missing or smaller than la_*_workspace_size() */
+  LA_ERR_CUDA = 5,             /* a CUDA runtime/driver call failed (see la_last_cuda_error) */
+  LA_ERR_TENSOR_MAP = 6        /* cuTensorMapEncodeTiled rejected a descriptor */
+} la_status;
+
+/* Codes written to the device error word. */
+#define LA_DEVERR_WAIT_TIMEOUT 1   /* a bounded mbarrier wait ran out; kernel returned early */
+#define LA_DEVERR_BLOCK_ID 2       /* block_table entry outside [0, num_blocks) */
+#define LA_DEVERR_SEQLEN 3         /* a sequence needs more blocks than max_blocks_per_seq */
+#define LA_DEVERR_ROPE_POS 4       /* a position is outside the rope table */
+
+int la_version(void);
+const char* la_status_string(int status);
+/* The last CUDA error code seen by the library on this thread (0 if none). */
+int la_last_cuda_error(void);
+
+/* Per-device one-time setup: shared-memory opt-in of every kernel and module
+ * load. Call before capturing any call into a CUDA graph. Idempotent. */
+int la_init(int device);
+
+/* ------------------------------------------------------------------------
+ * (a) Fused pre-attention: per-head QK RMSNorm, NeoX RoPE and paged KV write.
+ *
+ * Replaces, for one layer, the op sequence of leaninfer/qwen3/model.py:50-55:
+ *   q = q_norm(q_proj(x)); k = k_norm(k_proj(x))          (model.py:50-51)
+ *   q = apply_rope(q, cos, sin); k = apply_rope(k, ...)    (model.py:53-54,
+ *                                                           layers.py:18-23)
+ *   cache.write(layer, block_tables, pos, k, v)            (model.py:55,
+ *                                                           cache_manager.py:63-76)
+ * with the rounding order of the reference: RMSNorm in fp32 (weight multiply
+ * included) rounded once to bf16; x*cos, rotate_half(x)*sin and their sum each
+ * rounded to bf16. rope_cos / rope_sin are [rope_max_pos, head_dim/2] bf16
+ * tables indexed by absolute position (the first half of build_rope's
+ * cat(angles, angles), layers.py:7-15).
+ *
+ * Tokens: if cu_seqlens is NULL, num_tokens = num_seqs * q_len and token i is
+ * position seq_start_pos[i / q_len] + i % q_len of sequence i / q_len
+ * (decode: q_len = 1). Otherwise token i belongs to the sequence s with
+ * cu_seqlens[s] <= i < cu_seqlens[s+1] (packed varlen prefill).
+ * q / k / v: [num_tokens, heads, head_dim] with the given element strides.
+ * q_out receives the normed, rotated q; k (normed, rotated) and v are written
+ * to k_cache / v_cache at block_table[s][col / block_size], col % block_size.
+ * ------------------------------------------------------------------------ */
+int la_qk_norm_rope_paged_write(
+    const void* q, int64_t q_token_stride, int64_t q_head_stride,
+    const void* k, int64_t k_token_stride, int64_t k_head_stride,
+    const void* v, int64_t v_token_stride, int64_t v_head_stride,
+    const void* q_norm_weight, const void* k_norm_weight, float eps,
+    const void* rope_cos, const void* rope_sin, int64_t rope_max_pos,
+    const int64_t* seq_start_pos, const int32_t* cu_seqlens,
+    int num_seqs, int q_len, int64_t num_tokens,
+    const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
+    void* k_cache, void* v_cache,
+    int64_t kv_block_stride, int64_t kv_token_stride, int64_t kv_head_stride,
+    int64_t num_blocks, int block_size,
+    void* q_out, int64_t qo_token_stride, int64_t qo_head_stride,
+    int num_q_heads, int num_kv_heads, int head_dim,
+    int* dev_error, cudaStream_t stream);
+
+/* Plain paged KV write (no norm, no rope): the scatter of BlockCache.write
+ * (leaninfer/engine/cache_manager.py:63-76). k / v: [num_tokens, Hkv, D]. */
+int la_paged_kv_write(
+    const void* k, int64_t k_token_stride, int64_t k_head_stride,
+    const void* v, int64_t v_token_stride, int64_t v_head_stride,
+    const int64_t* seq_start_pos, const int32_t* cu_seqlens,
+    int num_seqs, int q_len, int64_t num_tokens,
+    const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
+    void* k_cache, void* v_cache,
+    int64_t kv_block_stride, int64_t kv_token_stride, int64_t kv_head_stride,
+    int64_t num_blocks, int block_size,
+    int num_kv_heads, int head_dim,
+    int* dev_error, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------
+ * (b) Paged GQA decode attention, split-KV with a combine pass.
+ *
+ * Replaces flash_attn.flash_attn_with_kvcache(q, k_cache, v_cache,
+ * cache_seqlens=, block_table=, causal=True, num_splits=1) as called at
+ * leaninfer/qwen3/model.py:60-67 (one query token per sequence).
+ * q: [batch, 1, num_q_heads, head_dim] bf16; out: same shape. Query head h
+ * attends to kv head h / (num_q_heads / num_kv_heads) over keys
+ * 0 .. cache_seqlens[b]-1. softmax_lse (nullable): [batch, num_q_heads] fp32,
+ * natural log. A sequence with cache_seqlens[b] <= 0 gets a zero output and
+ * lse = -inf. block_size must be a multiple of 16; head_dim must be 128;
+ * num_kv_heads must divide 8 and num_q_heads / num_kv_heads must be <= 8.
+ * workspace: device memory of at least la_paged_decode_workspace_size() bytes
+ * (partial results of sequences split across CTAs), 256-byte aligned.
+ * ------------------------------------------------------------------------ */
+int la_paged_decode_workspace_size(int device, int num_q_heads, int num_kv_heads, int head_dim,
+                                   size_t* bytes);
+
+int la_paged_decode(
+    const void* q, int64_t q_batch_stride, int64_t q_head_stride,
+    const void* k_cache, const void* v_cache,
+    int64_t kv_block_stride, int64_t kv_token_stride, int64_t kv_head_stride,
+    int64_t num_blocks, int block_size,
+    const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
+    const int32_t* cache_seqlens,
+    int batch, int num_q_heads, int num_kv_heads, int head_dim,
+    float softmax_scale,
+    void* out, int64_t out_batch_stride, int64_t out_head_stride,
+    float* softmax_lse,
+    void* workspace, size_t workspace_bytes,
+    int* dev_error, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEAN_ATTN_H_ */

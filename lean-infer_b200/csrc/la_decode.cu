@@ -1,0 +1,690 @@
+// (b) Paged GQA decode attention for sm_100a: a persistent, warp-specialised
+// split-KV kernel plus a combine kernel.
+//
+// Semantics (leaninfer/qwen3/model.py:60-67 -> flash_attn_with_kvcache with a
+// block table, one query token, causal bottom-right alignment, which at
+// q_len = 1 means "all keys 0..cache_seqlens[b]-1"):
+//   out[b, h] = softmax(scale * q[b, h] . K[b, :, h / G]^T) . V[b, :, h / G]
+// where K[b, t] = k_cache[block_table[b, t / BS], t % BS].
+//
+// Work decomposition. The key range of every sequence is cut into units of
+// TC = 16 * (8 / Hkv) tokens; a unit is one pipeline stage: 128 (token, kv
+// head) rows of K and of V, 32 KB each. The units of all sequences, laid end
+// to end, are split into gridDim.x equal contiguous ranges, one per CTA
+// (grid = #SMs, one CTA per SM), so every SM streams the same number of bytes
+// whatever the length mix. The partition is recomputed on the device from
+// cache_seqlens, so the launch shape never depends on device data and the
+// call can be captured in a CUDA graph. A CTA range covers whole sequences
+// (written straight to `out`) and at most two partial sequences at its ends
+// (written as fp32 (O, lse) partials to the workspace and merged by the
+// combine kernel).
+//
+// CTA: warp 8 is the producer (partition walk, block-table lookups, TMA
+// issue); warps 0-7 consume. Consumer warp w handles kv head w % Hkv and the
+// 16-token sub-chunk w / Hkv of each stage: S^T = K Q^T and O^T += V^T P^T on
+// mma.m16n8k16 (bf16 in, fp32 accumulate) with K/V fragments read by ldmatrix
+// from 128-byte-swizzled TMA tiles, online softmax in fp32 with warp-shuffle
+// max reductions, P transposed into the B operand with movmatrix.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <utility>
+
+#include "la_internal.h"
+#include "la_ptx.cuh"
+
+namespace la {
+namespace decode {
+
+constexpr int kD = 128;
+constexpr int kSub = 16;                 // tokens per consumer warp per stage (MMA M)
+constexpr int kCWarps = 8;               // consumer warps
+constexpr int kThreads = (kCWarps + 1) * 32;
+constexpr int kTileBytes = kSub * 128;   // 16 rows x 64 dims bf16 (one swizzle-128B tile)
+constexpr int kWarpBytes = 2 * kTileBytes;
+constexpr int kKVBytes = kCWarps * kWarpBytes;  // 32 KB per tensor per stage
+constexpr int kMaxStages = 4;
+
+constexpr int kFlagFirst = 1;  // first stage of this CTA's segment of the sequence
+constexpr int kFlagLast = 2;   // last stage of the segment
+constexpr int kFlagWhole = 4;  // the segment is the whole sequence
+
+struct StageDesc {
+  int b;
+  int tok0;
+  int ctx;
+  int flags;
+  int slot;  // partial slot base (2*cta + 0/1) for segments that are not whole
+  int pad[3];
+};
+
+struct Params {
+  const int* seqlens;
+  const int* block_table;
+  long long bt_stride;
+  int max_blocks;
+  int batch;
+  int hq, hkv, group, nsub;  // nsub = 8 / hkv consumer warps per kv head
+  int block_size;
+  long long num_blocks;
+  int tc;                    // tokens per stage
+  float scale_log2;
+  __nv_bfloat16* out;
+  long long out_b_stride, out_h_stride;
+  float* lse_out;
+  float* part_o;    // [slots][hq][D]
+  float* part_lse;  // [slots][hq] (log2 domain, scaled)
+  int* err;
+  int q_bytes;      // Q bytes landed per stage (both halves)
+  int q_half_bytes; // stride between the two Q halves (1024-byte aligned)
+  int stage_bytes;
+};
+
+// Number of stage units of a sequence, with the same clamping everywhere.
+__device__ __forceinline__ int seq_ctx(const Params& p, int b) {
+  int c = p.seqlens[b];
+  if (c < 0) c = 0;
+  const long long cap = static_cast<long long>(p.max_blocks) * p.block_size;
+  if (c > cap) {
+    if (p.err) atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
+    c = static_cast<int>(cap);
+  }
+  return c;
+}
+__device__ __forceinline__ int units_of(int ctx, int tc) { return (ctx + tc - 1) / tc; }
+
+__device__ __forceinline__ float warp_max_g(float v) {
+  // max over the 8 lanes that share lane % 4
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+  return v;
+}
+__device__ __forceinline__ float warp_sum_g(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  v += __shfl_xor_sync(0xffffffffu, v, 8);
+  v += __shfl_xor_sync(0xffffffffu, v, 16);
+  return v;
+}
+
+// Total units over all sequences, computed by one warp.
+__device__ long long total_units(const Params& p, int lane) {
+  long long tot = 0;
+  for (int base = 0; base < p.batch; base += 32) {
+    const int b = base + lane;
+    int n = (b < p.batch) ? units_of(seq_ctx(p, b), p.tc) : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+    tot += n;
+  }
+  return tot;
+}
+
+// First unit of CTA c: floor(c * T / G).
+__device__ __forceinline__ long long cta_start(long long c, long long T, long long G) { return c * T / G; }
+// CTA whose range contains unit x: floor(((x + 1) * G - 1) / T).
+__device__ __forceinline__ long long cta_of(long long x, long long T, long long G) { return ((x + 1) * G - 1) / T; }
+
+template <int kStages>
+__global__ void __launch_bounds__(kThreads, 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ctrl = smem + kStages * p.stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ctrl);
+  uint64_t* empty = full + kMaxStages;
+  StageDesc* descs = reinterpret_cast<StageDesc*>(ctrl + 128);
+  uint8_t* zero_row = ctrl + 256;
+  long long* sched = reinterpret_cast<long long*>(ctrl + 384);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCWarps);
+    }
+    fence_barrier_init();
+  }
+  if (threadIdx.x < 32) reinterpret_cast<uint32_t*>(zero_row)[threadIdx.x] = 0u;
+  if (warp == kCWarps && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  // Everything below may read data written by the previous kernel in the stream.
+  grid_dependency_wait();
+
+  if (warp == kCWarps) {
+    // Partition: this CTA's unit range and the sequence it starts in.
+    const long long T = total_units(p, lane);
+    const long long G = gridDim.x;
+    const long long u0 = cta_start(blockIdx.x, T, G);
+    const long long u1 = cta_start(blockIdx.x + 1, T, G);
+    long long acc = 0;
+    int b0 = p.batch;
+    long long pb0 = T;
+    if (u1 > u0) {
+      for (int base = 0; base < p.batch; base += 32) {
+        const int b = base + lane;
+        const int n = (b < p.batch) ? units_of(seq_ctx(p, b), p.tc) : 0;
+        int incl = n;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const long long end = acc + incl;  // cumulative end of sequence b
+        const unsigned hit = __ballot_sync(0xffffffffu, b < p.batch && end > u0);
+        if (hit) {
+          const int src = __ffs(hit) - 1;
+          const int incl_src = __shfl_sync(0xffffffffu, incl, src);
+          const int n_src = __shfl_sync(0xffffffffu, n, src);
+          b0 = base + src;
+          pb0 = acc + incl_src - n_src;
+          break;
+        }
+        acc += __shfl_sync(0xffffffffu, incl, 31);
+      }
+    }
+    if (lane == 0) {
+      sched[0] = u0;
+      sched[1] = (u1 > u0) ? u1 : u0;
+      sched[2] = b0;
+      sched[3] = pb0;
+    }
+  }
+  __syncthreads();
+  // The next kernel (the combine pass) may start its launch now; it waits for
+  // this grid's completion before reading the partials.
+  grid_launch_dependents();
+
+  const long long u0 = sched[0];
+  const long long n_units = sched[1] - sched[0];
+  const int hkv = p.hkv;
+
+  if (warp == kCWarps) {
+    // ------------------------------------------------------------ producer
+    int b = static_cast<int>(sched[2]);
+    long long pb = sched[3];
+    int ctx = (n_units > 0) ? seq_ctx(p, b) : 0;
+    int nb = units_of(ctx, p.tc);
+    long long k = 0;
+    for (; k < n_units; ++k) {
+      const long long u = u0 + k;
+      while (u >= pb + nb && b + 1 < p.batch) {
+        pb += nb;
+        ++b;
+        ctx = seq_ctx(p, b);
+        nb = units_of(ctx, p.tc);
+      }
+      if (u >= pb + nb) break;  // seqlens changed under the kernel: stop issuing
+      const int s = static_cast<int>(k % kStages);
+      const uint32_t ph = static_cast<uint32_t>((k / kStages) & 1);
+      if (!mbar_wait(&empty[s], ph ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
+      const int uis = static_cast<int>(u - pb);
+      const int tok0 = uis * p.tc;
+      uint8_t* st = smem + s * p.stage_bytes;
+
+      // Sub-chunk of warp-slot `lane` (lanes 0..7).
+      bool active = false;
+      int phys = -1, off = 0, head = 0;
+      if (lane < kCWarps) {
+        const int j = lane / hkv;
+        head = lane - j * hkv;
+        const int t = tok0 + kSub * j;
+        if (t < ctx) {
+          active = true;
+          const int lb = t / p.block_size;
+          off = t - lb * p.block_size;
+          if (lb < p.max_blocks) {
+            phys = p.block_table[static_cast<long long>(b) * p.bt_stride + lb];
+            // Out-of-pool ids are reported; TMA zero-fills the box for them.
+            if ((phys < 0 || phys >= p.num_blocks) && p.err) atomicCAS(p.err, 0, LA_DEVERR_BLOCK_ID);
+          } else if (p.err) {
+            atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
+          }
+        }
+      }
+      const unsigned act = __ballot_sync(0xffffffffu, active);
+      if (lane == 0) {
+        StageDesc d;
+        d.b = b;
+        d.tok0 = tok0;
+        d.ctx = ctx;
+        int flags = 0;
+        if (k == 0 || uis == 0) flags |= kFlagFirst;
+        if (k == n_units - 1 || uis == nb - 1) flags |= kFlagLast;
+        if (pb >= u0 && pb + nb <= u0 + n_units) flags |= kFlagWhole;
+        d.flags = flags;
+        d.slot = 2 * static_cast<int>(blockIdx.x) + (pb <= u0 ? 0 : 1);
+        descs[s] = d;
+        const uint32_t bytes = static_cast<uint32_t>(__popc(act)) * (2 * kWarpBytes) + p.q_bytes;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        uint8_t* qs = st + 2 * kKVBytes;
+        tma_load_3d(qs, &tm_q, &full[s], 0, 0, b);
+        tma_load_3d(qs + p.q_half_bytes, &tm_q, &full[s], 64, 0, b);
+      }
+      __syncwarp();
+      if (active) {
+        if (phys < 0) phys = -1;  // outside the pool: TMA fills zeros
+        uint8_t* kd = st + lane * kWarpBytes;
+        uint8_t* vd = st + kKVBytes + lane * kWarpBytes;
+        tma_load_4d(kd, &tm_k, &full[s], 0, head, off, phys);
+        tma_load_4d(kd + kTileBytes, &tm_k, &full[s], 64, head, off, phys);
+        tma_load_4d(vd, &tm_v, &full[s], 0, head, off, phys);
+        tma_load_4d(vd + kTileBytes, &tm_v, &full[s], 64, head, off, phys);
+      }
+    }
+    // On an early exit, let the copies already issued land before the CTA
+    // releases its shared memory (bounded).
+    if (k < n_units) {
+      for (long long kk = (k > kStages ? k - kStages : 0); kk < k; ++kk)
+        mbar_wait(&full[kk % kStages], static_cast<uint32_t>((kk / kStages) & 1), nullptr, 0);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int w = warp;
+  const int j = w / hkv;
+  const int h = w - j * hkv;
+  const int G = p.group;
+  const int g = lane >> 2;
+  const int tq = lane & 3;
+  const float sl2 = p.scale_log2;
+  const float NEG_INF = -__int_as_float(0x7f800000);
+
+  float o[8][4];
+  float m0 = NEG_INF, m1 = NEG_INF, l0 = 0.f, l1 = 0.f;
+  uint32_t qf[8][2];
+
+  for (long long k = 0; k < n_units; ++k) {
+    const int s = static_cast<int>(k % kStages);
+    const uint32_t ph = static_cast<uint32_t>((k / kStages) & 1);
+    if (!mbar_wait(&full[s], ph, p.err, LA_DEVERR_WAIT_TIMEOUT)) return;
+    const StageDesc d = descs[s];
+    uint8_t* st = smem + s * p.stage_bytes;
+
+    if (d.flags & kFlagFirst) {
+      m0 = m1 = NEG_INF;
+      l0 = l1 = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      // Q^T B-fragments for the 8 k-steps (128 dims); rows n >= G read zeros.
+      const uint8_t* qs = st + 2 * kKVBytes;
+      const int n = lane & 7;
+      const int mq = lane >> 3;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int chunk_all = 4 * kk + mq;  // 16-byte chunk index over 128 dims
+        const int half = chunk_all >> 3;
+        const int chunk = chunk_all & 7;
+        uint32_t addr;
+        if (n < G) {
+          const int row = h * G + n;
+          addr = smem_u32(qs + half * p.q_half_bytes) + swz128(row, chunk);
+        } else {
+          addr = smem_u32(zero_row);
+        }
+        uint32_t r[4];
+        ldmatrix_x4(r, addr);
+        qf[2 * kk][0] = r[0];
+        qf[2 * kk][1] = r[1];
+        qf[2 * kk + 1][0] = r[2];
+        qf[2 * kk + 1][1] = r[3];
+      }
+    }
+
+    const int t0 = d.tok0 + kSub * j;
+    int valid = d.ctx - t0;
+    valid = valid < 0 ? 0 : (valid > kSub ? kSub : valid);
+    if (valid > 0) {
+      const uint8_t* ks = st + w * kWarpBytes;
+      uint8_t* vs = st + kKVBytes + w * kWarpBytes;
+      // S^T = K Q^T (16 tokens x 8 query columns)
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+      {
+        const int mq = lane >> 3;
+        const int r = (lane & 7) + ((mq & 1) << 3);
+        const uint32_t kbase = smem_u32(ks);
+#pragma unroll
+        for (int kstep = 0; kstep < 8; ++kstep) {
+          const int half = kstep >> 2;
+          const int chunk = ((kstep & 3) << 1) + (mq >> 1);
+          uint32_t a[4];
+          ldmatrix_x4(a, kbase + half * kTileBytes + swz128(r, chunk));
+          mma_bf16_16816(sacc, a, qf[kstep][0], qf[kstep][1]);
+        }
+      }
+      // Mask, online softmax (columns 2tq, 2tq+1; tokens g, g+8).
+      const bool v0 = g < valid, v1 = (g + 8) < valid;
+      const float x0 = v0 ? sacc[0] * sl2 : NEG_INF;
+      const float x1 = v0 ? sacc[1] * sl2 : NEG_INF;
+      const float x2 = v1 ? sacc[2] * sl2 : NEG_INF;
+      const float x3 = v1 ? sacc[3] * sl2 : NEG_INF;
+      const float mn0 = fmaxf(m0, warp_max_g(fmaxf(x0, x2)));
+      const float mn1 = fmaxf(m1, warp_max_g(fmaxf(x1, x3)));
+      const float a0 = ex2(m0 - mn0), a1 = ex2(m1 - mn1);
+      m0 = mn0;
+      m1 = mn1;
+      const float p0 = ex2(x0 - mn0), p1 = ex2(x1 - mn1), p2 = ex2(x2 - mn0), p3 = ex2(x3 - mn1);
+      l0 = l0 * a0 + (p0 + p2);
+      l1 = l1 * a1 + (p1 + p3);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= a0;
+        o[mt][1] *= a1;
+        o[mt][2] *= a0;
+        o[mt][3] *= a1;
+      }
+      const uint32_t pb0 = movmatrix_trans(pack_bf16x2(p0, p1));
+      const uint32_t pb1 = movmatrix_trans(pack_bf16x2(p2, p3));
+      if (valid < kSub) {
+        // Rows past the sequence end may hold anything (even NaN): zero them so
+        // that P = 0 cannot meet a non-finite V in the MMA.
+        for (int i = lane; i < (kSub - valid) * 16; i += 32) {
+          const int row = valid + (i >> 4);
+          const int half = (i >> 3) & 1;
+          const int chunk = i & 7;
+          *reinterpret_cast<uint4*>(vs + half * kTileBytes + row * 128 + chunk * 16) = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+      // O^T += V^T P^T
+      {
+        const int mq = lane >> 3;
+        const int r = (lane & 7) + ((mq >> 1) << 3);  // token row
+        const uint32_t vbase = smem_u32(vs);
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int dd = mt * 16 + ((mq & 1) << 3);
+          const int half = dd >> 6;
+          const int chunk = (dd & 63) >> 3;
+          uint32_t a[4];
+          ldmatrix_x4_trans(a, vbase + half * kTileBytes + swz128(r, chunk));
+          mma_bf16_16816(o[mt], a, pb0, pb1);
+        }
+      }
+      if (valid < kSub) fence_proxy_async_smem();  // generic writes before the next TMA into this stage
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    if (d.flags & kFlagLast) {
+      const float L0 = warp_sum_g(l0), L1 = warp_sum_g(l1);
+      const int c0 = 2 * tq, c1 = 2 * tq + 1;
+      if ((d.flags & kFlagWhole) && p.nsub == 1) {
+        const float i0 = L0 > 0.f ? 1.f / L0 : 0.f;
+        const float i1 = L1 > 0.f ? 1.f / L1 : 0.f;
+        __nv_bfloat16* ob = p.out + static_cast<long long>(d.b) * p.out_b_stride;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int d0 = mt * 16 + g;
+          if (c0 < G) {
+            __nv_bfloat16* oh = ob + static_cast<long long>(h * G + c0) * p.out_h_stride;
+            oh[d0] = __float2bfloat16_rn(o[mt][0] * i0);
+            oh[d0 + 8] = __float2bfloat16_rn(o[mt][2] * i0);
+          }
+          if (c1 < G) {
+            __nv_bfloat16* oh = ob + static_cast<long long>(h * G + c1) * p.out_h_stride;
+            oh[d0] = __float2bfloat16_rn(o[mt][1] * i1);
+            oh[d0 + 8] = __float2bfloat16_rn(o[mt][3] * i1);
+          }
+        }
+        if (p.lse_out && g == 0) {
+          const float ln2 = 0.6931471805599453f;
+          if (c0 < G) p.lse_out[static_cast<long long>(d.b) * p.hq + h * G + c0] = L0 > 0.f ? (m0 + __log2f(L0)) * ln2 : NEG_INF;
+          if (c1 < G) p.lse_out[static_cast<long long>(d.b) * p.hq + h * G + c1] = L1 > 0.f ? (m1 + __log2f(L1)) * ln2 : NEG_INF;
+        }
+      } else {
+        const long long slot = static_cast<long long>(d.slot) * p.nsub + j;
+        float* po = p.part_o + slot * p.hq * kD;
+        const float i0 = L0 > 0.f ? 1.f / L0 : 0.f;
+        const float i1 = L1 > 0.f ? 1.f / L1 : 0.f;
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          const int d0 = mt * 16 + g;
+          if (c0 < G) {
+            float* oh = po + (h * G + c0) * kD;
+            oh[d0] = o[mt][0] * i0;
+            oh[d0 + 8] = o[mt][2] * i0;
+          }
+          if (c1 < G) {
+            float* oh = po + (h * G + c1) * kD;
+            oh[d0] = o[mt][1] * i1;
+            oh[d0 + 8] = o[mt][3] * i1;
+          }
+        }
+        if (g == 0) {
+          float* pl = p.part_lse + slot * p.hq;
+          if (c0 < G) pl[h * G + c0] = L0 > 0.f ? m0 + __log2f(L0) : NEG_INF;
+          if (c1 < G) pl[h * G + c1] = L1 > 0.f ? m1 + __log2f(L1) : NEG_INF;
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ combine
+// One CTA per sequence, one thread per head dimension. Sequences whose key
+// range lies inside one CTA's range (and nsub == 1) were written directly and
+// are skipped; the rest merge their partials with lse weights.
+__global__ void __launch_bounds__(128) paged_decode_combine_kernel(const Params p, int grid) {
+  const int b = blockIdx.x;
+  const int dim = threadIdx.x;
+  __shared__ long long s_info[4];
+  const float NEG_INF = -__int_as_float(0x7f800000);
+
+  grid_dependency_wait();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    // T and P_b (units before sequence b), by one warp.
+    long long tot = 0, before = 0;
+    for (int base = 0; base < p.batch; base += 32) {
+      const int bb = base + lane;
+      int n = (bb < p.batch) ? units_of(seq_ctx(p, bb), p.tc) : 0;
+      int nb = (bb < b) ? n : 0;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        n += __shfl_xor_sync(0xffffffffu, n, o);
+        nb += __shfl_xor_sync(0xffffffffu, nb, o);
+      }
+      tot += n;
+      before += nb;
+    }
+    if (lane == 0) {
+      s_info[0] = tot;
+      s_info[1] = before;
+      s_info[2] = units_of(seq_ctx(p, b), p.tc);
+    }
+  }
+  __syncthreads();
+  const long long T = s_info[0], Pb = s_info[1];
+  const int nb = static_cast<int>(s_info[2]);
+  const long long Gl = grid;
+  __nv_bfloat16* ob = p.out + static_cast<long long>(b) * p.out_b_stride;
+
+  if (nb == 0) {
+    for (int hh = 0; hh < p.hq; ++hh) ob[hh * p.out_h_stride + dim] = __float2bfloat16_rn(0.f);
+    if (p.lse_out)
+      for (int hh = dim; hh < p.hq; hh += blockDim.x) p.lse_out[static_cast<long long>(b) * p.hq + hh] = NEG_INF;
+    return;
+  }
+  const long long cf = cta_of(Pb, T, Gl);
+  const long long cl = cta_of(Pb + nb - 1, T, Gl);
+  if (cf == cl && p.nsub == 1) return;
+
+  const float ln2 = 0.6931471805599453f;
+  for (int hh = 0; hh < p.hq; ++hh) {
+    float mx = NEG_INF;
+    for (long long c = cf; c <= cl; ++c) {
+      const long long base_slot = 2 * c + (cta_start(c, T, Gl) >= Pb ? 0 : 1);
+      for (int jj = 0; jj < p.nsub; ++jj) mx = fmaxf(mx, p.part_lse[(base_slot * p.nsub + jj) * p.hq + hh]);
+    }
+    float acc = 0.f, wsum = 0.f;
+    if (mx != NEG_INF) {
+      for (long long c = cf; c <= cl; ++c) {
+        const long long base_slot = 2 * c + (cta_start(c, T, Gl) >= Pb ? 0 : 1);
+        for (int jj = 0; jj < p.nsub; ++jj) {
+          const long long slot = base_slot * p.nsub + jj;
+          const float ls = p.part_lse[slot * p.hq + hh];
+          if (ls == NEG_INF) continue;
+          const float wgt = ex2(ls - mx);
+          wsum += wgt;
+          acc += wgt * p.part_o[(slot * p.hq + hh) * kD + dim];
+        }
+      }
+    }
+    ob[hh * p.out_h_stride + dim] = __float2bfloat16_rn(wsum > 0.f ? acc / wsum : 0.f);
+    if (p.lse_out && dim == 0)
+      p.lse_out[static_cast<long long>(b) * p.hq + hh] = wsum > 0.f ? (mx + __log2f(wsum)) * ln2 : NEG_INF;
+  }
+}
+
+// ------------------------------------------------------------------ host
+static int stages_for(int q_area_bytes, int* stage_bytes, size_t* smem) {
+  const int sb = 2 * kKVBytes + q_area_bytes;
+  *stage_bytes = sb;
+  const size_t ctrl = 1024;
+  const size_t limit = 227 * 1024;
+  for (int st = 3; st >= 2; --st) {
+    const size_t need = 1024 /*align slack*/ + static_cast<size_t>(st) * sb + ctrl;
+    if (need <= limit) {
+      *smem = need;
+      return st;
+    }
+  }
+  return 0;
+}
+
+static int grid_for(int device) { return num_sms(device); }
+
+}  // namespace decode
+
+int decode_init(int device) {
+  (void)device;
+  const int lim = 227 * 1024;
+  cudaError_t e = cudaFuncSetAttribute(decode::paged_decode_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode::paged_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  if (e == cudaSuccess) {
+    cudaFuncAttributes a;
+    e = cudaFuncGetAttributes(&a, decode::paged_decode_combine_kernel);
+  }
+  return cuda_status(e);
+}
+
+}  // namespace la
+
+extern "C" int la_paged_decode_workspace_size(int device, int num_q_heads, int num_kv_heads, int head_dim,
+                                              size_t* bytes) {
+  if (!bytes || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim != 128 || num_kv_heads > 8 ||
+      8 % num_kv_heads != 0)
+    return LA_ERR_INVALID_ARGUMENT;
+  const int grid = la::decode::grid_for(device);
+  if (grid <= 0) return LA_ERR_CUDA;
+  const size_t slots = static_cast<size_t>(2) * grid * (8 / num_kv_heads);
+  const size_t o_bytes = slots * num_q_heads * head_dim * sizeof(float);
+  const size_t l_bytes = slots * num_q_heads * sizeof(float);
+  *bytes = ((o_bytes + 255) & ~size_t(255)) + ((l_bytes + 255) & ~size_t(255));
+  return LA_OK;
+}
+
+extern "C" int la_paged_decode(const void* q, int64_t q_batch_stride, int64_t q_head_stride, const void* k_cache,
+                               const void* v_cache, int64_t kv_block_stride, int64_t kv_token_stride,
+                               int64_t kv_head_stride, int64_t num_blocks, int block_size,
+                               const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
+                               const int32_t* cache_seqlens, int batch, int num_q_heads, int num_kv_heads,
+                               int head_dim, float softmax_scale, void* out, int64_t out_batch_stride,
+                               int64_t out_head_stride, float* softmax_lse, void* workspace,
+                               size_t workspace_bytes, int* dev_error, cudaStream_t stream) {
+  using namespace la;
+  using namespace la::decode;
+  if (!q || !k_cache || !v_cache || !block_table || !cache_seqlens || !out) return LA_ERR_INVALID_ARGUMENT;
+  if (batch < 0 || num_blocks <= 0 || block_size <= 0 || max_blocks_per_seq <= 0) return LA_ERR_INVALID_ARGUMENT;
+  if (batch == 0) return LA_OK;
+  if (head_dim != kD) return LA_ERR_UNSUPPORTED;
+  if (num_kv_heads <= 0 || num_kv_heads > 8 || 8 % num_kv_heads != 0) return LA_ERR_UNSUPPORTED;
+  if (num_q_heads <= 0 || num_q_heads % num_kv_heads != 0) return LA_ERR_INVALID_ARGUMENT;
+  const int group = num_q_heads / num_kv_heads;
+  if (group > 8 || num_q_heads > 256) return LA_ERR_UNSUPPORTED;
+  if (block_size % kSub != 0) return LA_ERR_UNSUPPORTED;
+  if (!(softmax_scale > 0.f)) return LA_ERR_INVALID_ARGUMENT;
+  // TMA: 16-byte aligned bases and byte strides.
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16)) return LA_ERR_ALIGNMENT;
+  if ((q_batch_stride * 2) % 16 || (q_head_stride * 2) % 16 || (kv_block_stride * 2) % 16 ||
+      (kv_token_stride * 2) % 16 || (kv_head_stride * 2) % 16)
+    return LA_ERR_ALIGNMENT;
+  if (q_batch_stride <= 0 || q_head_stride <= 0 || kv_block_stride <= 0 || kv_token_stride <= 0 ||
+      kv_head_stride <= 0 || out_batch_stride <= 0 || out_head_stride <= 0)
+    return LA_ERR_INVALID_ARGUMENT;
+
+  const int device = current_device();
+  if (device < 0) return LA_ERR_CUDA;
+  const int grid = grid_for(device);
+  if (grid <= 0) return LA_ERR_CUDA;
+  size_t need = 0;
+  int st = la_paged_decode_workspace_size(device, num_q_heads, num_kv_heads, head_dim, &need);
+  if (st != LA_OK) return st;
+  if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return LA_ERR_WORKSPACE;
+
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[3] = {128, static_cast<uint64_t>(num_q_heads), static_cast<uint64_t>(batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(q_head_stride) * 2, static_cast<uint64_t>(q_batch_stride) * 2};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(num_q_heads), 1};
+    if ((st = encode_tensor_map_bf16(&tq, q, 3, dims, strides, box, true)) != LA_OK) return st;
+  }
+  {
+    const uint64_t dims[4] = {128, static_cast<uint64_t>(num_kv_heads), static_cast<uint64_t>(block_size),
+                              static_cast<uint64_t>(num_blocks)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(kv_head_stride) * 2, static_cast<uint64_t>(kv_token_stride) * 2,
+                                 static_cast<uint64_t>(kv_block_stride) * 2};
+    const uint32_t box[4] = {64, 1, static_cast<uint32_t>(kSub), 1};
+    if ((st = encode_tensor_map_bf16(&tk, k_cache, 4, dims, strides, box, true)) != LA_OK) return st;
+    if ((st = encode_tensor_map_bf16(&tv, v_cache, 4, dims, strides, box, true)) != LA_OK) return st;
+  }
+
+  Params p;
+  p.seqlens = cache_seqlens;
+  p.block_table = block_table;
+  p.bt_stride = bt_seq_stride;
+  p.max_blocks = max_blocks_per_seq;
+  p.batch = batch;
+  p.hq = num_q_heads;
+  p.hkv = num_kv_heads;
+  p.group = group;
+  p.nsub = 8 / num_kv_heads;
+  p.block_size = block_size;
+  p.num_blocks = num_blocks;
+  p.tc = kSub * p.nsub;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_b_stride = out_batch_stride;
+  p.out_h_stride = out_head_stride;
+  p.lse_out = softmax_lse;
+  const size_t slots = static_cast<size_t>(2) * grid * p.nsub;
+  const size_t o_bytes = (slots * num_q_heads * kD * sizeof(float) + 255) & ~size_t(255);
+  p.part_o = static_cast<float*>(workspace);
+  p.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + o_bytes);
+  p.err = dev_error;
+  // Each Q half tile starts on a 1024-byte boundary (the 128-byte swizzle atom).
+  p.q_half_bytes = (num_q_heads * 128 + 1023) & ~1023;
+  p.q_bytes = 2 * num_q_heads * 128;
+  size_t smem = 0;
+  const int stages = stages_for(2 * p.q_half_bytes, &p.stage_bytes, &smem);
+  if (stages == 0) return LA_ERR_UNSUPPORTED;
+
+  cudaError_t e;
+  if (stages == 3)
+    e = launch_pdl(paged_decode_kernel<3>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p);
+  else
+    e = launch_pdl(paged_decode_kernel<2>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p);
+  if (e != cudaSuccess) return cuda_status(e);
+  e = launch_pdl(paged_decode_combine_kernel, dim3(batch), dim3(128), 0, stream, p, grid);
+  return cuda_status(e);
+}
