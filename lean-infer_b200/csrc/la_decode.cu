@@ -43,7 +43,11 @@ constexpr int kCWarps = 8;               // consumer warps
 constexpr int kThreads = (kCWarps + 1) * 32;
 constexpr int kTileBytes = kSub * 128;   // 16 rows x 64 dims bf16 (one swizzle-128B tile)
 constexpr int kWarpBytes = 2 * kTileBytes;
-constexpr int kKVBytes = kCWarps * kWarpBytes;  // 32 KB per tensor per stage
+constexpr int kKVHalf = kCWarps * kTileBytes;   // one 64-dim half of all warps' tiles: 16 KB
+constexpr int kKVBytes = 2 * kKVHalf;           // 32 KB per tensor per stage
+// Stage layout per tensor: [half][warp w][16 rows][128 B]; warp w = j*Hkv + h
+// holds kv head h of sub-chunk j, so the Hkv heads of a sub-chunk are one
+// contiguous run that a single TMA box [64 dims, 16 tokens, Hkv heads] fills.
 constexpr int kMaxStages = 4;
 
 constexpr int kFlagFirst = 1;  // first stage of this CTA's segment of the sequence
@@ -79,6 +83,7 @@ struct Params {
   int q_bytes;      // Q bytes landed per stage (both halves)
   int q_half_bytes; // stride between the two Q halves (1024-byte aligned)
   int stage_bytes;
+  int big_box;      // 1: K/V maps are [D, BS, Hkv, NB] with box (64, 16, Hkv, 1)
 };
 
 // Number of stage units of a sequence, with the same clamping everywhere.
@@ -138,6 +143,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   StageDesc* descs = reinterpret_cast<StageDesc*>(ctrl + 128);
   uint8_t* zero_row = ctrl + 256;
   long long* sched = reinterpret_cast<long long*>(ctrl + 384);
+  uint64_t* mg_full = reinterpret_cast<uint64_t*>(ctrl + 448);   // all consumer warps wrote their state
+  uint64_t* mg_empty = reinterpret_cast<uint64_t*>(ctrl + 456);  // the j = 0 warps read it
+  float* merge = reinterpret_cast<float*>(ctrl + 1024);          // [8 warps][TQ][8][36] fp32 (nsub > 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -147,6 +155,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kCWarps);
     }
+    mbar_init(mg_full, kCWarps);
+    mbar_init(mg_empty, p.hkv);
     fence_barrier_init();
   }
   if (threadIdx.x < 32) reinterpret_cast<uint32_t*>(zero_row)[threadIdx.x] = 0u;
@@ -269,14 +279,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(qs + p.q_half_bytes, &tm_q, &full[s], 64, 0, b);
       }
       __syncwarp();
-      if (active) {
-        if (phys < 0) phys = -1;  // outside the pool: TMA fills zeros
-        uint8_t* kd = st + lane * kWarpBytes;
-        uint8_t* vd = st + kKVBytes + lane * kWarpBytes;
+      if (phys < 0) phys = -1;  // outside the pool: TMA fills zeros
+      if (p.big_box) {
+        if (active && head == 0) {  // one lane per sub-chunk: all kv heads in one box per half
+          uint8_t* kd = st + lane * kTileBytes;
+          uint8_t* vd = st + kKVBytes + lane * kTileBytes;
+          tma_load_4d(kd, &tm_k, &full[s], 0, off, 0, phys);
+          tma_load_4d(kd + kKVHalf, &tm_k, &full[s], 64, off, 0, phys);
+          tma_load_4d(vd, &tm_v, &full[s], 0, off, 0, phys);
+          tma_load_4d(vd + kKVHalf, &tm_v, &full[s], 64, off, 0, phys);
+        }
+      } else if (active) {
+        uint8_t* kd = st + lane * kTileBytes;
+        uint8_t* vd = st + kKVBytes + lane * kTileBytes;
         tma_load_4d(kd, &tm_k, &full[s], 0, head, off, phys);
-        tma_load_4d(kd + kTileBytes, &tm_k, &full[s], 64, head, off, phys);
+        tma_load_4d(kd + kKVHalf, &tm_k, &full[s], 64, head, off, phys);
         tma_load_4d(vd, &tm_v, &full[s], 0, head, off, phys);
-        tma_load_4d(vd + kTileBytes, &tm_v, &full[s], 64, head, off, phys);
+        tma_load_4d(vd + kKVHalf, &tm_v, &full[s], 64, head, off, phys);
       }
     }
     // On an early exit, let the copies already issued land before the CTA
@@ -301,6 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float o[8][4];
   float m0 = NEG_INF, m1 = NEG_INF, l0 = 0.f, l1 = 0.f;
   uint32_t qf[8][2];
+  long long seg_ends = 0;  // segment ends seen (phase of the merge barriers)
 
   for (long long k = 0; k < n_units; ++k) {
     const int s = static_cast<int>(k % kStages);
@@ -343,8 +363,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int valid = d.ctx - t0;
     valid = valid < 0 ? 0 : (valid > kSub ? kSub : valid);
     if (valid > 0) {
-      const uint8_t* ks = st + w * kWarpBytes;
-      uint8_t* vs = st + kKVBytes + w * kWarpBytes;
+      const uint8_t* ks = st + w * kTileBytes;  // + half * kKVHalf
+      uint8_t* vs = st + kKVBytes + w * kTileBytes;
       // S^T = K Q^T (16 tokens x 8 query columns)
       float sacc[4] = {0.f, 0.f, 0.f, 0.f};
       {
@@ -356,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int half = kstep >> 2;
           const int chunk = ((kstep & 3) << 1) + (mq >> 1);
           uint32_t a[4];
-          ldmatrix_x4(a, kbase + half * kTileBytes + swz128(r, chunk));
+          ldmatrix_x4(a, kbase + half * kKVHalf + swz128(r, chunk));
           mma_bf16_16816(sacc, a, qf[kstep][0], qf[kstep][1]);
         }
       }
@@ -390,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int row = valid + (i >> 4);
           const int half = (i >> 3) & 1;
           const int chunk = i & 7;
-          *reinterpret_cast<uint4*>(vs + half * kTileBytes + row * 128 + chunk * 16) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(vs + half * kKVHalf + row * 128 + chunk * 16) = make_uint4(0, 0, 0, 0);
         }
         __syncwarp();
       }
@@ -405,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int half = dd >> 6;
           const int chunk = (dd & 63) >> 3;
           uint32_t a[4];
-          ldmatrix_x4_trans(a, vbase + half * kTileBytes + swz128(r, chunk));
+          ldmatrix_x4_trans(a, vbase + half * kKVHalf + swz128(r, chunk));
           mma_bf16_16816(o[mt], a, pb0, pb1);
         }
       }
@@ -415,9 +435,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) mbar_arrive(&empty[s]);
 
     if (d.flags & kFlagLast) {
-      const float L0 = warp_sum_g(l0), L1 = warp_sum_g(l1);
+      float L0 = warp_sum_g(l0), L1 = warp_sum_g(l1);
       const int c0 = 2 * tq, c1 = 2 * tq + 1;
-      if ((d.flags & kFlagWhole) && p.nsub == 1) {
+      bool writer = true;
+      if (p.nsub > 1) {
+        // Several warps hold partial states of the same kv head (one per
+        // sub-chunk j). Merge them in shared memory into warp j = 0 so every
+        // segment leaves one state per head, as with nsub == 1.
+        const int TQ = (G + 1) >> 1;  // lanes (per g) that hold real columns
+        const uint32_t par = static_cast<uint32_t>(seg_ends & 1);
+        if (!mbar_wait(mg_empty, par ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) return;
+        if (tq < TQ) {
+          float* slot = merge + ((w * TQ + tq) * 8 + g) * 36;
+          slot[0] = m0;
+          slot[1] = m1;
+          slot[2] = L0;
+          slot[3] = L1;
+#pragma unroll
+          for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) slot[4 + mt * 4 + r] = o[mt][r];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(mg_full);
+        writer = (j == 0);
+        if (writer) {
+          if (!mbar_wait(mg_full, par, p.err, LA_DEVERR_WAIT_TIMEOUT)) return;
+          if (tq < TQ) {
+            for (int jj = 1; jj < p.nsub; ++jj) {
+              const float* sl = merge + (((jj * hkv + h) * TQ + tq) * 8 + g) * 36;
+              const float om0 = sl[0], om1 = sl[1], oL0 = sl[2], oL1 = sl[3];
+              const float n0 = fmaxf(m0, om0), n1 = fmaxf(m1, om1);
+              // a side with no keys (m = -inf) contributes nothing
+              const float a0 = (m0 == NEG_INF) ? 0.f : ex2(m0 - n0), b0 = (om0 == NEG_INF) ? 0.f : ex2(om0 - n0);
+              const float a1 = (m1 == NEG_INF) ? 0.f : ex2(m1 - n1), b1 = (om1 == NEG_INF) ? 0.f : ex2(om1 - n1);
+#pragma unroll
+              for (int mt = 0; mt < 8; ++mt) {
+                o[mt][0] = o[mt][0] * a0 + sl[4 + mt * 4 + 0] * b0;
+                o[mt][1] = o[mt][1] * a1 + sl[4 + mt * 4 + 1] * b1;
+                o[mt][2] = o[mt][2] * a0 + sl[4 + mt * 4 + 2] * b0;
+                o[mt][3] = o[mt][3] * a1 + sl[4 + mt * 4 + 3] * b1;
+              }
+              L0 = L0 * a0 + oL0 * b0;
+              L1 = L1 * a1 + oL1 * b1;
+              m0 = n0;
+              m1 = n1;
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(mg_empty);
+        }
+        ++seg_ends;
+      }
+      if (writer && (d.flags & kFlagWhole)) {
         const float i0 = L0 > 0.f ? 1.f / L0 : 0.f;
         const float i1 = L1 > 0.f ? 1.f / L1 : 0.f;
         __nv_bfloat16* ob = p.out + static_cast<long long>(d.b) * p.out_b_stride;
@@ -440,9 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (c0 < G) p.lse_out[static_cast<long long>(d.b) * p.hq + h * G + c0] = L0 > 0.f ? (m0 + __log2f(L0)) * ln2 : NEG_INF;
           if (c1 < G) p.lse_out[static_cast<long long>(d.b) * p.hq + h * G + c1] = L1 > 0.f ? (m1 + __log2f(L1)) * ln2 : NEG_INF;
         }
-      } else {
-        const long long slot = static_cast<long long>(d.slot) * p.nsub + j;
-        float* po = p.part_o + slot * p.hq * kD;
+      } else if (writer) {
+        float* po = p.part_o + static_cast<long long>(d.slot) * p.hq * kD;
         const float i0 = L0 > 0.f ? 1.f / L0 : 0.f;
         const float i1 = L1 > 0.f ? 1.f / L1 : 0.f;
 #pragma unroll
@@ -460,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (g == 0) {
-          float* pl = p.part_lse + slot * p.hq;
+          float* pl = p.part_lse + static_cast<long long>(d.slot) * p.hq;
           if (c0 < G) pl[h * G + c0] = L0 > 0.f ? m0 + __log2f(L0) : NEG_INF;
           if (c1 < G) pl[h * G + c1] = L1 > 0.f ? m1 + __log2f(L1) : NEG_INF;
         }
@@ -470,86 +539,101 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ combine
-// One CTA per sequence, one thread per head dimension. Sequences whose key
-// range lies inside one CTA's range (and nsub == 1) were written directly and
-// are skipped; the rest merge their partials with lse weights.
-__global__ void __launch_bounds__(128) paged_decode_combine_kernel(const Params p, int grid) {
+// Grid (batch, Hq), one warp per (sequence, query head); lane l owns dims
+// 4l..4l+3. Sequences whose key range lies inside one CTA's range were
+// written directly by the decode kernel and are skipped. The
+// others merge their partials in slot order with an online (max, sum) merge;
+// slots are fetched 8 at a time so their loads overlap.
+constexpr int kCombineBatch = 8;
+
+__global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p, int grid) {
   const int b = blockIdx.x;
-  const int dim = threadIdx.x;
-  __shared__ long long s_info[4];
+  const int hh = blockIdx.y;
+  const int lane = threadIdx.x;
   const float NEG_INF = -__int_as_float(0x7f800000);
 
   grid_dependency_wait();
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    // T and P_b (units before sequence b), by one warp.
-    long long tot = 0, before = 0;
-    for (int base = 0; base < p.batch; base += 32) {
-      const int bb = base + lane;
-      int n = (bb < p.batch) ? units_of(seq_ctx(p, bb), p.tc) : 0;
-      int nb = (bb < b) ? n : 0;
+  // T (all units) and P_b (units before sequence b).
+  long long T = 0, Pb = 0;
+  for (int base = 0; base < p.batch; base += 32) {
+    const int bb = base + lane;
+    int n = (bb < p.batch) ? units_of(seq_ctx(p, bb), p.tc) : 0;
+    int nb = (bb < b) ? n : 0;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        n += __shfl_xor_sync(0xffffffffu, n, o);
-        nb += __shfl_xor_sync(0xffffffffu, nb, o);
-      }
-      tot += n;
-      before += nb;
+    for (int o = 16; o > 0; o >>= 1) {
+      n += __shfl_xor_sync(0xffffffffu, n, o);
+      nb += __shfl_xor_sync(0xffffffffu, nb, o);
     }
-    if (lane == 0) {
-      s_info[0] = tot;
-      s_info[1] = before;
-      s_info[2] = units_of(seq_ctx(p, b), p.tc);
-    }
+    T += n;
+    Pb += nb;
   }
-  __syncthreads();
-  const long long T = s_info[0], Pb = s_info[1];
-  const int nb = static_cast<int>(s_info[2]);
+  const int nb = units_of(seq_ctx(p, b), p.tc);
   const long long Gl = grid;
-  __nv_bfloat16* ob = p.out + static_cast<long long>(b) * p.out_b_stride;
+  __nv_bfloat16* oh = p.out + static_cast<long long>(b) * p.out_b_stride + static_cast<long long>(hh) * p.out_h_stride +
+                      lane * 4;
+  float* lse = p.lse_out ? p.lse_out + static_cast<long long>(b) * p.hq + hh : nullptr;
 
   if (nb == 0) {
-    for (int hh = 0; hh < p.hq; ++hh) ob[hh * p.out_h_stride + dim] = __float2bfloat16_rn(0.f);
-    if (p.lse_out)
-      for (int hh = dim; hh < p.hq; hh += blockDim.x) p.lse_out[static_cast<long long>(b) * p.hq + hh] = NEG_INF;
+    *reinterpret_cast<uint2*>(oh) = make_uint2(0u, 0u);
+    if (lse && lane == 0) *lse = NEG_INF;
     return;
   }
   const long long cf = cta_of(Pb, T, Gl);
   const long long cl = cta_of(Pb + nb - 1, T, Gl);
-  if (cf == cl && p.nsub == 1) return;
+  if (cf == cl) return;  // written directly by the decode kernel
 
-  const float ln2 = 0.6931471805599453f;
-  for (int hh = 0; hh < p.hq; ++hh) {
-    float mx = NEG_INF;
-    for (long long c = cf; c <= cl; ++c) {
-      const long long base_slot = 2 * c + (cta_start(c, T, Gl) >= Pb ? 0 : 1);
-      for (int jj = 0; jj < p.nsub; ++jj) mx = fmaxf(mx, p.part_lse[(base_slot * p.nsub + jj) * p.hq + hh]);
+  float m = NEG_INF, l = 0.f;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  long long c = cf;
+  while (true) {
+    long long slots[kCombineBatch];
+    int n = 0;
+    while (n < kCombineBatch && c <= cl) {
+      const long long s0 = cta_start(c, T, Gl);
+      if (s0 == cta_start(c + 1, T, Gl)) {  // empty range (T < G): wrote nothing
+        ++c;
+        continue;
+      }
+      slots[n++] = 2 * c + (s0 >= Pb ? 0 : 1);
+      ++c;
     }
-    float acc = 0.f, wsum = 0.f;
-    if (mx != NEG_INF) {
-      for (long long c = cf; c <= cl; ++c) {
-        const long long base_slot = 2 * c + (cta_start(c, T, Gl) >= Pb ? 0 : 1);
-        for (int jj = 0; jj < p.nsub; ++jj) {
-          const long long slot = base_slot * p.nsub + jj;
-          const float ls = p.part_lse[slot * p.hq + hh];
-          if (ls == NEG_INF) continue;
-          const float wgt = ex2(ls - mx);
-          wsum += wgt;
-          acc += wgt * p.part_o[(slot * p.hq + hh) * kD + dim];
-        }
+    if (n == 0) break;
+    float ls[kCombineBatch];
+    float4 ov[kCombineBatch];
+#pragma unroll
+    for (int u = 0; u < kCombineBatch; ++u) {
+      if (u < n) {
+        ls[u] = p.part_lse[slots[u] * p.hq + hh];
+        ov[u] = *reinterpret_cast<const float4*>(p.part_o + (slots[u] * p.hq + hh) * kD + lane * 4);
       }
     }
-    ob[hh * p.out_h_stride + dim] = __float2bfloat16_rn(wsum > 0.f ? acc / wsum : 0.f);
-    if (p.lse_out && dim == 0)
-      p.lse_out[static_cast<long long>(b) * p.hq + hh] = wsum > 0.f ? (mx + __log2f(wsum)) * ln2 : NEG_INF;
+#pragma unroll
+    for (int u = 0; u < kCombineBatch; ++u) {
+      if (u < n && ls[u] != NEG_INF) {
+        const float mn = fmaxf(m, ls[u]);
+        const float a = ex2(m - mn), w = ex2(ls[u] - mn);
+        acc[0] = acc[0] * a + w * ov[u].x;
+        acc[1] = acc[1] * a + w * ov[u].y;
+        acc[2] = acc[2] * a + w * ov[u].z;
+        acc[3] = acc[3] * a + w * ov[u].w;
+        l = l * a + w;
+        m = mn;
+      }
+    }
   }
+  const float inv = l > 0.f ? 1.f / l : 0.f;
+  uint2 v;
+  v.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+  v.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+  *reinterpret_cast<uint2*>(oh) = v;
+  if (lse && lane == 0) *lse = l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
 }
 
 // ------------------------------------------------------------------ host
-static int stages_for(int q_area_bytes, int* stage_bytes, size_t* smem) {
+static int stages_for(int q_area_bytes, int merge_bytes, int* stage_bytes, size_t* smem) {
   const int sb = 2 * kKVBytes + q_area_bytes;
   *stage_bytes = sb;
-  const size_t ctrl = 1024;
+  const size_t ctrl = 1024 + merge_bytes;
   const size_t limit = 227 * 1024;
   for (int st = 3; st >= 2; --st) {
     const size_t need = 1024 /*align slack*/ + static_cast<size_t>(st) * sb + ctrl;
@@ -587,7 +671,7 @@ extern "C" int la_paged_decode_workspace_size(int device, int num_q_heads, int n
     return LA_ERR_INVALID_ARGUMENT;
   const int grid = la::decode::grid_for(device);
   if (grid <= 0) return LA_ERR_CUDA;
-  const size_t slots = static_cast<size_t>(2) * grid * (8 / num_kv_heads);
+  const size_t slots = static_cast<size_t>(2) * grid;
   const size_t o_bytes = slots * num_q_heads * head_dim * sizeof(float);
   const size_t l_bytes = slots * num_q_heads * sizeof(float);
   *bytes = ((o_bytes + 255) & ~size_t(255)) + ((l_bytes + 255) & ~size_t(255));
@@ -622,6 +706,8 @@ extern "C" int la_paged_decode(const void* q, int64_t q_batch_stride, int64_t q_
   if (q_batch_stride <= 0 || q_head_stride <= 0 || kv_block_stride <= 0 || kv_token_stride <= 0 ||
       kv_head_stride <= 0 || out_batch_stride <= 0 || out_head_stride <= 0)
     return LA_ERR_INVALID_ARGUMENT;
+  // the combine pass stores 4 bf16 per lane
+  if (!aligned(out, 8) || out_batch_stride % 4 || out_head_stride % 4) return LA_ERR_ALIGNMENT;
 
   const int device = current_device();
   if (device < 0) return LA_ERR_CUDA;
@@ -639,7 +725,20 @@ extern "C" int la_paged_decode(const void* q, int64_t q_batch_stride, int64_t q_
     const uint32_t box[3] = {64, static_cast<uint32_t>(num_q_heads), 1};
     if ((st = encode_tensor_map_bf16(&tq, q, 3, dims, strides, box, true)) != LA_OK) return st;
   }
+  int big_box = 0;
   {
+    // Preferred: token axis before the head axis, so one box covers all kv
+    // heads of 16 tokens (strides need not grow with the dimension index).
+    const uint64_t dims[4] = {128, static_cast<uint64_t>(block_size), static_cast<uint64_t>(num_kv_heads),
+                              static_cast<uint64_t>(num_blocks)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(kv_token_stride) * 2, static_cast<uint64_t>(kv_head_stride) * 2,
+                                 static_cast<uint64_t>(kv_block_stride) * 2};
+    const uint32_t box[4] = {64, static_cast<uint32_t>(kSub), static_cast<uint32_t>(num_kv_heads), 1};
+    if (encode_tensor_map_bf16(&tk, k_cache, 4, dims, strides, box, true) == LA_OK &&
+        encode_tensor_map_bf16(&tv, v_cache, 4, dims, strides, box, true) == LA_OK)
+      big_box = 1;
+  }
+  if (!big_box) {
     const uint64_t dims[4] = {128, static_cast<uint64_t>(num_kv_heads), static_cast<uint64_t>(block_size),
                               static_cast<uint64_t>(num_blocks)};
     const uint64_t strides[3] = {static_cast<uint64_t>(kv_head_stride) * 2, static_cast<uint64_t>(kv_token_stride) * 2,
@@ -667,16 +766,18 @@ extern "C" int la_paged_decode(const void* q, int64_t q_batch_stride, int64_t q_
   p.out_b_stride = out_batch_stride;
   p.out_h_stride = out_head_stride;
   p.lse_out = softmax_lse;
-  const size_t slots = static_cast<size_t>(2) * grid * p.nsub;
+  const size_t slots = static_cast<size_t>(2) * grid;
   const size_t o_bytes = (slots * num_q_heads * kD * sizeof(float) + 255) & ~size_t(255);
   p.part_o = static_cast<float*>(workspace);
   p.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + o_bytes);
   p.err = dev_error;
   // Each Q half tile starts on a 1024-byte boundary (the 128-byte swizzle atom).
+  p.big_box = big_box;
   p.q_half_bytes = (num_q_heads * 128 + 1023) & ~1023;
   p.q_bytes = 2 * num_q_heads * 128;
   size_t smem = 0;
-  const int stages = stages_for(2 * p.q_half_bytes, &p.stage_bytes, &smem);
+  const int merge_bytes = (p.nsub > 1) ? kCWarps * ((group + 1) / 2) * 8 * 36 * 4 : 0;
+  const int stages = stages_for(2 * p.q_half_bytes, merge_bytes, &p.stage_bytes, &smem);
   if (stages == 0) return LA_ERR_UNSUPPORTED;
 
   cudaError_t e;
@@ -685,6 +786,6 @@ extern "C" int la_paged_decode(const void* q, int64_t q_batch_stride, int64_t q_
   else
     e = launch_pdl(paged_decode_kernel<2>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p);
   if (e != cudaSuccess) return cuda_status(e);
-  e = launch_pdl(paged_decode_combine_kernel, dim3(batch), dim3(128), 0, stream, p, grid);
+  e = launch_pdl(paged_decode_combine_kernel, dim3(batch, num_q_heads), dim3(32), 0, stream, p, grid);
   return cuda_status(e);
 }

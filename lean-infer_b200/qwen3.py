@@ -1,0 +1,229 @@
+"""Qwen3 decoder with the reference's attention ops replaced by the sm_100a
+kernels — the engine integration of the attention backend.
+
+Same architecture and math as leaninfer/qwen3/model.py (Qwen3MLP :25-33,
+Qwen3Attention :36-69, Qwen3DecoderLayer :72-83, Qwen3Model :87-101,
+Qwen3ForCausalLM :104-112, lm_head tied to the embedding). Differences are
+confined to how the work is launched:
+  * q/k/v projections run as one GEMM on concatenated weights (and gate/up as
+    one), the same products in bf16;
+  * q_norm/k_norm + apply_rope + cache.write (model.py:50-55) are one launch
+    of qk_norm_rope_paged_write, with rope from a position-indexed table
+    instead of build_rope per forward (model.py:98);
+  * decode attention (model.py:60-67) is flash_attn_with_kvcache from this
+    package; prefill attention (model.py:56-57) is flash_attn_varlen_func.
+Weights are random-init bf16 (no checkpoint is loaded: the benchmark runs on
+synthetic data).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import flash_attn_interface as fai
+from .cache import BlockCache
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    """Field-for-field leaninfer.qwen3.model_config.ModelConfig
+    (model_config.py:20-31); defaults are Qwen3-0.6B."""
+    num_hidden_layers: int = 28
+    hidden_size: int = 1024
+    num_attention_heads: int = 16
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    intermediate_size: int = 3072
+    vocab_size: int = 151936
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e6
+
+
+class Qwen3Attention(nn.Module):
+    def __init__(self, cfg: ModelConfig, head_offset: int = 0, num_kv_heads: int | None = None) -> None:
+        super().__init__()
+        self.cfg = cfg
+        self.hkv = cfg.num_key_value_heads if num_kv_heads is None else num_kv_heads
+        self.hq = self.hkv * (cfg.num_attention_heads // cfg.num_key_value_heads)
+        D = cfg.head_dim
+        self.qkv_proj = nn.Linear(cfg.hidden_size, (self.hq + 2 * self.hkv) * D, bias=False)
+        self.q_norm = nn.Parameter(torch.ones(D))
+        self.k_norm = nn.Parameter(torch.ones(D))
+        self.o_proj = nn.Linear(cfg.num_attention_heads * D, cfg.hidden_size, bias=False)
+
+    def attend(self, x: torch.Tensor, cache: BlockCache, layer: int, block_tables: torch.Tensor, pos: torch.Tensor,
+               cache_seqlens: torch.Tensor | None, rope, cu_seqlens: torch.Tensor | None = None,
+               max_seqlen: int = 0) -> torch.Tensor:
+        """Attention output [T, hq*D] before o_proj. x: [T, hidden]."""
+        T = x.shape[0]
+        D = self.cfg.head_dim
+        qkv = self.qkv_proj(x)
+        q = qkv[:, : self.hq * D].view(T, self.hq, D)
+        k = qkv[:, self.hq * D: (self.hq + self.hkv) * D].view(T, self.hkv, D)
+        v = qkv[:, (self.hq + self.hkv) * D:].view(T, self.hkv, D)
+        kc, vc = cache.k[layer], cache.v[layer]
+        if cache_seqlens is not None:  # decode: one token per sequence
+            q = fai.qk_norm_rope_paged_write(q, k, v, self.q_norm, self.k_norm, rope[0], rope[1], pos, block_tables,
+                                             kc, vc, eps=self.cfg.rms_norm_eps)
+            o = fai.flash_attn_with_kvcache(q.view(T, 1, self.hq, D), kc, vc, cache_seqlens=cache_seqlens,
+                                            block_table=block_tables, causal=True, num_splits=1)
+        else:  # prefill of packed prompts starting at pos
+            k_out = torch.empty_like(k)
+            q = fai.qk_norm_rope_paged_write(q, k, v, self.q_norm, self.k_norm, rope[0], rope[1], pos, block_tables,
+                                             kc, vc, eps=self.cfg.rms_norm_eps, cu_seqlens=cu_seqlens, k_out=k_out)
+            o = fai.flash_attn_varlen_func(q, k_out, v, cu_seqlens, cu_seqlens, max_seqlen, max_seqlen, causal=True)
+        return o.reshape(T, self.hq * D)
+
+    def forward(self, x, cache, layer, block_tables, pos, cache_seqlens, rope, cu_seqlens=None, max_seqlen=0):
+        return self.o_proj(self.attend(x, cache, layer, block_tables, pos, cache_seqlens, rope, cu_seqlens,
+                                       max_seqlen))
+
+
+class Qwen3MLP(nn.Module):
+    def __init__(self, cfg: ModelConfig) -> None:
+        super().__init__()
+        self.gate_up_proj = nn.Linear(cfg.hidden_size, 2 * cfg.intermediate_size, bias=False)
+        self.down_proj = nn.Linear(cfg.intermediate_size, cfg.hidden_size, bias=False)
+        self.inter = cfg.intermediate_size
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        gu = self.gate_up_proj(x)
+        return self.down_proj(F.silu(gu[:, : self.inter]) * gu[:, self.inter:])
+
+
+class Qwen3DecoderLayer(nn.Module):
+    def __init__(self, cfg: ModelConfig) -> None:
+        super().__init__()
+        self.self_attn = Qwen3Attention(cfg)
+        self.mlp = Qwen3MLP(cfg)
+        self.input_layernorm = nn.Parameter(torch.ones(cfg.hidden_size))
+        self.post_attention_layernorm = nn.Parameter(torch.ones(cfg.hidden_size))
+        self.eps = cfg.rms_norm_eps
+
+    def forward(self, h, cache, layer, block_tables, pos, cache_seqlens, rope, cu_seqlens=None, max_seqlen=0):
+        x = F.rms_norm(h, (h.shape[-1],), self.input_layernorm, self.eps)
+        h = h + self.self_attn(x, cache, layer, block_tables, pos, cache_seqlens, rope, cu_seqlens, max_seqlen)
+        x = F.rms_norm(h, (h.shape[-1],), self.post_attention_layernorm, self.eps)
+        return h + self.mlp(x)
+
+
+class Qwen3ForCausalLM(nn.Module):
+    def __init__(self, cfg: ModelConfig) -> None:
+        super().__init__()
+        self.config = cfg
+        self.embed_tokens = nn.Embedding(cfg.vocab_size, cfg.hidden_size)
+        self.layers = nn.ModuleList(Qwen3DecoderLayer(cfg) for _ in range(cfg.num_hidden_layers))
+        self.norm = nn.Parameter(torch.ones(cfg.hidden_size))
+        self.max_pos = 0
+        self._rope = None
+
+    def rope(self, max_pos: int):
+        dev = self.embed_tokens.weight.device
+        if self._rope is None or self.max_pos < max_pos:
+            self.max_pos = max(max_pos, 4096)
+            self._rope = fai.rope_tables(self.max_pos, self.config.head_dim, self.config.rope_theta, dev)
+        return self._rope
+
+    def forward(self, input_ids: torch.Tensor, cache: BlockCache, block_tables: torch.Tensor, pos: torch.Tensor,
+                cache_seqlens: torch.Tensor | None, cu_seqlens: torch.Tensor | None = None,
+                max_seqlen: int = 0) -> torch.Tensor:
+        """Decode: input_ids [B, 1], cache_seqlens [B] -> logits [B, 1, vocab].
+        Prefill: input_ids [T] packed, cu_seqlens [S+1] -> logits [T, vocab].
+        The rope table must already cover every position (call rope() before
+        capturing a graph)."""
+        ids = input_ids.reshape(-1)
+        h = self.embed_tokens(ids)
+        rope = self._rope if self._rope is not None else self.rope(4096)
+        for i, layer in enumerate(self.layers):
+            h = layer(h, cache, i, block_tables, pos, cache_seqlens, rope, cu_seqlens, max_seqlen)
+        h = F.rms_norm(h, (h.shape[-1],), self.norm, self.config.rms_norm_eps)
+        logits = F.linear(h, self.embed_tokens.weight)
+        return logits.view(input_ids.shape[0], -1, logits.shape[-1]) if cache_seqlens is not None else logits
+
+
+def random_model(cfg: ModelConfig, device, seed: int = 0, dtype=torch.bfloat16) -> Qwen3ForCausalLM:
+    """Random-init weights (nn defaults; norm weights near 1) in `dtype`."""
+    torch.manual_seed(seed)
+    with torch.device(device):
+        m = Qwen3ForCausalLM(cfg)
+    with torch.no_grad():
+        g = torch.Generator(device=device).manual_seed(seed)
+        for layer in m.layers:
+            layer.self_attn.q_norm.copy_(1 + 0.1 * torch.randn(cfg.head_dim, generator=g, device=device))
+            layer.self_attn.k_norm.copy_(1 + 0.1 * torch.randn(cfg.head_dim, generator=g, device=device))
+    return m.to(dtype).eval()
+
+
+class DecodeGraph:
+    """Fixed-B decode step captured in a CUDA graph — the engine's DecodeGraph
+    (leaninfer/engine/llm_engine.py:23-86): pinned host staging buffers,
+    static device buffers ids [B,1] i64, pos [B] i64, bt [B, max_blocks] i32,
+    ctx [B] i32; three warm-up forwards on a side stream, then capture. Idle
+    rows get pos 0, ctx 1 and block 0 (the trash block)."""
+
+    def __init__(self, model: Qwen3ForCausalLM, cache: BlockCache, n_slots: int, max_blocks: int) -> None:
+        self.model, self.cache = model, cache
+        dev = cache.device
+        self.host_ids = torch.zeros(n_slots, 1, dtype=torch.long, pin_memory=True)
+        self.host_pos = torch.zeros(n_slots, dtype=torch.long, pin_memory=True)
+        self.host_bt = torch.zeros(n_slots, max_blocks, dtype=torch.int32, pin_memory=True)
+        self.host_ctx = torch.ones(n_slots, dtype=torch.int32, pin_memory=True)
+        self.ids = torch.zeros(n_slots, 1, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(n_slots, dtype=torch.long, device=dev)
+        self.bt = torch.zeros(n_slots, max_blocks, dtype=torch.int32, device=dev)
+        self.ctx = torch.ones(n_slots, dtype=torch.int32, device=dev)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.logits: torch.Tensor | None = None
+        self.next_tokens: torch.Tensor | None = None
+        model.rope(max_blocks * cache.block_size)
+
+    @property
+    def h2d_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.host_ids, self.host_pos, self.host_bt, self.host_ctx))
+
+    def _forward(self):
+        logits = self.model(self.ids, self.cache, self.bt, self.pos, self.ctx)
+        return logits, logits[:, -1].argmax(-1)
+
+    def capture(self) -> None:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                self._forward()
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits, self.next_tokens = self._forward()
+
+    def stage(self, ids, pos, bt, ctx) -> None:
+        """Fill the pinned host buffers (numpy-style views, as the engine does)."""
+        self.host_ids.copy_(ids)
+        self.host_pos.copy_(pos)
+        self.host_bt.zero_()
+        self.host_bt[:, : bt.shape[1]].copy_(bt)
+        self.host_ctx.copy_(ctx)
+
+    def upload(self) -> None:
+        self.ids.copy_(self.host_ids, non_blocking=True)
+        self.pos.copy_(self.host_pos, non_blocking=True)
+        self.bt.copy_(self.host_bt, non_blocking=True)
+        self.ctx.copy_(self.host_ctx, non_blocking=True)
+
+    def replay(self) -> None:
+        if self.graph is None:
+            self.capture()
+        self.graph.replay()
+
+    def step(self) -> list[int]:
+        """H2D copy of the staged inputs, graph replay, D2H of the next tokens
+        (llm_engine.py:65-86)."""
+        self.upload()
+        self.replay()
+        return self.next_tokens.tolist()
+
+    def release(self) -> None:
+        self.graph = None

@@ -129,7 +129,7 @@ def test_strided_q_view(pkg, cuda_dev):
 def test_nonfinite_tail_is_masked(pkg, cuda_dev):
     """Pool rows past cache_seqlens holding NaN/Inf must not leak into the output."""
     W = _workloads()
-    w = W.decode_batch(4, 0, 0, lengths=torch.tensor([5, 17, 250, 300]), nb=None, seed=8)
+    w = W.decode_batch(4, 0, 0, lengths=torch.tensor([5, 17, 250, 300]), num_blocks=None, seed=8)
     kc, vc = w.k_cache.clone(), w.v_cache.clone()
     for b in range(4):
         L = int(w.cache_seqlens[b])
@@ -172,7 +172,7 @@ def test_pinned_by_reference_prefill(pkg, cuda_dev):
 
 def test_bad_block_id_reported(pkg, cuda_dev):
     W = _workloads()
-    w = W.decode_batch(2, 300, 300, nb=8, seed=10)
+    w = W.decode_batch(2, 300, 300, num_blocks=8, seed=10)
     bt = w.block_table.clone()
     bt[1, 1] = 10_000  # outside the pool: read as zeros, reported
     pkg.flash_attn_with_kvcache(w.q.to(cuda_dev), w.k_cache.to(cuda_dev), w.v_cache.to(cuda_dev),
@@ -186,8 +186,8 @@ def test_cuda_graph_capture_and_replay(pkg, cuda_dev):
     """The decode call captures into a CUDA graph (no allocation, no host
     sync, device-side split decisions) and replays with new lengths/tables."""
     W = _workloads()
-    w1 = W.decode_batch(64, 300, 1000, nb=512, seed=11)
-    w2 = W.decode_batch(64, 1, 1024, nb=512, seed=12)
+    w1 = W.decode_batch(64, 300, 1000, num_blocks=512, seed=11)
+    w2 = W.decode_batch(64, 1, 1024, num_blocks=512, seed=12)
     q = w1.q.to(cuda_dev)
     kc, vc = w1.k_cache.to(cuda_dev), w1.v_cache.to(cuda_dev)
     bt = torch.zeros(64, 4, dtype=torch.int32, device=cuda_dev)
