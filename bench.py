@@ -1,0 +1,372 @@
+#!/usr/bin/env python
+"""Benchmark: Qwen3-0.6B decode step at B=128 per GPU on the sm_100a kernels.
+
+Workload (one step): the full decode step of a random-init bf16 Qwen3-0.6B
+(28 layers, hidden 1024, 16/8 GQA heads, head_dim 128, SwiGLU 3072, vocab
+151936, QK-RMSNorm, RoPE theta 1e6) for 128 sequences per GPU with contexts
+uniform in [512, 1024] over a paged cache of 512 blocks x 256 tokens,
+captured in a CUDA graph as the engine's DecodeGraph does. Synthetic data:
+seeded random weights, KV pool, token ids and lengths. Every step streams
+~11.6 GB of KV cache (larger than the 126 MB L2), so no L2 flush is needed.
+
+  value        tokens/s of the device-timed graph replay (next-token argmax
+               included), summed over GPUs; weak scaling (128 rows per GPU).
+  e2e          the same through DecodeGraph.step(): pinned host -> device
+               copy of ids/pos/block table/lengths, replay, next tokens back
+               to the host, every step.
+  roofline     the paged decode attention op (decode kernel + combine) timed
+               alone over the 28 layer caches with CUDA events: algorithmic
+               KV bytes per launch / launch duration, against the measured
+               HBM copy bandwidth.
+  cpu_baseline the reference's decode step in fp32 on the host cores
+               (oracle.qwen3_step), on a layer sample scaled to 28 layers.
+
+--impl reference times that CPU path alone (rank 0), with the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+B_PER_GPU = 128
+CTX_LO, CTX_HI = 512, 1024
+NUM_BLOCKS, BLOCK_SIZE = 512, 256
+METRIC = "decode tok/s (Qwen3-0.6B decode step, B=128/GPU, ctx U[512,1024], paged 256-token blocks, CUDA graph)"
+WORKLOAD = "qwen3-0.6b decode step, B=128 per GPU, contexts U[512,1024], 512x256-token paged KV blocks"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def env_int(name, default):
+    v = os.environ.get(name)
+    return int(v) if v is not None else default
+
+
+def measured_peak_hbm():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the decode kernel from the committed ncu
+    summary (profiles/decode_attention_b128.md), or None."""
+    p = REPO / "profiles" / "decode_attention_b128.md"
+    if not p.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.]+)", p.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        # address the GPU by UUID: CUDA's device order need not match nvidia-smi's
+        try:
+            self.index = f"GPU-{torch.cuda.get_device_properties(index).uuid}"
+        except Exception:
+            self.index = str(index)
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def synth_inputs(rank: int, seed: int = 0):
+    """Seeded per-rank decode inputs: lengths, block tables, ids."""
+    import __graft_entry__
+
+    __graft_entry__.load_package()
+    from lean_infer_b200 import workloads as W
+
+    s = seed + 1000 * rank
+    while True:
+        L = W.seq_lengths(B_PER_GPU, CTX_LO, CTX_HI, s)
+        try:
+            bt, _ = W.deal_blocks(L, BLOCK_SIZE, NUM_BLOCKS, s)
+            break
+        except ValueError:
+            s += 1
+    g = torch.Generator().manual_seed(s + 3)
+    ids = torch.randint(0, 151936, (B_PER_GPU, 1), generator=g)
+    return ids, (L - 1).long(), bt, L.to(torch.int32)
+
+
+def cpu_reference_run(steps: int, warmup: int, sample_layers: int = 4):
+    """The reference's fp32 decode step on the host cores; returns tok/s and
+    a description of the sample."""
+    from oracle.qwen3_step import CpuQwen3Decode
+
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    m = CpuQwen3Decode(sample_layers=sample_layers)
+    ids, pos, bt, ctx = synth_inputs(0)
+    times = []
+    for i in range(warmup + steps):
+        m.decode_step(ids, pos, bt, ctx)
+        if i >= warmup:
+            times.append(m.full_step_seconds())
+    sec = statistics.median(times)
+    return {
+        "value": B_PER_GPU / sec,
+        "unit": "tok/s",
+        "cores": cores,
+        "kind": "port",
+        "sample": (f"fp32 torch on {cores} host threads; B=128 rows, {sample_layers} of 28 layers per step "
+                   f"(layer time scaled x{28 / sample_layers:g}, embedding and lm_head timed once), "
+                   f"median of {steps} steps after {warmup} warm-up"),
+        "ms_per_step": sec * 1e3,
+    }
+
+
+def run_reference(args):
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    r = cpu_reference_run(args.steps, args.warmup, args.sample_layers)
+    out = {
+        "metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
+                   "parallelism": "host cores"},
+        "impl": "reference",
+        "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def run_ours(args):
+    import __graft_entry__
+
+    pkg = __graft_entry__.load_package()
+    from lean_infer_b200 import qwen3
+    from lean_infer_b200.cache import BlockCache
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local = env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    cfg = qwen3.ModelConfig()
+    model = qwen3.random_model(cfg, dev, seed=1234)
+    cache = BlockCache(cfg.num_hidden_layers, NUM_BLOCKS, BLOCK_SIZE, cfg.num_key_value_heads, cfg.head_dim, dev,
+                       zero=False)
+    gen = torch.Generator(device=dev).manual_seed(77 + rank)
+    for t in (cache.k, cache.v):
+        flat = t.view(-1)
+        step = 1 << 28
+        for i in range(0, flat.numel(), step):
+            n = min(step, flat.numel() - i)
+            flat[i:i + n] = torch.randn(n, generator=gen, device=dev)
+    ids, pos, bt, ctx = synth_inputs(rank)
+    max_blocks = -(-CTX_HI // BLOCK_SIZE)
+    dg = qwen3.DecodeGraph(model, cache, B_PER_GPU, max_blocks)
+    dg.stage(ids, pos, bt, ctx)
+    dg.upload()
+    dg.capture()
+    torch.cuda.synchronize()
+    pkg.check_device_errors(local)
+
+    # ---------------------------------------------------------------- value
+    for _ in range(args.warmup):
+        dg.replay()
+    torch.cuda.synchronize()
+    launches_per_step = cfg.num_hidden_layers * 3  # fused pre-attention, decode, combine
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            dg.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    value = world * B_PER_GPU / (ms / 1e3)
+
+    # ---------------------------------------------------------------- e2e
+    for _ in range(max(1, args.warmup // 2)):
+        dg.step()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        dg.stage(ids, pos, bt, ctx)
+        toks = dg.step()  # H2D copies, replay, D2H of the next tokens (syncs)
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(t0.elapsed_time(t1) / args.steps)
+    assert len(toks) == B_PER_GPU
+    d2h = B_PER_GPU * 8
+
+    # ---------------------------------------------------------------- roofline
+    # The decode attention op alone over the 28 layer caches (q from the
+    # workload's distribution), captured in a graph, CUDA events on its stream.
+    qs = [torch.randn(B_PER_GPU, 1, cfg.num_attention_heads, cfg.head_dim, device=dev).to(torch.bfloat16)
+          for _ in range(cfg.num_hidden_layers)]
+    d_bt, d_ctx = dg.bt, dg.ctx
+
+    def attn_all():
+        for li in range(cfg.num_hidden_layers):
+            pkg.flash_attn_with_kvcache(qs[li], cache.k[li], cache.v[li], cache_seqlens=d_ctx, block_table=d_bt,
+                                        causal=True, num_splits=1)
+
+    attn_all()
+    g_attn = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_attn):
+        attn_all()
+    for _ in range(2):
+        g_attn.replay()
+    torch.cuda.synchronize()
+    reps = max(2, args.steps // 2)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for _ in range(reps):
+        g_attn.replay()
+    a1.record()
+    torch.cuda.synchronize()
+    pkg.check_device_errors(local)
+    us_per_launch = max_over_ranks(a0.elapsed_time(a1) * 1e3 / (reps * cfg.num_hidden_layers))
+    kv_bytes = int(ctx.long().sum()) * cfg.num_key_value_heads * cfg.head_dim * 2 * 2
+    qo_bytes = 2 * B_PER_GPU * cfg.num_attention_heads * cfg.head_dim * 2
+    alg_bytes = kv_bytes + qo_bytes
+    achieved = alg_bytes / (us_per_launch * 1e-6) / 1e9
+    peak, peak_kind = measured_peak_hbm()
+    del g_attn
+    dg.release()
+
+    result = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random weights, KV pool, ids, lengths)",
+        "config": {"workload": WORKLOAD, "global_batch": world * B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
+                   "parallelism": f"request-sharded x{world} (no collective)",
+                   "l2": "inputs larger than L2 (~11.6 GB KV streamed per step)", "cuda_graph": True},
+        "e2e": {"value": world * B_PER_GPU / (e2e_ms / 1e3), "unit": "tok/s",
+                "h2d_bytes_per_step": dg.h2d_bytes, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "paged decode attention (la_paged_decode: decode + combine)",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s",
+                     "traffic": profiled_traffic(), "alg_bytes_per_launch": alg_bytes,
+                     "us_per_launch": us_per_launch},
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = cpu_reference_run(args.cpu_steps, 1, args.sample_layers)
+        result["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--sample-layers", type=int, default=4, help="layers per CPU reference step (scaled to 28)")
+    ap.add_argument("--cpu-steps", type=int, default=2, help="timed CPU steps for cpu_baseline")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,100 @@
+"""CPU fp32 restatement of the reference model's decode step — the CPU
+baseline of the benchmark. TEST / BASELINE INFRASTRUCTURE ONLY.
+
+Follows leaninfer/qwen3/model.py:25-112 op for op in fp32 on the host cores:
+embedding, per layer input RMSNorm, q/k/v projections, q_norm/k_norm,
+build_rope + apply_rope (layers.py:7-23), BlockCache.write
+(cache_manager.py:63-76), paged decode attention (the flash_attn_with_kvcache
+contract, computed as gather-by-block_table + one masked fp32 SDPA per layer),
+o_proj, post-attention RMSNorm, SwiGLU MLP, final norm and the tied lm_head.
+
+Weights are random (the benchmark runs on synthetic data). A bounded sample
+can run `sample_layers` of the model's layers: decode_step() then reports the
+time of the layer loop and of the embedding/head separately, and
+full_step_seconds() scales the layer part to the full depth (every layer does
+identical work). All sampled layers share one KV pool (the work per layer is
+unchanged; the host memory footprint drops).
+"""
+from __future__ import annotations
+
+import time
+
+import torch
+import torch.nn.functional as F
+
+from . import paged_attention as opa
+from . import pre_attention as opre
+
+
+class CpuQwen3Decode:
+    def __init__(self, num_layers=28, hidden=1024, heads=16, kv_heads=8, head_dim=128, inter=3072, vocab=151936,
+                 eps=1e-6, theta=1e6, num_blocks=512, block_size=256, seed=0, sample_layers=None):
+        g = torch.Generator().manual_seed(seed)
+        self.L, self.H, self.Hq, self.Hkv, self.D = num_layers, hidden, heads, kv_heads, head_dim
+        self.eps, self.theta = eps, theta
+        self.n_alloc = num_layers if sample_layers is None else min(sample_layers, num_layers)
+
+        # Seeded noise, tiled from a 1 Mi-element block: seeding every element
+        # of ~2 GB with the host RNG would take longer than the timed work.
+        noise = torch.randn(1 << 20, generator=g)
+
+        def fill(shape, scale):
+            n = 1
+            for d in shape:
+                n *= d
+            reps = -(-n // noise.numel())
+            return (noise.repeat(reps)[:n] * scale).view(*shape)
+
+        def lin(o, i):
+            return fill((o, i), 1.0 / i ** 0.5)
+
+        self.embed = fill((vocab, hidden), 1.0)
+        self.layers = []
+        for _ in range(self.n_alloc):
+            self.layers.append(dict(
+                wq=lin(heads * head_dim, hidden), wk=lin(kv_heads * head_dim, hidden),
+                wv=lin(kv_heads * head_dim, hidden), wo=lin(hidden, heads * head_dim),
+                qn=torch.ones(head_dim), kn=torch.ones(head_dim),
+                wg=lin(inter, hidden), wu=lin(inter, hidden), wd=lin(hidden, inter),
+                ln1=torch.ones(hidden), ln2=torch.ones(hidden)))
+        self.norm = torch.ones(hidden)
+        self.k_pool = fill((num_blocks, block_size, kv_heads, head_dim), 1.0)
+        self.v_pool = fill((num_blocks, block_size, kv_heads, head_dim), 1.0).roll(7, dims=0)
+        self.last_times = (0.0, 0.0)
+
+    def full_step_seconds(self) -> float:
+        """Time of the last step scaled to all num_layers layers."""
+        t_layers, t_rest = self.last_times
+        return t_rest + t_layers * self.L / self.n_alloc
+
+    @torch.no_grad()
+    def decode_step(self, ids, pos, block_table, cache_seqlens):
+        """ids [B, 1] int64, pos [B] int64, block_table [B, nb] int32,
+        cache_seqlens [B] int32 -> logits [B, 1, vocab] (fp32). Runs the
+        allocated layers (all of them unless sample_layers was given)."""
+        B = ids.shape[0]
+        Hq, Hkv, D = self.Hq, self.Hkv, self.D
+        t0 = time.perf_counter()
+        h = self.embed[ids]  # [B, 1, H]
+        cos, sin = opre.build_rope(pos, 1, D, self.theta, torch.float32)
+        t1 = time.perf_counter()
+        kp, vp = self.k_pool, self.v_pool
+        for i in range(self.n_alloc):
+            w = self.layers[i]
+            x = F.rms_norm(h, (self.H,), w["ln1"], self.eps)
+            q = F.rms_norm((x @ w["wq"].T).view(B, 1, Hq, D), (D,), w["qn"], self.eps).transpose(1, 2)
+            k = F.rms_norm((x @ w["wk"].T).view(B, 1, Hkv, D), (D,), w["kn"], self.eps).transpose(1, 2)
+            v = (x @ w["wv"].T).view(B, 1, Hkv, D).transpose(1, 2)
+            q = opre.apply_rope(q, cos, sin)
+            k = opre.apply_rope(k, cos, sin)
+            opre.block_cache_write(kp, vp, block_table, pos, k, v)
+            o = opa.paged_decode_padded(q.transpose(1, 2), kp, vp, block_table, cache_seqlens)
+            h = h + o.reshape(B, 1, Hq * D) @ w["wo"].T
+            x = F.rms_norm(h, (self.H,), w["ln2"], self.eps)
+            h = h + (F.silu(x @ w["wg"].T) * (x @ w["wu"].T)) @ w["wd"].T
+        t2 = time.perf_counter()
+        h = F.rms_norm(h, (self.H,), self.norm, self.eps)
+        logits = h @ self.embed.T
+        t3 = time.perf_counter()
+        self.last_times = (t2 - t1, (t1 - t0) + (t3 - t2))
+        return logits
