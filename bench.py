@@ -75,7 +75,7 @@ def profiled_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -94,7 +94,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except Exception:
@@ -185,7 +185,10 @@ def run_reference(args):
     rank = env_int("RANK", 0)
     if rank != 0:
         return
-    r = cpu_reference_run(args.steps, args.warmup, args.sample_layers)
+    # K timed steps after W warm-up, each a bounded sample: fewer layers per
+    # step as K grows so the whole run stays within a few minutes
+    layers = args.sample_layers if args.steps <= 30 else (2 if args.steps <= 100 else 1)
+    r = cpu_reference_run(args.steps, args.warmup, layers)
     out = {
         "metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
@@ -350,16 +353,69 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
 
 
+def run_case(args):
+    """Single-kernel cases for profilers (ncu): run one op a few times on a
+    small, fixed input and exit. --case decode-b128 | decode-long |
+    prefill-b16 | prefill-b1 | pre-attn-b128."""
+    import __graft_entry__
+
+    pkg = __graft_entry__.load_package()
+    from lean_infer_b200 import workloads as W
+
+    dev = torch.device("cuda", 0)
+    reps = 3
+    if args.case in ("decode-b128", "decode-long"):
+        if args.case == "decode-b128":  # one layer of the benchmark step: 408 MB of KV, > L2
+            w = W.decode_batch(128, CTX_LO, CTX_HI, num_blocks=NUM_BLOCKS, block_size=BLOCK_SIZE, seed=1, device=dev)
+        else:  # B=32, contexts U[8192, 32768]
+            w = W.decode_batch(32, 8192, 32768, num_blocks=None, block_size=BLOCK_SIZE, seed=40, device=dev)
+        for _ in range(reps):
+            pkg.flash_attn_with_kvcache(w.q, w.k_cache, w.v_cache, cache_seqlens=w.cache_seqlens,
+                                        block_table=w.block_table, causal=True)
+        info = {"kv_bytes": w.kv_bytes}
+    elif args.case in ("prefill-b16", "prefill-b1"):
+        B = 16 if args.case == "prefill-b16" else 1
+        w = W.prefill_batch(B, CTX_LO, CTX_HI, seed=3, device=dev)
+        mx = int(w.lengths.max())
+        for _ in range(reps):
+            pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx, causal=True)
+        info = {"causal_flops": w.causal_flops}
+    elif args.case == "pre-attn-b128":
+        from lean_infer_b200 import qwen3
+
+        L = W.seq_lengths(128, CTX_LO, CTX_HI, 0)
+        bt, nb = W.deal_blocks(L, BLOCK_SIZE, NUM_BLOCKS, 0)
+        qkv = torch.randn(128, 4096, device=dev).to(torch.bfloat16)
+        kc = torch.zeros(nb, BLOCK_SIZE, 8, 128, dtype=torch.bfloat16, device=dev)
+        vc = torch.zeros_like(kc)
+        cos, sin = pkg.rope_tables(4096, 128, 1e6, dev)
+        w1 = torch.ones(128, dtype=torch.bfloat16, device=dev)
+        for _ in range(reps):
+            pkg.qk_norm_rope_paged_write(qkv[:, :2048].view(128, 16, 128), qkv[:, 2048:3072].view(128, 8, 128),
+                                         qkv[:, 3072:].view(128, 8, 128), w1, w1, cos, sin, (L - 1).to(dev),
+                                         bt.to(dev), kc, vc)
+        info = {"tokens": 128}
+    else:
+        raise SystemExit(f"unknown case {args.case}")
+    torch.cuda.synchronize()
+    pkg.check_device_errors(0)
+    print(json.dumps({"case": args.case, **info}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--sample-layers", type=int, default=4, help="layers per CPU reference step (scaled to 28)")
     ap.add_argument("--cpu-steps", type=int, default=2, help="timed CPU steps for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default=None, help="run one kernel case for a profiler and exit")
     args = ap.parse_args()
+    if args.case:
+        run_case(args)
+        return
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":

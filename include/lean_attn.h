@@ -85,6 +85,8 @@ int la_init(int device);
  * q / k / v: [num_tokens, heads, head_dim] with the given element strides.
  * q_out receives the normed, rotated q; k (normed, rotated) and v are written
  * to k_cache / v_cache at block_table[s][col / block_size], col % block_size.
+ * k_out (nullable) also receives the normed, rotated k as [num_tokens, Hkv, D]
+ * (the fresh keys a prefill attends to, model.py:56-57).
  * ------------------------------------------------------------------------ */
 int la_qk_norm_rope_paged_write(
     const void* q, int64_t q_token_stride, int64_t q_head_stride,
@@ -99,6 +101,7 @@ int la_qk_norm_rope_paged_write(
     int64_t kv_block_stride, int64_t kv_token_stride, int64_t kv_head_stride,
     int64_t num_blocks, int block_size,
     void* q_out, int64_t qo_token_stride, int64_t qo_head_stride,
+    void* k_out, int64_t ko_token_stride, int64_t ko_head_stride,
     int num_q_heads, int num_kv_heads, int head_dim,
     int* dev_error, cudaStream_t stream);
 
@@ -146,6 +149,31 @@ int la_paged_decode(
     void* out, int64_t out_batch_stride, int64_t out_head_stride,
     float* softmax_lse,
     void* workspace, size_t workspace_bytes,
+    int* dev_error, cudaStream_t stream);
+
+/* ------------------------------------------------------------------------
+ * (c) Causal varlen prefill attention on tcgen05 / TMEM.
+ *
+ * Replaces F.scaled_dot_product_attention(q, k, v, is_causal=True,
+ * enable_gqa=True) at leaninfer/qwen3/model.py:56-57 (one prompt, B=1) with
+ * the flash-attn varlen contract: q [total_tokens, Hq, D], k / v
+ * [total_tokens, Hkv, D] bf16 holding num_seqs packed sequences, sequence s
+ * being tokens cu_seqlens[s] .. cu_seqlens[s+1]-1 (int32, on the device);
+ * max_seqlen >= every length (a shorter value is reported as
+ * LA_DEVERR_SEQLEN). causal != 0 masks key j > query i within a sequence.
+ * out: [total_tokens, Hq, D] bf16 (strides and base 16-byte aligned).
+ * softmax_lse (nullable): [Hq, total_tokens] fp32, natural log.
+ * head_dim must be 128 and Hq / Hkv one of 1, 2, 4, 8. No workspace.
+ * ------------------------------------------------------------------------ */
+int la_prefill_varlen(
+    const void* q, int64_t q_token_stride, int64_t q_head_stride,
+    const void* k, int64_t k_token_stride, int64_t k_head_stride,
+    const void* v, int64_t v_token_stride, int64_t v_head_stride,
+    const int32_t* cu_seqlens, int num_seqs, int max_seqlen, int64_t total_tokens,
+    int num_q_heads, int num_kv_heads, int head_dim,
+    float softmax_scale, int causal,
+    void* out, int64_t out_token_stride, int64_t out_head_stride,
+    float* softmax_lse,
     int* dev_error, cudaStream_t stream);
 
 #ifdef __cplusplus

@@ -46,6 +46,7 @@ _SIGNATURES = {
         c_int64, c_int64, c_int64,
         c_int64, c_int,
         c_void_p, c_int64, c_int64,
+        c_void_p, c_int64, c_int64,
         c_int, c_int, c_int,
         c_void_p, c_void_p,
     ],
@@ -76,17 +77,15 @@ _SIGNATURES = {
         c_void_p, c_size_t,
         c_void_p, c_void_p,
     ],
-    "la_prefill_workspace_size": [c_int, c_int, c_int, c_int, c_int, POINTER(c_size_t)],
     "la_prefill_varlen": [
         c_void_p, c_int64, c_int64,
         c_void_p, c_int64, c_int64,
         c_void_p, c_int64, c_int64,
-        c_void_p, c_int, c_int,
+        c_void_p, c_int, c_int, c_int64,
         c_int, c_int, c_int,
         c_float, c_int,
         c_void_p, c_int64, c_int64,
         c_void_p,
-        c_void_p, c_size_t,
         c_void_p, c_void_p,
     ],
 }

@@ -102,6 +102,7 @@ int la_init(int device) {
   if (la::num_sms(device) <= 0) st = LA_ERR_CUDA;
   if (st == LA_OK) st = la::decode_init(device);
   if (st == LA_OK) st = la::pre_attn_init(device);
+  if (st == LA_OK) st = la::prefill_init(device);
   if (prev >= 0 && prev != device) cudaSetDevice(prev);
   return st;
 }

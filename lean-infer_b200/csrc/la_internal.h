@@ -48,5 +48,6 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 // Per-kernel init hooks called by la_init().
 int decode_init(int device);
 int pre_attn_init(int device);
+int prefill_init(int device);
 
 }  // namespace la

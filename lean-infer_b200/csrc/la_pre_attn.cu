@@ -1,5 +1,5 @@
 // (a) Fused pre-attention kernel: per-head QK RMSNorm + NeoX RoPE + paged KV
-// scatter, one warp per token.
+// scatter, one warp per (token, head row).
 //
 // Reference op sequence (one layer), all replaced by one launch:
 //   q = q_norm(q.view(b, n, Hq, D))              leaninfer/qwen3/model.py:50
@@ -60,6 +60,8 @@ struct Params {
   int bs;
   __nv_bfloat16* qo;
   long long qo_ts, qo_hs;
+  __nv_bfloat16* ko;  // optional contiguous copy of the rotated k
+  long long ko_ts, ko_hs;
   int hq, hkv;
   bool norm_rope;  // false: plain scatter of k/v (no q)
   int* err;
@@ -110,12 +112,19 @@ __device__ __forceinline__ void norm_rope_row(float (&x)[4], const float (&w)[4]
   }
 }
 
+// One warp per (token, row): rows 0..Hq-1 are q heads, then Hkv k heads, then
+// Hkv v heads (no q rows and no norm for the plain write). Every warp does one
+// load -> (norm, rope) -> store chain, so the launch is one memory round trip
+// deep whatever the head count.
 __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_write_kernel(const Params p) {
   grid_dependency_wait();
-  const int lane = threadIdx.x & 31;
-  const long long tok = static_cast<long long>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
   // Let the attention kernel that follows start its prologue.
   grid_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int rows = p.hq + 2 * p.hkv;
+  const long long wg = static_cast<long long>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+  const long long tok = wg / rows;
+  const int r = static_cast<int>(wg - tok * rows);
   if (tok >= p.num_tokens) return;
 
   int s;
@@ -134,8 +143,27 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_write_kernel(const P
     t = tok - p.cu[s];
   }
   const long long col = p.pos[s] + t;
+  const int d0 = lane * 4;
 
-  // Destination row in the paged cache.
+  if (r < p.hq) {  // q row: norm + rope -> q_out
+    float c[4], sn[4], w[4], x[4];
+    long long rp = col;
+    if (rp < 0 || rp >= p.max_pos) {
+      if (p.err) atomicCAS(p.err, 0, LA_DEVERR_ROPE_POS);
+      rp = 0;
+    }
+    load4(p.q + tok * p.q_ts + r * p.q_hs + d0, x);
+    load4(p.rcos + rp * (kD / 2) + (d0 & 63), c);
+    load4(p.rsin + rp * (kD / 2) + (d0 & 63), sn);
+    load4(p.qw + d0, w);
+    norm_rope_row(x, w, c, sn, p.eps, lane);
+    store4(p.qo + tok * p.qo_ts + r * p.qo_hs + d0, x);
+    return;
+  }
+
+  // k or v row: destination row in the paged cache.
+  const bool is_k = r < p.hq + p.hkv;
+  const int h = is_k ? r - p.hq : r - p.hq - p.hkv;
   long long dst = -1;
   if (col >= 0) {
     const long long lb = col / p.bs;
@@ -149,42 +177,25 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_write_kernel(const P
   } else if (p.err) {
     atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
   }
-  const int d0 = lane * 4;
 
-  if (p.norm_rope) {
-    float c[4], sn[4], wq[4], wk[4];
+  if (is_k && p.norm_rope) {
+    float c[4], sn[4], w[4], x[4];
     long long rp = col;
     if (rp < 0 || rp >= p.max_pos) {
       if (p.err) atomicCAS(p.err, 0, LA_DEVERR_ROPE_POS);
       rp = 0;
     }
+    load4(p.k + tok * p.k_ts + h * p.k_hs + d0, x);
     load4(p.rcos + rp * (kD / 2) + (d0 & 63), c);
     load4(p.rsin + rp * (kD / 2) + (d0 & 63), sn);
-    load4(p.qw + d0, wq);
-    load4(p.kw + d0, wk);
-    for (int h = 0; h < p.hq; ++h) {
-      float x[4];
-      load4(p.q + tok * p.q_ts + h * p.q_hs + d0, x);
-      norm_rope_row(x, wq, c, sn, p.eps, lane);
-      store4(p.qo + tok * p.qo_ts + h * p.qo_hs + d0, x);
-    }
-    for (int h = 0; h < p.hkv; ++h) {
-      float x[4];
-      load4(p.k + tok * p.k_ts + h * p.k_hs + d0, x);
-      norm_rope_row(x, wk, c, sn, p.eps, lane);
-      if (dst >= 0) store4(p.kc + dst + h * p.kv_hs + d0, x);
-    }
-  } else if (dst >= 0) {
-    for (int h = 0; h < p.hkv; ++h) {
-      const uint2 u = *reinterpret_cast<const uint2*>(p.k + tok * p.k_ts + h * p.k_hs + d0);
-      *reinterpret_cast<uint2*>(p.kc + dst + h * p.kv_hs + d0) = u;
-    }
-  }
-  if (dst >= 0) {
-    for (int h = 0; h < p.hkv; ++h) {
-      const uint2 u = *reinterpret_cast<const uint2*>(p.v + tok * p.v_ts + h * p.v_hs + d0);
-      *reinterpret_cast<uint2*>(p.vc + dst + h * p.kv_hs + d0) = u;
-    }
+    load4(p.kw + d0, w);
+    norm_rope_row(x, w, c, sn, p.eps, lane);
+    if (dst >= 0) store4(p.kc + dst + h * p.kv_hs + d0, x);
+    if (p.ko) store4(p.ko + tok * p.ko_ts + h * p.ko_hs + d0, x);
+  } else if (dst >= 0) {  // plain copy: v rows, and k rows of the plain write
+    const __nv_bfloat16* src = is_k ? p.k + tok * p.k_ts + h * p.k_hs : p.v + tok * p.v_ts + h * p.v_hs;
+    __nv_bfloat16* dc = (is_k ? p.kc : p.vc) + dst + h * p.kv_hs;
+    *reinterpret_cast<uint2*>(dc + d0) = *reinterpret_cast<const uint2*>(src + d0);
   }
 }
 
@@ -207,7 +218,8 @@ static int check_common(const Params& p) {
 
 static int launch(const Params& p, cudaStream_t stream) {
   if (p.num_tokens == 0) return LA_OK;
-  const long long blocks = (p.num_tokens + kWarps - 1) / kWarps;
+  const long long warps = p.num_tokens * (p.hq + 2 * p.hkv);
+  const long long blocks = (warps + kWarps - 1) / kWarps;
   if (blocks > 0x7fffffffLL) return LA_ERR_INVALID_ARGUMENT;
   return cuda_status(launch_pdl(qk_norm_rope_write_kernel, dim3(static_cast<unsigned>(blocks)), dim3(kWarps * 32), 0,
                                 stream, p));
@@ -230,11 +242,11 @@ extern "C" int la_qk_norm_rope_paged_write(
     const int64_t* seq_start_pos, const int32_t* cu_seqlens, int num_seqs, int q_len, int64_t num_tokens,
     const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq, void* k_cache, void* v_cache,
     int64_t kv_block_stride, int64_t kv_token_stride, int64_t kv_head_stride, int64_t num_blocks, int block_size,
-    void* q_out, int64_t qo_token_stride, int64_t qo_head_stride, int num_q_heads, int num_kv_heads, int head_dim,
-    int* dev_error, cudaStream_t stream) {
+    void* q_out, int64_t qo_token_stride, int64_t qo_head_stride, void* k_out, int64_t ko_token_stride,
+    int64_t ko_head_stride, int num_q_heads, int num_kv_heads, int head_dim, int* dev_error, cudaStream_t stream) {
   using namespace la;
   if (head_dim != pre::kD) return LA_ERR_UNSUPPORTED;
-  pre::Params p;
+  pre::Params p = {};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.q_ts = q_token_stride;
   p.q_hs = q_head_stride;
@@ -268,6 +280,9 @@ extern "C" int la_qk_norm_rope_paged_write(
   p.qo = static_cast<__nv_bfloat16*>(q_out);
   p.qo_ts = qo_token_stride;
   p.qo_hs = qo_head_stride;
+  p.ko = static_cast<__nv_bfloat16*>(k_out);
+  p.ko_ts = ko_token_stride;
+  p.ko_hs = ko_head_stride;
   p.hq = num_q_heads;
   p.hkv = num_kv_heads;
   p.norm_rope = true;
@@ -278,9 +293,11 @@ extern "C" int la_qk_norm_rope_paged_write(
       num_q_heads <= 0)
     return LA_ERR_INVALID_ARGUMENT;
   if (!(eps >= 0.f)) return LA_ERR_INVALID_ARGUMENT;
-  const long long st2[] = {q_token_stride, q_head_stride, qo_token_stride, qo_head_stride};
+  const long long st2[] = {q_token_stride, q_head_stride, qo_token_stride, qo_head_stride,
+                           k_out ? ko_token_stride : 0, k_out ? ko_head_stride : 0};
   for (long long x : st2)
     if (x % 4) return LA_ERR_ALIGNMENT;
+  if (k_out && !aligned(k_out, 8)) return LA_ERR_ALIGNMENT;
   if (!aligned(q, 8) || !aligned(q_out, 8) || !aligned(q_norm_weight, 8) || !aligned(k_norm_weight, 8) ||
       !aligned(rope_cos, 8) || !aligned(rope_sin, 8))
     return LA_ERR_ALIGNMENT;

@@ -1,0 +1,376 @@
+// (c) Causal varlen prefill attention on the 5th-generation tensor cores
+// (tcgen05.mma, accumulators in TMEM, operands staged by TMA), sm_100a.
+//
+// Semantics: for every packed sequence s (tokens cu_seqlens[s] ..
+// cu_seqlens[s+1]-1) and query head h, softmax(scale * Q K^T) V over the keys of
+// the same sequence and kv head h / G, causal (key j visible to query i iff
+// j <= i) — the reference's F.scaled_dot_product_attention(q, k, v,
+// is_causal=True, enable_gqa=True) at leaninfer/qwen3/model.py:56-57, applied
+// to many prompts at once (flash-attn varlen contract).
+//
+// CTA tile: 128 query rows = the tq = 128/G consecutive tokens of the G query
+// heads that share one kv head (GQA packing: every K/V tile feeds all G
+// heads), against KV tiles of 128 keys. Per KV tile j:
+//   S_j  = Q K_j^T        tcgen05.mma M128 N128 K16 x8, fp32 in TMEM (2 buffers)
+//   P_j  = exp2(S_j*scale*log2e - m)  by 4 softmax warps, one thread per row,
+//          written to shared memory as bf16 in the MMA's K-major layout
+//   O   += P_j V_j        tcgen05.mma with V read MN-major, fp32 in TMEM
+// The row max is only raised (and O, l rescaled) when a tile's max exceeds the
+// running one by more than 8 (log2 units), so P stays <= 256 and most tiles
+// skip the O rescale. S_{j+1} is issued while softmax works on S_j.
+//
+// Warps: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 = softmax and
+// epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows of that quarter).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "la_internal.h"
+#include "la_ptx.cuh"
+
+namespace la {
+namespace prefill {
+
+constexpr int kD = 128;
+constexpr int kRows = 128;          // query rows per CTA
+constexpr int kKeys = 128;          // keys per KV tile
+constexpr int kHalf = kRows * 128;  // one 64-wide half of a 128-row tile: 16 KB (SW128 rows)
+constexpr int kTile = 2 * kHalf;    // 32 KB
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O [256,384)
+constexpr uint32_t kColO = 256;
+constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, false, false);
+constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, false, true);
+constexpr size_t kSmemBytes = 6 * kTile + 1024 /*barriers*/ + 1024 /*align slack*/;
+
+struct Params {
+  const int* cu;
+  int num_seqs;
+  int n_qt;  // query tiles of the longest sequence
+  int tq;    // tokens per query tile (128 / group)
+  int hq, hkv, group;
+  int causal;
+  float scale_log2;
+  __nv_bfloat16* out;
+  long long out_ts, out_hs;
+  float* lse;  // [hq, total] natural log, or null
+  long long total;
+  int* err;
+};
+
+// K-major operand (rows of 128 bytes, SW128): k-step ks covers elements
+// 16ks..16ks+15 of the 128-wide reduction dimension, split into two halves.
+__device__ __forceinline__ uint64_t desc_kmajor(const uint8_t* tile, int ks) {
+  return smem_desc_sw128(smem_u32(tile) + (ks >> 2) * kHalf + (ks & 3) * 32, 16, 1024);
+}
+// MN-major operand (V: rows = keys, 128 B = 64 dims per half): k-step ks
+// covers keys 16ks..16ks+15 = two 8-row groups (SBO 1024 B); the second
+// 64-dim half is LBO = 16 KB away.
+__device__ __forceinline__ uint64_t desc_mnmajor(const uint8_t* tile, int ks) {
+  return smem_desc_sw128(smem_u32(tile) + ks * 2048, kHalf, 1024);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + kTile;      // 2 stages
+  uint8_t* sV = smem + 3 * kTile;  // 2 stages
+  uint8_t* sP = smem + 5 * kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTile);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_empty = bars + 7;   // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int s = blockIdx.x / p.hkv;
+  const int h = blockIdx.x - s * p.hkv;
+  const int qt = p.n_qt - 1 - static_cast<int>(blockIdx.y);  // longest (most KV tiles) first
+  const float NEG_INF = -__int_as_float(0x7f800000);
+
+  grid_dependency_wait();
+  const int seq0 = p.cu[s];
+  const int L = p.cu[s + 1] - seq0;
+  if (blockIdx.y == 0 && threadIdx.x == 0 && L > p.n_qt * p.tq && p.err) atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
+  const int q0 = qt * p.tq;
+  if (q0 >= L) return;  // whole CTA, before any barrier or TMEM use
+  const int kv_end = p.causal ? min(q0 + p.tq, L) : L;
+  const int n_kv = (kv_end + kKeys - 1) / kKeys;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(q_full, kTile);
+      for (int g = 0; g < p.group; ++g)
+        for (int half = 0; half < 2; ++half)
+          tma_load_3d(sQ + half * kHalf + g * p.tq * 128, &tm_q, q_full, half * 64, h * p.group + g, seq0 + q0);
+      int j = 0;
+      for (; j < n_kv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+        for (int half = 0; half < 2; ++half) {
+          tma_load_3d(sK + st * kTile + half * kHalf, &tm_k, &kv_full[st], half * 64, h, seq0 + j * kKeys);
+          tma_load_3d(sV + st * kTile + half * kHalf, &tm_v, &kv_full[st], half * 64, h, seq0 + j * kKeys);
+        }
+      }
+      if (j < n_kv)  // early exit: let issued copies land (bounded)
+        for (int jj = (j > 2 ? j - 2 : 0); jj < j; ++jj) mbar_wait(&kv_full[jj & 1], (jj >> 1) & 1, nullptr, 0);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(q_full, 0, p.err, LA_DEVERR_WAIT_TIMEOUT);
+      for (int j = 0; ok && j <= n_kv; ++j) {
+        if (j < n_kv) {
+          const int st = j & 1;
+          ok = mbar_wait(&kv_full[st], (j >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT) &&
+               mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint8_t* kt = sK + st * kTile;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_f16_ss(tmem + st * kKeys, desc_kmajor(sQ, ks), desc_kmajor(kt, ks), kIdescQK, ks > 0 ? 1u : 0u);
+          umma_commit(&s_full[st]);
+        }
+        if (j >= 1) {
+          const int i = j - 1;
+          ok = mbar_wait(p_full, i & 1, p.err, LA_DEVERR_WAIT_TIMEOUT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint8_t* vt = sV + (i & 1) * kTile;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_f16_ss(tmem + kColO, desc_kmajor(sP, ks), desc_mnmajor(vt, ks), kIdescPV,
+                        (i > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(o_done);
+          umma_commit(&kv_empty[i & 1]);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int g = row / p.tq;
+    const int t = q0 + (row - g * p.tq);  // token index within the sequence
+    const int lim = p.causal ? min(t + 1, L) : L;  // keys [0, lim) are visible
+    const float sl2 = p.scale_log2;
+    float m = NEG_INF, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int sb = j & 1;
+      // tcgen05.ld is warp-collective: keep the decision to continue warp-uniform
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (j >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(taddr + sb * kKeys + c * 32, sv[c]);
+      tc_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+
+      const int nvis = lim - j * kKeys;  // visible columns of this tile
+      float mt = NEG_INF;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float x = (c * 32 + e < nvis) ? sv[c][e] * sl2 : NEG_INF;
+          sv[c][e] = x;
+          mt = fmaxf(mt, x);
+        }
+      const float m_new = (mt > m + 8.f) ? mt : m;
+      const float alpha = ex2(m - m_new);  // 0 on the first tile, 1 when m is kept
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float pe = ex2(sv[c][e] - m_new);
+          sv[c][e] = pe;
+          rs += pe;
+        }
+      l = l * alpha + rs;
+
+      if (j >= 1) {  // PV_{j-1} done: P buffer free, O stable
+        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, m_new != m)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tmem_ld32(taddr + kColO + c * 32, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(taddr + kColO + c * 32, o);
+          }
+          tc_wait_st();
+        }
+      }
+      m = m_new;
+      // P row -> shared memory, bf16, K-major SW128 (keys 0-63 | 64-127).
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        const int c = ch >> 2, e0 = (ch & 3) * 8;
+        uint4 u;
+        u.x = pack_bf16x2(sv[c][e0 + 0], sv[c][e0 + 1]);
+        u.y = pack_bf16x2(sv[c][e0 + 2], sv[c][e0 + 3]);
+        u.z = pack_bf16x2(sv[c][e0 + 4], sv[c][e0 + 5]);
+        u.w = pack_bf16x2(sv[c][e0 + 6], sv[c][e0 + 7]);
+        const int half = ch >> 3, chunk = ch & 7;
+        *reinterpret_cast<uint4*>(sP + half * kHalf + swz128(row, chunk)) = u;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ------------------------------------------------------------ epilogue
+    if (__all_sync(0xffffffffu, ok && mbar_wait(o_done, (n_kv - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int qh = h * p.group + g;
+      __nv_bfloat16* orow = p.out + static_cast<long long>(seq0 + t) * p.out_ts + static_cast<long long>(qh) * p.out_hs;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        tmem_ld32(taddr + kColO + c * 32, o);  // all lanes: tcgen05.ld is warp-collective
+        tc_wait_ld();
+        if (t < L) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint4 u;
+            u.x = pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv);
+            u.y = pack_bf16x2(o[q4 * 8 + 2] * inv, o[q4 * 8 + 3] * inv);
+            u.z = pack_bf16x2(o[q4 * 8 + 4] * inv, o[q4 * 8 + 5] * inv);
+            u.w = pack_bf16x2(o[q4 * 8 + 6] * inv, o[q4 * 8 + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + q4 * 8) = u;
+          }
+        }
+      }
+      if (p.lse && t < L)
+        p.lse[static_cast<long long>(qh) * p.total + seq0 + t] =
+            l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace prefill
+
+int prefill_init(int device) {
+  (void)device;
+  return cuda_status(cudaFuncSetAttribute(prefill::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(prefill::kSmemBytes)));
+}
+
+}  // namespace la
+
+extern "C" int la_prefill_varlen(const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,
+                                 int64_t k_token_stride, int64_t k_head_stride, const void* v, int64_t v_token_stride,
+                                 int64_t v_head_stride, const int32_t* cu_seqlens, int num_seqs, int max_seqlen,
+                                 int64_t total_tokens, int num_q_heads, int num_kv_heads, int head_dim,
+                                 float softmax_scale, int causal, void* out, int64_t out_token_stride,
+                                 int64_t out_head_stride, float* softmax_lse, int* dev_error, cudaStream_t stream) {
+  using namespace la;
+  using namespace la::prefill;
+  if (!q || !k || !v || !cu_seqlens || !out) return LA_ERR_INVALID_ARGUMENT;
+  if (num_seqs < 0 || max_seqlen < 0 || total_tokens < 0) return LA_ERR_INVALID_ARGUMENT;
+  if (num_seqs == 0 || max_seqlen == 0 || total_tokens == 0) return LA_OK;
+  if (head_dim != kD) return LA_ERR_UNSUPPORTED;
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return LA_ERR_INVALID_ARGUMENT;
+  const int group = num_q_heads / num_kv_heads;
+  if (group != 1 && group != 2 && group != 4 && group != 8) return LA_ERR_UNSUPPORTED;
+  if (!(softmax_scale > 0.f)) return LA_ERR_INVALID_ARGUMENT;
+  if (total_tokens > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
+  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16)) return LA_ERR_ALIGNMENT;
+  const long long st[] = {q_token_stride, q_head_stride, k_token_stride, k_head_stride, v_token_stride, v_head_stride,
+                          out_token_stride, out_head_stride};
+  for (long long x : st)
+    if (x <= 0 || x % 8) return LA_ERR_ALIGNMENT;
+
+  const int tq = kRows / group;
+  CUtensorMap tq_map, tk_map, tv_map;
+  int stt;
+  {
+    const uint64_t dims[3] = {128, static_cast<uint64_t>(num_q_heads), static_cast<uint64_t>(total_tokens)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(q_head_stride) * 2, static_cast<uint64_t>(q_token_stride) * 2};
+    const uint32_t box[3] = {64, 1, static_cast<uint32_t>(tq)};
+    if ((stt = encode_tensor_map_bf16(&tq_map, q, 3, dims, strides, box, true)) != LA_OK) return stt;
+  }
+  {
+    const uint64_t dims[3] = {128, static_cast<uint64_t>(num_kv_heads), static_cast<uint64_t>(total_tokens)};
+    const uint32_t box[3] = {64, 1, kKeys};
+    const uint64_t ks[2] = {static_cast<uint64_t>(k_head_stride) * 2, static_cast<uint64_t>(k_token_stride) * 2};
+    const uint64_t vs[2] = {static_cast<uint64_t>(v_head_stride) * 2, static_cast<uint64_t>(v_token_stride) * 2};
+    if ((stt = encode_tensor_map_bf16(&tk_map, k, 3, dims, ks, box, true)) != LA_OK) return stt;
+    if ((stt = encode_tensor_map_bf16(&tv_map, v, 3, dims, vs, box, true)) != LA_OK) return stt;
+  }
+  Params p;
+  p.cu = cu_seqlens;
+  p.num_seqs = num_seqs;
+  p.tq = tq;
+  p.n_qt = (max_seqlen + tq - 1) / tq;
+  p.hq = num_q_heads;
+  p.hkv = num_kv_heads;
+  p.group = group;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_ts = out_token_stride;
+  p.out_hs = out_head_stride;
+  p.lse = softmax_lse;
+  p.total = total_tokens;
+  p.err = dev_error;
+  if (p.n_qt > 65535 || static_cast<long long>(num_seqs) * num_kv_heads > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
+  const dim3 grid(static_cast<unsigned>(num_seqs * num_kv_heads), static_cast<unsigned>(p.n_qt));
+  return cuda_status(launch_pdl(prefill_kernel, grid, dim3(kThreads), kSmemBytes, stream, tq_map, tk_map, tv_map, p));
+}

@@ -275,8 +275,10 @@ def qk_norm_rope_paged_write(
     eps: float = 1e-6,
     cu_seqlens: Optional[torch.Tensor] = None,
     q_out: Optional[torch.Tensor] = None,
+    k_out: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
-    """Fused q_norm/k_norm + RoPE + cache.write for one layer; returns q_out.
+    """Fused q_norm/k_norm + RoPE + cache.write for one layer; returns q_out
+    (and writes the rotated k to k_out as well when given).
 
     q: [T, Hq, D] (or [B, n, Hq, D]); k, v: [T, Hkv, D] (or [B, n, Hkv, D]),
     the raw projections. pos: int64 [num_seqs] start position of each
@@ -312,6 +314,10 @@ def qk_norm_rope_paged_write(
     if q_out is None:
         q_out = torch.empty((T, Hq, D), dtype=q.dtype, device=q.device)
     qo = _tokens_view(q_out, "q_out")
+    ko = None
+    if k_out is not None:
+        ko = _tokens_view(k_out, "k_out")
+        _check(ko.shape == k3.shape and ko.dtype == torch.bfloat16 and ko.stride(-1) == 1, "k_out must match k")
     dev = _device_index(q)
     with torch.cuda.device(dev):
         ensure_init(dev)
@@ -329,6 +335,7 @@ def qk_norm_rope_paged_write(
             k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
             k_cache.shape[0], k_cache.shape[1],
             _ptr(qo), qo.stride(0), qo.stride(1),
+            _ptr(ko), ko.stride(0) if ko is not None else 0, ko.stride(1) if ko is not None else 0,
             Hq, Hkv, D,
             _ptr(error_word(dev)), _stream(q.device),
         )
@@ -373,3 +380,96 @@ def paged_kv_write(
             Hkv, D,
             _ptr(error_word(dev)), _stream(k.device),
         )
+
+
+# --------------------------------------------------------------------------
+# (c) causal varlen prefill
+# --------------------------------------------------------------------------
+def flash_attn_varlen_func(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    cu_seqlens_q: torch.Tensor,
+    cu_seqlens_k: torch.Tensor,
+    max_seqlen_q: int,
+    max_seqlen_k: int,
+    dropout_p: float = 0.0,
+    softmax_scale: Optional[float] = None,
+    causal: bool = False,
+    window_size=(-1, -1),
+    softcap: float = 0.0,
+    alibi_slopes: Optional[torch.Tensor] = None,
+    deterministic: bool = False,
+    return_attn_probs: bool = False,
+    block_table: Optional[torch.Tensor] = None,
+    return_softmax_lse: bool = False,
+):
+    """Packed self-attention over varlen sequences (flash-attn 2.8.3 varlen
+    signature): q [T, Hq, D], k/v [T, Hkv, D] bf16, cu_seqlens int32 [S+1].
+    Query and key sequences are the same tokens (prefill): cu_seqlens_k must
+    be cu_seqlens_q. Returns out [T, Hq, D] (and lse [Hq, T] fp32 when
+    return_softmax_lse)."""
+    if dropout_p != 0.0 or tuple(window_size) != (-1, -1) or softcap != 0.0 or alibi_slopes is not None:
+        raise NotImplementedError("dropout / sliding window / softcap / alibi")
+    if return_attn_probs:
+        raise NotImplementedError("return_attn_probs")
+    if block_table is not None:
+        raise NotImplementedError("paged KV in prefill: pass the fresh k/v")
+    if cu_seqlens_k is not cu_seqlens_q and cu_seqlens_k.data_ptr() != cu_seqlens_q.data_ptr():
+        raise NotImplementedError("cross-attention (cu_seqlens_k != cu_seqlens_q)")
+    _check(q.dim() == 3 and k.dim() == 3 and v.dim() == 3, "q/k/v must be [total_tokens, heads, head_dim]")
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    _check(k.shape[0] == T and v.shape == k.shape and k.shape[2] == D, "q/k/v shapes differ")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check(t.dtype == torch.bfloat16 and t.stride(-1) == 1, f"{name} must be bf16 with a contiguous last axis")
+    _check(cu_seqlens_q.dtype == torch.int32 and cu_seqlens_q.is_contiguous(), "cu_seqlens must be contiguous int32")
+    dev = _device_index(q)
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    out = torch.empty((T, Hq, D), dtype=q.dtype, device=q.device)
+    lse = torch.empty((Hq, T), dtype=torch.float32, device=q.device) if return_softmax_lse else None
+    S = cu_seqlens_q.numel() - 1
+    with torch.cuda.device(dev):
+        ensure_init(dev)
+        _lib.call(
+            "la_prefill_varlen",
+            _ptr(q), q.stride(0), q.stride(1),
+            _ptr(k), k.stride(0), k.stride(1),
+            _ptr(v), v.stride(0), v.stride(1),
+            _ptr(cu_seqlens_q), S, int(max(max_seqlen_q, max_seqlen_k)), T,
+            Hq, Hkv, D,
+            ctypes.c_float(scale), 1 if causal else 0,
+            _ptr(out), out.stride(0), out.stride(1),
+            _ptr(lse),
+            _ptr(error_word(dev)), _stream(q.device),
+        )
+    return (out, lse) if return_softmax_lse else out
+
+
+_uniform_cu: dict[tuple, torch.Tensor] = {}
+
+
+def scaled_dot_product_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, attn_mask=None,
+                                 dropout_p: float = 0.0, is_causal: bool = False, scale: Optional[float] = None,
+                                 enable_gqa: bool = False) -> torch.Tensor:
+    """Drop-in for the prefill call F.scaled_dot_product_attention(q, k, v,
+    is_causal=True, enable_gqa=True) at leaninfer/qwen3/model.py:57:
+    q [B, Hq, L, D], k/v [B, Hkv, L, D] bf16 -> [B, Hq, L, D]. Runs the varlen
+    kernel with B sequences of length L (no copy when the [B, L, H, D] memory
+    order of the engine's transposed projections is contiguous)."""
+    if attn_mask is not None or dropout_p != 0.0:
+        raise NotImplementedError("attn_mask / dropout")
+    B, Hq, L, D = q.shape
+    Hkv = k.shape[1]
+    if Hq != Hkv and not enable_gqa:
+        raise RuntimeError("Hq != Hkv requires enable_gqa=True")
+    qt, kt, vt = (x.transpose(1, 2) for x in (q, k, v))  # [B, L, H, D]
+    qt, kt, vt = (x if x.is_contiguous() else x.contiguous() for x in (qt, kt, vt))
+    key = (B, L, q.device)
+    cu = _uniform_cu.get(key)
+    if cu is None:
+        cu = torch.arange(0, (B + 1) * L, L, dtype=torch.int32, device=q.device)
+        _uniform_cu[key] = cu
+    out = flash_attn_varlen_func(qt.view(B * L, Hq, D), kt.view(B * L, Hkv, D), vt.view(B * L, Hkv, D), cu, cu, L, L,
+                                 softmax_scale=scale, causal=is_causal)
+    return out.view(B, L, Hq, D).transpose(1, 2)

@@ -1,0 +1,126 @@
+"""Causal varlen prefill (kernel c, tcgen05/TMEM) against the fp32 CPU oracle
+and the reference's own SDPA output (golden fixture).
+
+Tolerance: max |out - oracle| <= 2e-2 on bf16 outputs; lse within 1e-2."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import paged_attention as opa
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _case(lengths, hq=16, hkv=8, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.tensor(lengths, dtype=torch.int64)
+    cu = torch.zeros(len(lengths) + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens, 0)
+    T = int(cu[-1])
+    q = torch.randn(T, hq, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(T, hkv, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(T, hkv, 128, generator=g).to(torch.bfloat16)
+    return q, k, v, cu, int(lens.max()) if len(lengths) else 0
+
+
+def run(pkg, dev, lengths, hq=16, hkv=8, seed=0, causal=True, lse=False):
+    q, k, v, cu, mx = _case(lengths, hq, hkv, seed)
+    res = pkg.flash_attn_varlen_func(q.to(dev), k.to(dev), v.to(dev), cu.to(dev), cu.to(dev), mx, mx, causal=causal,
+                                     return_softmax_lse=lse)
+    out, lse_d = res if lse else (res, None)
+    torch.cuda.synchronize()
+    pkg.check_device_errors(dev.index)
+    if causal:
+        ref = opa.varlen_causal_prefill(q, k, v, cu, return_lse=lse)
+    else:
+        ref = _noncausal(q, k, v, cu)
+    ref, ref_lse = ref if lse else (ref, None)
+    got = out.cpu().float()
+    assert torch.isfinite(got).all()
+    err = (got - ref).abs().max().item()
+    assert err <= TOL, f"max abs err {err}"
+    if lse:
+        assert (lse_d.cpu().t() - ref_lse).abs().max().item() <= 1e-2
+    return err
+
+
+def _noncausal(q, k, v, cu):
+    out = torch.zeros(q.shape, dtype=torch.float32)
+    for s in range(cu.numel() - 1):
+        a, b = int(cu[s]), int(cu[s + 1])
+        if b > a:
+            o = torch.nn.functional.scaled_dot_product_attention(
+                q[a:b].float().transpose(0, 1)[None], k[a:b].float().transpose(0, 1)[None],
+                v[a:b].float().transpose(0, 1)[None], enable_gqa=True)
+            out[a:b] = o[0].transpose(0, 1)
+    return out
+
+
+def test_golden_reference_sdpa(pkg, cuda_dev):
+    """The reference's own fp32 SDPA prefill (model.py:56-57), L=80."""
+    g = dict(np.load(GOLDEN / "attention_prefill.npz"))
+    q = torch.from_numpy(g["q"]).transpose(0, 1).contiguous().to(torch.bfloat16)
+    k = torch.from_numpy(g["k"]).transpose(0, 1).contiguous().to(torch.bfloat16)
+    v = torch.from_numpy(g["v"]).transpose(0, 1).contiguous().to(torch.bfloat16)
+    L = q.shape[0]
+    cu = torch.tensor([0, L], dtype=torch.int32, device=cuda_dev)
+    out = pkg.flash_attn_varlen_func(q.to(cuda_dev), k.to(cuda_dev), v.to(cuda_dev), cu, cu, L, L, causal=True)
+    err = (out.cpu().float() - torch.from_numpy(g["o"]).transpose(0, 1)).abs().max().item()
+    assert err <= TOL, err
+
+
+def test_config_b16_packed(pkg, cuda_dev):
+    """16 packed prompts, lengths U[512,1024]."""
+    from lean_infer_b200 import workloads as W
+
+    L = W.seq_lengths(16, 512, 1024, 3).tolist()
+    run(pkg, cuda_dev, L, seed=1, lse=True)
+
+
+def test_config_b1(pkg, cuda_dev):
+    run(pkg, cuda_dev, [777], seed=2)
+
+
+@pytest.mark.parametrize("L", [1, 2, 63, 64, 65, 127, 128, 129, 255, 256, 1024, 1100])
+def test_lengths(pkg, cuda_dev, L):
+    run(pkg, cuda_dev, [L], seed=L)
+
+
+def test_ragged_with_empty(pkg, cuda_dev):
+    run(pkg, cuda_dev, [5, 0, 300, 1, 0, 129, 64], seed=9, lse=True)
+
+
+@pytest.mark.parametrize("group", [1, 4, 8])
+def test_group_sizes(pkg, cuda_dev, group):
+    run(pkg, cuda_dev, [100, 333, 17], hq=4 * group, hkv=4, seed=20 + group)
+
+
+def test_noncausal(pkg, cuda_dev):
+    run(pkg, cuda_dev, [200, 77, 300], seed=31, causal=False)
+
+
+def test_sdpa_drop_in(pkg, cuda_dev):
+    """The call-site form: q [B, Hq, L, D], k/v [B, Hkv, L, D]."""
+    g = torch.Generator().manual_seed(4)
+    B, L = 2, 300
+    q = torch.randn(B, L, 16, 128, generator=g).to(torch.bfloat16).transpose(1, 2)
+    k = torch.randn(B, L, 8, 128, generator=g).to(torch.bfloat16).transpose(1, 2)
+    v = torch.randn(B, L, 8, 128, generator=g).to(torch.bfloat16).transpose(1, 2)
+    out = pkg.scaled_dot_product_attention(q.to(cuda_dev), k.to(cuda_dev), v.to(cuda_dev), is_causal=True,
+                                           enable_gqa=True)
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=True,
+                                                           enable_gqa=True)
+    assert out.shape == q.shape
+    assert (out.cpu().float() - ref).abs().max().item() <= TOL
+
+
+def test_max_seqlen_too_small_reported(pkg, cuda_dev):
+    q, k, v, cu, mx = _case([300, 40])
+    pkg.flash_attn_varlen_func(q.to(cuda_dev), k.to(cuda_dev), v.to(cuda_dev), cu.to(cuda_dev), cu.to(cuda_dev),
+                               100, 100, causal=True)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="longer"):
+        pkg.check_device_errors(cuda_dev.index)
