@@ -416,7 +416,10 @@ def flash_attn_varlen_func(
     if block_table is not None:
         raise NotImplementedError("paged KV in prefill: pass the fresh k/v")
     if cu_seqlens_k is not cu_seqlens_q and cu_seqlens_k.data_ptr() != cu_seqlens_q.data_ptr():
-        raise NotImplementedError("cross-attention (cu_seqlens_k != cu_seqlens_q)")
+        # distinct tensors: compare the values (a device sync; pass one tensor
+        # twice, as prefill does, to avoid it)
+        if cu_seqlens_k.shape != cu_seqlens_q.shape or not torch.equal(cu_seqlens_k, cu_seqlens_q):
+            raise NotImplementedError("cross-attention (cu_seqlens_k != cu_seqlens_q)")
     _check(q.dim() == 3 and k.dim() == 3 and v.dim() == 3, "q/k/v must be [total_tokens, heads, head_dim]")
     T, Hq, D = q.shape
     Hkv = k.shape[1]

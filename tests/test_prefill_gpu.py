@@ -28,7 +28,8 @@ def _case(lengths, hq=16, hkv=8, seed=0):
 
 def run(pkg, dev, lengths, hq=16, hkv=8, seed=0, causal=True, lse=False):
     q, k, v, cu, mx = _case(lengths, hq, hkv, seed)
-    res = pkg.flash_attn_varlen_func(q.to(dev), k.to(dev), v.to(dev), cu.to(dev), cu.to(dev), mx, mx, causal=causal,
+    cud = cu.to(dev)
+    res = pkg.flash_attn_varlen_func(q.to(dev), k.to(dev), v.to(dev), cud, cud, mx, mx, causal=causal,
                                      return_softmax_lse=lse)
     out, lse_d = res if lse else (res, None)
     torch.cuda.synchronize()
