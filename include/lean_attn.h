@@ -151,6 +151,37 @@ int la_paged_decode(
     void* workspace, size_t workspace_bytes,
     int* dev_error, cudaStream_t stream);
 
+/* Allocation-free form of la_paged_decode, for callers that cannot allocate
+ * device memory where they run decode: a C/C++ host in the middle of a
+ * stream capture (cudaMalloc cannot be captured), a runtime that hands out
+ * device memory only from a fixed arena, or a latency-bound loop where an
+ * allocation would synchronise the device. It has no counterpart in the
+ * reference (flash-attn allocates its own split buffers).
+ * Same arguments and results as la_paged_decode without the workspace: the
+ * split-KV partials live in a fixed LA_NOALLOC_SCRATCH_BYTES array inside
+ * this library, held on every GPU that loads it until the process exits.
+ * Calls whose partials need more (2 * #SMs * num_q_heads * (head_dim + 1)
+ * fp32, e.g. more than 27 query heads on a 148-SM B200) return
+ * LA_ERR_WORKSPACE. No call allocates. All calls share the array, so calls
+ * that overlap on the GPU (other streams or threads) race; nothing in it must
+ * start at zero. The first call on each device resolves the array's device
+ * address (and loads the module there): make that first call before any
+ * stream capture. */
+#define LA_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+int la_paged_decode_noalloc(
+    const void* q, int64_t q_batch_stride, int64_t q_head_stride,
+    const void* k_cache, const void* v_cache,
+    int64_t kv_block_stride, int64_t kv_token_stride, int64_t kv_head_stride,
+    int64_t num_blocks, int block_size,
+    const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
+    const int32_t* cache_seqlens,
+    int batch, int num_q_heads, int num_kv_heads, int head_dim,
+    float softmax_scale,
+    void* out, int64_t out_batch_stride, int64_t out_head_stride,
+    float* softmax_lse,
+    int* dev_error, cudaStream_t stream);
+
 /* ------------------------------------------------------------------------
  * (c) Causal varlen prefill attention on tcgen05 / TMEM.
  *

@@ -77,6 +77,19 @@ _SIGNATURES = {
         c_void_p, c_size_t,
         c_void_p, c_void_p,
     ],
+    "la_paged_decode_noalloc": [
+        c_void_p, c_int64, c_int64,
+        c_void_p, c_void_p,
+        c_int64, c_int64, c_int64,
+        c_int64, c_int,
+        c_void_p, c_int64, c_int,
+        c_void_p,
+        c_int, c_int, c_int, c_int,
+        c_float,
+        c_void_p, c_int64, c_int64,
+        c_void_p,
+        c_void_p, c_void_p,
+    ],
     "la_prefill_varlen": [
         c_void_p, c_int64, c_int64,
         c_void_p, c_int64, c_int64,
