@@ -181,6 +181,59 @@ def cpu_reference_run(steps: int, warmup: int, sample_layers: int = 4):
     }
 
 
+def kv_head_sharded_layer(pkg, dist, world, rank, dev, reps, max_over_ranks):
+    """The KV-head-sharded partition at `world` GPUs: 128*world requests, each
+    rank holding 8/world kv heads of all of them; one 'layer' = the decode
+    kernel on the local heads + NCCL all-gather of the [B, 16/world, 128]
+    outputs into [B, 16, 128]. Times are CUDA events, max over ranks."""
+    from lean_infer_b200 import sharding as S
+    from lean_infer_b200 import workloads as W
+
+    sh = S.kv_head_shard(rank, world, 8, 16)
+    B = B_PER_GPU * world
+    L = W.seq_lengths(B, CTX_LO, CTX_HI, 500)  # identical on every rank
+    bt, nb = W.deal_blocks(L, BLOCK_SIZE, None, 500)
+    gen = torch.Generator(device=dev).manual_seed(900 + rank)
+    pools = []
+    for _ in range(4):  # rotate 4 pools (each > L2) so no layer reads cached KV
+        kc = torch.randn((nb, BLOCK_SIZE, sh.num_kv_heads, 128), generator=gen, device=dev).to(torch.bfloat16)
+        vc = torch.randn((nb, BLOCK_SIZE, sh.num_kv_heads, 128), generator=gen, device=dev).to(torch.bfloat16)
+        pools.append((kc, vc))
+    q = torch.randn((B, 1, sh.num_q_heads, 128), generator=gen, device=dev).to(torch.bfloat16)
+    seq, btd = L.to(torch.int32).to(dev), bt.to(dev)
+    dec = S.KVHeadShardedDecode(sh)
+    o_fixed = torch.randn((B, 1, sh.num_q_heads, 128), generator=gen, device=dev).to(torch.bfloat16)
+
+    def attn(i):
+        kc, vc = pools[i % 4]
+        return pkg.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=seq, block_table=btd, causal=True)
+
+    def timed(fn):
+        for i in range(4):
+            fn(i)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fn(i)
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        return max_over_ranks(e0.elapsed_time(e1) * 1e3 / reps)
+
+    t_layer = timed(lambda i: dec.gather(attn(i)))
+    t_attn = timed(attn)
+    t_ag = timed(lambda i: dec.gather(o_fixed))
+    kv_total = int(L.sum()) * 8 * 128 * 2 * 2
+    pkg.check_device_errors(dev.index)
+    return {"requests": B, "kv_heads_per_gpu": sh.num_kv_heads, "us_per_layer": t_layer,
+            "decode_us": t_attn, "allgather_us": t_ag,
+            "allgather_bytes_per_gpu": B * sh.num_q_heads * 128 * 2,
+            "kv_gbs_total": kv_total / (t_layer * 1e-6) / 1e9,
+            "tok_per_s_attention_only": B / (t_layer * 28 * 1e-6)}
+
+
 def run_reference(args):
     rank = env_int("RANK", 0)
     if rank != 0:
@@ -343,6 +396,9 @@ def run_ours(args):
                      "us_per_launch": us_per_launch},
         "clocks": clk.summary(),
     }
+    if world > 1:
+        result["kv_head_sharded"] = kv_head_sharded_layer(pkg, dist, world, rank, dev, max(8, args.steps // 10),
+                                                          max_over_ranks)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r = cpu_reference_run(args.cpu_steps, 1, args.sample_layers)
         result["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}

@@ -212,3 +212,20 @@ def test_cuda_graph_capture_and_replay(pkg, cuda_dev):
         ref = opa.paged_decode(w1.q, w1.k_cache, w1.v_cache, w.block_table, w.cache_seqlens)
         assert (out.cpu().float() - ref).abs().max().item() <= TOL
     del graph
+
+
+def test_matches_flash_attn_with_kvcache(pkg, cuda_dev):
+    """Against the reference's own decode kernel, flash_attn_with_kvcache
+    (flash-attn 2.8.3), called exactly as model.py:60-67 calls it."""
+    fa = pytest.importorskip("flash_attn")
+    W = _workloads()
+    for B, seed in ((8, 61), (128, 62)):
+        w = W.decode_batch(B, 512, 1024, num_blocks=512, seed=seed, device=cuda_dev)
+        kw = dict(cache_seqlens=w.cache_seqlens, block_table=w.block_table, causal=True, num_splits=1)
+        try:
+            ref = fa.flash_attn_with_kvcache(w.q, w.k_cache, w.v_cache, **kw)
+        except RuntimeError as e:  # e.g. no kernel image for this GPU in the wheel
+            pytest.skip(f"flash_attn_with_kvcache does not run here: {e}")
+        out = pkg.flash_attn_with_kvcache(w.q, w.k_cache, w.v_cache, **kw)
+        torch.cuda.synchronize()
+        assert (out.float() - ref.float()).abs().max().item() <= TOL

@@ -125,3 +125,19 @@ def test_max_seqlen_too_small_reported(pkg, cuda_dev):
     torch.cuda.synchronize()
     with pytest.raises(RuntimeError, match="longer"):
         pkg.check_device_errors(cuda_dev.index)
+
+
+def test_matches_flash_attn_varlen(pkg, cuda_dev):
+    """Against flash-attn 2.8.3's varlen kernel on the same packed prompts."""
+    fa = pytest.importorskip("flash_attn")
+    from lean_infer_b200 import workloads as W
+
+    w = W.prefill_batch(16, 512, 1024, seed=3, device=cuda_dev)
+    mx = int(w.lengths.max())
+    try:
+        ref = fa.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx, causal=True)
+    except RuntimeError as e:
+        pytest.skip(f"flash_attn_varlen_func does not run here: {e}")
+    out = pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx, causal=True)
+    torch.cuda.synchronize()
+    assert (out.float() - ref.float()).abs().max().item() <= TOL
