@@ -42,7 +42,7 @@ constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O [256,384)
 constexpr uint32_t kColO = 256;
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, false, false);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, false, true);
-constexpr size_t kSmemBytes = 6 * kTile + 1024 /*barriers*/ + 1024 /*align slack*/;
+constexpr size_t kSmemBytes = 7 * kTile + 1024 /*barriers*/ + 1024 /*align slack*/;
 
 struct Params {
   const int* cu;
@@ -71,44 +71,70 @@ __device__ __forceinline__ uint64_t desc_mnmajor(const uint8_t* tile, int ks) {
   return smem_desc_sw128(smem_u32(tile) + ks * 2048, kHalf, 1024);
 }
 
+// Work items are (sequence, kv head, query tile), enumerated heaviest query
+// tile first: item i -> qt = n_qt - 1 - i / (S * Hkv), (s, h) from i % (S * Hkv).
+// CTA c (persistent, one per SM) takes items c, c + G, c + 2G, ...; items whose
+// tile starts past the end of its sequence are skipped. Every role walks the
+// same item sequence, so no item descriptors are exchanged.
+struct Item {
+  int s, h, q0, seq0, L, n_kv;
+};
+
+__device__ __forceinline__ bool next_item(const Params& p, int& idx, Item& it) {
+  const int per_qt = p.num_seqs * p.hkv;
+  const int total = p.n_qt * per_qt;
+  for (idx += gridDim.x; idx < total; idx += gridDim.x) {
+    const int qt = p.n_qt - 1 - idx / per_qt;
+    const int bh = idx - (idx / per_qt) * per_qt;
+    it.s = bh / p.hkv;
+    it.h = bh - it.s * p.hkv;
+    it.seq0 = p.cu[it.s];
+    it.L = p.cu[it.s + 1] - it.seq0;
+    it.q0 = qt * p.tq;
+    if (it.q0 < it.L) {
+      const int kv_end = p.causal ? min(it.q0 + p.tq, it.L) : it.L;
+      it.n_kv = (kv_end + kKeys - 1) / kKeys;
+      return true;
+    }
+  }
+  return false;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + kTile;      // 2 stages
-  uint8_t* sV = smem + 3 * kTile;  // 2 stages
-  uint8_t* sP = smem + 5 * kTile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTile);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_empty = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
+  uint8_t* sQ = smem;              // 2 buffers (items k, k+1)
+  uint8_t* sK = smem + 2 * kTile;  // 2 stages
+  uint8_t* sV = smem + 4 * kTile;  // 2 stages
+  uint8_t* sP = smem + 6 * kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTile);
+  uint64_t* q_full = bars + 0;    // [2]
+  uint64_t* q_empty = bars + 2;   // [2]
+  uint64_t* kv_full = bars + 4;   // [2]
+  uint64_t* kv_empty = bars + 6;  // [2]
+  uint64_t* s_full = bars + 8;    // [2]
+  uint64_t* s_empty = bars + 10;  // [2]
+  uint64_t* p_full = bars + 12;
+  uint64_t* o_done = bars + 13;
+  uint64_t* o_empty = bars + 14;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int s = blockIdx.x / p.hkv;
-  const int h = blockIdx.x - s * p.hkv;
-  const int qt = p.n_qt - 1 - static_cast<int>(blockIdx.y);  // longest (most KV tiles) first
   const float NEG_INF = -__int_as_float(0x7f800000);
 
   grid_dependency_wait();
-  const int seq0 = p.cu[s];
-  const int L = p.cu[s + 1] - seq0;
-  if (blockIdx.y == 0 && threadIdx.x == 0 && L > p.n_qt * p.tq && p.err) atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
-  const int q0 = qt * p.tq;
-  if (q0 >= L) return;  // whole CTA, before any barrier or TMEM use
-  const int kv_end = p.causal ? min(q0 + p.tq, L) : L;
-  const int n_kv = (kv_end + kKeys - 1) / kKeys;
-
+  {  // a CTA without work leaves before touching barriers or TMEM
+    int idx = static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x);
+    Item it;
+    if (!next_item(p, idx, it)) return;
+  }
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
@@ -116,6 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(p_full, 128);
     mbar_init(o_done, 1);
+    mbar_init(o_empty, 128);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -133,167 +160,201 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(q_full, kTile);
-      for (int g = 0; g < p.group; ++g)
-        for (int half = 0; half < 2; ++half)
-          tma_load_3d(sQ + half * kHalf + g * p.tq * 128, &tm_q, q_full, half * 64, h * p.group + g, seq0 + q0);
-      int j = 0;
-      for (; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
-        for (int half = 0; half < 2; ++half) {
-          tma_load_3d(sK + st * kTile + half * kHalf, &tm_k, &kv_full[st], half * 64, h, seq0 + j * kKeys);
-          tma_load_3d(sV + st * kTile + half * kHalf, &tm_v, &kv_full[st], half * 64, h, seq0 + j * kKeys);
+      int idx = static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x);
+      Item it;
+      int k = 0, t = 0;  // items and KV tiles issued by this CTA
+      bool ok = true;
+      while (ok && next_item(p, idx, it)) {
+        if (it.q0 == (p.n_qt - 1) * p.tq && it.L > p.n_qt * p.tq && p.err) atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
+        const int qb = k & 1;
+        if (!mbar_wait(&q_empty[qb], ((k >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
+        mbar_arrive_expect_tx(&q_full[qb], kTile);
+        for (int g = 0; g < p.group; ++g)
+          for (int half = 0; half < 2; ++half)
+            tma_load_3d(sQ + qb * kTile + half * kHalf + g * p.tq * 128, &tm_q, &q_full[qb], half * 64,
+                        it.h * p.group + g, it.seq0 + it.q0);
+        for (int j = 0; j < it.n_kv; ++j, ++t) {
+          const int st = t & 1;
+          if (!mbar_wait(&kv_empty[st], ((t >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+          for (int half = 0; half < 2; ++half) {
+            tma_load_3d(sK + st * kTile + half * kHalf, &tm_k, &kv_full[st], half * 64, it.h, it.seq0 + j * kKeys);
+            tma_load_3d(sV + st * kTile + half * kHalf, &tm_v, &kv_full[st], half * 64, it.h, it.seq0 + j * kKeys);
+          }
         }
+        ++k;
       }
-      if (j < n_kv)  // early exit: let issued copies land (bounded)
-        for (int jj = (j > 2 ? j - 2 : 0); jj < j; ++jj) mbar_wait(&kv_full[jj & 1], (jj >> 1) & 1, nullptr, 0);
+      if (!ok)  // early exit: let the copies already issued land (bounded)
+        for (int u = (t > 2 ? t - 2 : 0); u < t; ++u) mbar_wait(&kv_full[u & 1], (u >> 1) & 1, nullptr, 0);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      bool ok = mbar_wait(q_full, 0, p.err, LA_DEVERR_WAIT_TIMEOUT);
-      for (int j = 0; ok && j <= n_kv; ++j) {
-        if (j < n_kv) {
-          const int st = j & 1;
-          ok = mbar_wait(&kv_full[st], (j >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT) &&
-               mbar_wait(&s_empty[st], ((j >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT);
+      int idx = static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x);
+      Item it;
+      int k = 0, t = 0;
+      bool ok = true;
+      auto pv = [&](int u, int ju, int kk) -> bool {  // O += P V for global tile u (item-local ju)
+        if (!mbar_wait(p_full, u & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)) return false;
+        if (ju == 0 && kk >= 1 && !mbar_wait(o_empty, (kk - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)) return false;
+        tc_fence_after();
+        const uint8_t* vt = sV + (u & 1) * kTile;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_f16_ss(tmem + kColO, desc_kmajor(sP, ks), desc_mnmajor(vt, ks), kIdescPV,
+                      (ju > 0 || ks > 0) ? 1u : 0u);
+        umma_commit(o_done);
+        umma_commit(&kv_empty[u & 1]);
+        return true;
+      };
+      while (ok && next_item(p, idx, it)) {
+        const int qb = k & 1;
+        if (!mbar_wait(&q_full[qb], (k >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
+        const uint8_t* qt = sQ + qb * kTile;
+        const int t0 = t;
+        for (int j = 0; j < it.n_kv; ++j, ++t) {
+          const int st = t & 1;
+          ok = mbar_wait(&kv_full[st], (t >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT) &&
+               mbar_wait(&s_empty[st], ((t >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT);
           if (!ok) break;
           tc_fence_after();
           const uint8_t* kt = sK + st * kTile;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            umma_f16_ss(tmem + st * kKeys, desc_kmajor(sQ, ks), desc_kmajor(kt, ks), kIdescQK, ks > 0 ? 1u : 0u);
+            umma_f16_ss(tmem + st * kKeys, desc_kmajor(qt, ks), desc_kmajor(kt, ks), kIdescQK, ks > 0 ? 1u : 0u);
           umma_commit(&s_full[st]);
+          if (j == it.n_kv - 1) umma_commit(&q_empty[qb]);  // this item's Q is no longer read
+          if (j >= 1 && !(ok = pv(t - 1, j - 1, k))) break;
         }
-        if (j >= 1) {
-          const int i = j - 1;
-          ok = mbar_wait(p_full, i & 1, p.err, LA_DEVERR_WAIT_TIMEOUT);
-          if (!ok) break;
-          tc_fence_after();
-          const uint8_t* vt = sV + (i & 1) * kTile;
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            umma_f16_ss(tmem + kColO, desc_kmajor(sP, ks), desc_mnmajor(vt, ks), kIdescPV,
-                        (i > 0 || ks > 0) ? 1u : 0u);
-          umma_commit(o_done);
-          umma_commit(&kv_empty[i & 1]);
-        }
+        if (!ok || !(ok = pv(t0 + it.n_kv - 1, it.n_kv - 1, k))) break;
+        ++k;
       }
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ softmax
+    // ------------------------------------------------------------ softmax + epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const int g = row / p.tq;
-    const int t = q0 + (row - g * p.tq);  // token index within the sequence
-    const int lim = p.causal ? min(t + 1, L) : L;  // keys [0, lim) are visible
     const float sl2 = p.scale_log2;
-    float m = NEG_INF, l = 0.f;
+    int idx = static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x);
+    Item it;
+    int k = 0, t = 0;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int sb = j & 1;
-      // tcgen05.ld is warp-collective: keep the decision to continue warp-uniform
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (j >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float sv[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(taddr + sb * kKeys + c * 32, sv[c]);
-      tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
-
-      const int nvis = lim - j * kKeys;  // visible columns of this tile
-      float mt = NEG_INF;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float x = (c * 32 + e < nvis) ? sv[c][e] * sl2 : NEG_INF;
-          sv[c][e] = x;
-          mt = fmaxf(mt, x);
-        }
-      const float m_new = (mt > m + 8.f) ? mt : m;
-      const float alpha = ex2(m - m_new);  // 0 on the first tile, 1 when m is kept
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float pe = ex2(sv[c][e] - m_new);
-          sv[c][e] = pe;
-          rs += pe;
-        }
-      l = l * alpha + rs;
-
-      if (j >= 1) {  // PV_{j-1} done: P buffer free, O stable
-        if (!__all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
+    while (ok && next_item(p, idx, it)) {
+      const int tok = it.q0 + (row - g * p.tq);  // token index within the sequence
+      const int lim = p.causal ? min(tok + 1, it.L) : it.L;  // keys [0, lim) are visible
+      float m = NEG_INF, l = 0.f;
+      for (int j = 0; j < it.n_kv; ++j, ++t) {
+        const int sb = t & 1;
+        // tcgen05.ld is warp-collective: keep the decision to continue warp-uniform
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (t >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, m_new != m)) {
+        float sv[4][32];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float o[32];
-            tmem_ld32(taddr + kColO + c * 32, o);
-            tc_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] *= alpha;
-            tmem_st32(taddr + kColO + c * 32, o);
-          }
-          tc_wait_st();
-        }
-      }
-      m = m_new;
-      // P row -> shared memory, bf16, K-major SW128 (keys 0-63 | 64-127).
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        const int c = ch >> 2, e0 = (ch & 3) * 8;
-        uint4 u;
-        u.x = pack_bf16x2(sv[c][e0 + 0], sv[c][e0 + 1]);
-        u.y = pack_bf16x2(sv[c][e0 + 2], sv[c][e0 + 3]);
-        u.z = pack_bf16x2(sv[c][e0 + 4], sv[c][e0 + 5]);
-        u.w = pack_bf16x2(sv[c][e0 + 6], sv[c][e0 + 7]);
-        const int half = ch >> 3, chunk = ch & 7;
-        *reinterpret_cast<uint4*>(sP + half * kHalf + swz128(row, chunk)) = u;
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    // ------------------------------------------------------------ epilogue
-    if (__all_sync(0xffffffffu, ok && mbar_wait(o_done, (n_kv - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const int qh = h * p.group + g;
-      __nv_bfloat16* orow = p.out + static_cast<long long>(seq0 + t) * p.out_ts + static_cast<long long>(qh) * p.out_hs;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float o[32];
-        tmem_ld32(taddr + kColO + c * 32, o);  // all lanes: tcgen05.ld is warp-collective
+        for (int c = 0; c < 4; ++c) tmem_ld32(taddr + sb * kKeys + c * 32, sv[c]);
         tc_wait_ld();
-        if (t < L) {
+        tc_fence_before();
+        mbar_arrive(&s_empty[sb]);
+
+        const int nvis = lim - j * kKeys;  // visible columns of this tile
+        float mt = NEG_INF;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float x = (c * 32 + e < nvis) ? sv[c][e] * sl2 : NEG_INF;
+            sv[c][e] = x;
+            mt = fmaxf(mt, x);
+          }
+        const float m_new = (mt > m + 8.f) ? mt : m;
+        const float alpha = ex2(m - m_new);  // 0 on the first tile, 1 when m is kept
+        float rs = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float pe = ex2(sv[c][e] - m_new);
+            sv[c][e] = pe;
+            rs += pe;
+          }
+        l = l * alpha + rs;
+        // The P buffer and O are free once PV of the previous tile is done; for
+        // an item's first tile this thread already waited for it (epilogue).
+        if (j >= 1) {
+          if (!__all_sync(0xffffffffu, mbar_wait(o_done, (t - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (__any_sync(0xffffffffu, m_new != m)) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              float o[32];
+              tmem_ld32(taddr + kColO + c * 32, o);
+              tc_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] *= alpha;
+              tmem_st32(taddr + kColO + c * 32, o);
+            }
+            tc_wait_st();
+          }
+        }
+        m = m_new;
+        // P row -> shared memory, bf16, K-major SW128 (keys 0-63 | 64-127).
+#pragma unroll
+        for (int ch = 0; ch < 16; ++ch) {
+          const int c = ch >> 2, e0 = (ch & 3) * 8;
+          uint4 u;
+          u.x = pack_bf16x2(sv[c][e0 + 0], sv[c][e0 + 1]);
+          u.y = pack_bf16x2(sv[c][e0 + 2], sv[c][e0 + 3]);
+          u.z = pack_bf16x2(sv[c][e0 + 4], sv[c][e0 + 5]);
+          u.w = pack_bf16x2(sv[c][e0 + 6], sv[c][e0 + 7]);
+          const int half = ch >> 3, chunk = ch & 7;
+          *reinterpret_cast<uint4*>(sP + half * kHalf + swz128(row, chunk)) = u;
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(p_full);
+      }
+      if (!ok) break;
+      // ---------------------------------------------------------- epilogue
+      if (!__all_sync(0xffffffffu, mbar_wait(o_done, (t - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) break;
+      tc_fence_after();
+      float o[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(taddr + kColO + c * 32, o[c]);
+      tc_wait_ld();
+      tc_fence_before();
+      mbar_arrive(o_empty);  // O may now be overwritten by the next item's first PV
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int qh = it.h * p.group + g;
+      if (tok < it.L) {
+        __nv_bfloat16* orow =
+            p.out + static_cast<long long>(it.seq0 + tok) * p.out_ts + static_cast<long long>(qh) * p.out_hs;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
             uint4 u;
-            u.x = pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv);
-            u.y = pack_bf16x2(o[q4 * 8 + 2] * inv, o[q4 * 8 + 3] * inv);
-            u.z = pack_bf16x2(o[q4 * 8 + 4] * inv, o[q4 * 8 + 5] * inv);
-            u.w = pack_bf16x2(o[q4 * 8 + 6] * inv, o[q4 * 8 + 7] * inv);
+            u.x = pack_bf16x2(o[c][q4 * 8 + 0] * inv, o[c][q4 * 8 + 1] * inv);
+            u.y = pack_bf16x2(o[c][q4 * 8 + 2] * inv, o[c][q4 * 8 + 3] * inv);
+            u.z = pack_bf16x2(o[c][q4 * 8 + 4] * inv, o[c][q4 * 8 + 5] * inv);
+            u.w = pack_bf16x2(o[c][q4 * 8 + 6] * inv, o[c][q4 * 8 + 7] * inv);
             *reinterpret_cast<uint4*>(orow + c * 32 + q4 * 8) = u;
           }
-        }
+        if (p.lse)
+          p.lse[static_cast<long long>(qh) * p.total + it.seq0 + tok] =
+              l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
       }
-      if (p.lse && t < L)
-        p.lse[static_cast<long long>(qh) * p.total + seq0 + t] =
-            l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
+      ++k;
     }
   }
   tc_fence_before();
@@ -370,7 +431,11 @@ extern "C" int la_prefill_varlen(const void* q, int64_t q_token_stride, int64_t 
   p.lse = softmax_lse;
   p.total = total_tokens;
   p.err = dev_error;
-  if (p.n_qt > 65535 || static_cast<long long>(num_seqs) * num_kv_heads > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
-  const dim3 grid(static_cast<unsigned>(num_seqs * num_kv_heads), static_cast<unsigned>(p.n_qt));
+  const long long items = static_cast<long long>(p.n_qt) * num_seqs * num_kv_heads;
+  if (items > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
+  const int device = current_device();
+  const int sms = device >= 0 ? num_sms(device) : 0;
+  if (sms <= 0) return LA_ERR_CUDA;
+  const dim3 grid(static_cast<unsigned>(items < sms ? items : sms));  // persistent: <= one CTA per SM
   return cuda_status(launch_pdl(prefill_kernel, grid, dim3(kThreads), kSmemBytes, stream, tq_map, tk_map, tv_map, p));
 }

@@ -62,6 +62,57 @@ class CpuQwen3Decode:
         self.v_pool = fill((num_blocks, block_size, kv_heads, head_dim), 1.0).roll(7, dims=0)
         self.last_times = (0.0, 0.0)
 
+    @classmethod
+    def from_weights(cls, w: dict, cfg: dict, num_blocks: int, block_size: int):
+        """Build the oracle model from explicit fp32 weights (the same values
+        a GPU model holds) instead of random ones. `w` holds embed [V, H],
+        norm [H] and per-layer lists wq, wk, wv, wo, qn, kn, wg, wu, wd, ln1,
+        ln2; the KV pools start at zero and are written by decode_step /
+        prefill. Every layer gets its own pool."""
+        m = cls.__new__(cls)
+        m.L, m.H, m.Hq, m.Hkv, m.D = cfg["layers"], cfg["hidden"], cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
+        m.eps, m.theta = cfg["eps"], cfg["theta"]
+        m.n_alloc = m.L
+        m.embed, m.norm = w["embed"], w["norm"]
+        m.layers = [dict((k, w[k][i]) for k in ("wq", "wk", "wv", "wo", "qn", "kn", "wg", "wu", "wd", "ln1", "ln2"))
+                    for i in range(m.L)]
+        shape = (m.L, num_blocks, block_size, m.Hkv, m.D)
+        m.k_pools, m.v_pools = torch.zeros(shape), torch.zeros(shape)
+        m.k_pool = m.v_pool = None
+        m.last_times = (0.0, 0.0)
+        return m
+
+    @torch.no_grad()
+    def forward(self, ids, pos, block_table, cache_seqlens):
+        """Reference forward (model.py:95-112) for B rows of q_len tokens
+        starting at pos: writes the per-layer pools, returns fp32 logits
+        [B, q_len, V]. Attention: causal SDPA over the fresh q/k/v when
+        cache_seqlens is None (prefill, model.py:56-57), else paged decode over
+        the pool (the flash_attn_with_kvcache contract, q_len = 1)."""
+        B, n = ids.shape
+        Hq, Hkv, D = self.Hq, self.Hkv, self.D
+        h = self.embed[ids]
+        cos, sin = opre.build_rope(pos, n, D, self.theta, torch.float32)
+        for i in range(self.L):
+            w = self.layers[i]
+            x = F.rms_norm(h, (self.H,), w["ln1"], self.eps)
+            q = F.rms_norm((x @ w["wq"].T).view(B, n, Hq, D), (D,), w["qn"], self.eps).transpose(1, 2)
+            k = F.rms_norm((x @ w["wk"].T).view(B, n, Hkv, D), (D,), w["kn"], self.eps).transpose(1, 2)
+            v = (x @ w["wv"].T).view(B, n, Hkv, D).transpose(1, 2)
+            q = opre.apply_rope(q, cos, sin)
+            k = opre.apply_rope(k, cos, sin)
+            opre.block_cache_write(self.k_pools[i], self.v_pools[i], block_table, pos, k, v)
+            if cache_seqlens is None:
+                o = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True).transpose(1, 2)
+            else:
+                o = opa.paged_decode(q.transpose(1, 2), self.k_pools[i], self.v_pools[i], block_table,
+                                     cache_seqlens)
+            h = h + o.reshape(B, n, Hq * D) @ w["wo"].T
+            x = F.rms_norm(h, (self.H,), w["ln2"], self.eps)
+            h = h + (F.silu(x @ w["wg"].T) * (x @ w["wu"].T)) @ w["wd"].T
+        h = F.rms_norm(h, (self.H,), self.norm, self.eps)
+        return h @ self.embed.T
+
     def full_step_seconds(self) -> float:
         """Time of the last step scaled to all num_layers layers."""
         t_layers, t_rest = self.last_times
