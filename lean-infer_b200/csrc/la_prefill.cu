@@ -264,27 +264,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(&s_empty[sb]);
 
+        // Row max of the raw scores with 8 independent partial maxima (short
+        // dependency chains: one warp per scheduler cannot hide a 128-long one).
         const int nvis = lim - j * kKeys;  // visible columns of this tile
-        float mt = NEG_INF;
+        float mx[8];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int a = 0; a < 8; ++a) mx[a] = NEG_INF;
+        if (__all_sync(0xffffffffu, nvis >= kKeys)) {  // whole tile visible: no mask
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float x = (c * 32 + e < nvis) ? sv[c][e] * sl2 : NEG_INF;
-            sv[c][e] = x;
-            mt = fmaxf(mt, x);
-          }
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[c][e]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float x = (c * 32 + e < nvis) ? sv[c][e] : NEG_INF;
+              sv[c][e] = x;
+              mx[e & 7] = fmaxf(mx[e & 7], x);
+            }
+        }
+        const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
         const float m_new = (mt > m + 8.f) ? mt : m;
         const float alpha = ex2(m - m_new);  // 0 on the first tile, 1 when m is kept
-        float rs = 0.f;
+        const float neg_m = -m_new;
+        float ps[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) ps[a] = 0.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float pe = ex2(sv[c][e] - m_new);
+            const float pe = ex2(fmaf(sv[c][e], sl2, neg_m));  // masked: -inf -> 0
             sv[c][e] = pe;
-            rs += pe;
+            ps[e & 7] += pe;
           }
+        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         l = l * alpha + rs;
         // The P buffer and O are free once PV of the previous tile is done; for
         // an item's first tile this thread already waited for it (epilogue).

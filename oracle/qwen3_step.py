@@ -92,7 +92,7 @@ class CpuQwen3Decode:
         B, n = ids.shape
         Hq, Hkv, D = self.Hq, self.Hkv, self.D
         h = self.embed[ids]
-        cos, sin = opre.build_rope(pos, n, D, self.theta, torch.float32)
+        cos, sin = opre.build_rope(pos, n, D, self.theta, h.dtype)  # model.py:98
         for i in range(self.L):
             w = self.layers[i]
             x = F.rms_norm(h, (self.H,), w["ln1"], self.eps)

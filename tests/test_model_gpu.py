@@ -2,11 +2,22 @@
 pre-attention, varlen prefill, paged decode in the CUDA-graph DecodeGraph)
 against the CPU fp32 restatement of the reference model
 (leaninfer/qwen3/model.py) holding the same weights. A small depth and vocab
-keep the oracle fast; the shapes per layer are Qwen3-0.6B's."""
+keep the oracle fast; the shapes per layer are Qwen3-0.6B's.
+
+Tolerance: the model computes in bf16, the oracle in fp32. Run on the CPU,
+the reference's own model differs between fp32 and bf16 by ~0.5 % relative L2
+on these logits (max |diff| ~4 on logits up to ~1000, argmax identical), so
+the bound is relative L2 <= 2 % and >= 90 % argmax agreement."""
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
+
+
+def _close(got, want):
+    rel = ((got - want).norm() / want.norm()).item()
+    agree = (got.argmax(-1) == want.argmax(-1)).float().mean().item()
+    return rel, agree
 
 
 def _weights(model):
@@ -66,14 +77,15 @@ def test_prefill_then_graph_decode_matches_reference_model(pkg, cuda_dev):
     for i, L in enumerate(lens):
         lr = ref.forward(prompts[i].view(1, L), pos0[i:i + 1], bt[i:i + 1], None)[0]
         lg = logits[int(cu[i]):int(cu[i + 1])].float().cpu()
-        assert (lg - lr).abs().max().item() < 0.25, i  # bf16 model vs fp32 oracle, |logit| ~ 10
-        assert (lg.argmax(-1) == lr.argmax(-1)).float().mean().item() > 0.9
+        rel, agree = _close(lg, lr)
+        assert rel <= 0.02 and agree >= 0.9, (i, rel, agree)
     # K/V written by prefill
     for layer in range(cfg.num_hidden_layers):
         for i, L in enumerate(lens):
             blk = bt[i, 0].item()
             n = min(L, BS)
-            assert (cache.k[layer, blk, :n].float().cpu() - ref.k_pools[layer, blk, :n]).abs().max().item() < 0.1
+            got, want = cache.k[layer, blk, :n].float().cpu(), ref.k_pools[layer, blk, :n]
+            assert ((got - want).norm() / want.norm()).item() <= 0.02
 
     # 4 decode steps through the captured DecodeGraph
     dg = qwen3.DecodeGraph(model, cache, len(lens), max_blocks)
@@ -84,7 +96,8 @@ def test_prefill_then_graph_decode_matches_reference_model(pkg, cuda_dev):
         toks = dg.step()
         lr = ref.forward(nxt.view(-1, 1), pos, bt, (pos + 1).to(torch.int32))[:, 0]
         lg = dg.logits[:, 0].float().cpu()
-        assert (lg - lr).abs().max().item() < 0.25
+        rel, _ = _close(lg, lr)
+        assert rel <= 0.02, rel
         assert (torch.tensor(toks) == lr.argmax(-1)).float().mean().item() >= 2 / 3
         nxt = lr.argmax(-1)  # follow the oracle's tokens so both stay on the same path
         pos = pos + 1
