@@ -53,6 +53,7 @@ typedef enum {
 #define LA_DEVERR_BLOCK_ID 2       /* block_table entry outside [0, num_blocks) */
 #define LA_DEVERR_SEQLEN 3         /* a sequence needs more blocks than max_blocks_per_seq */
 #define LA_DEVERR_ROPE_POS 4       /* a position is outside the rope table */
+#define LA_DEVERR_SMEM_ALIGN 5     /* dynamic shared memory base not 1024-byte aligned (kernel returned) */
 
 int la_version(void);
 const char* la_status_string(int status);

@@ -19,6 +19,7 @@ DEVERR_NAMES = {
     2: "block id outside the pool",
     3: "sequence longer than its block table",
     4: "position outside the rope table",
+    5: "shared memory base misaligned",
 }
 
 

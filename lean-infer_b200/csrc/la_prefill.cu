@@ -10,14 +10,21 @@
 //
 // CTA tile: 128 query rows = the tq = 128/G consecutive tokens of the G query
 // heads that share one kv head (GQA packing: every K/V tile feeds all G
-// heads), against KV tiles of 128 keys. Per KV tile j:
-//   S_j  = Q K_j^T        tcgen05.mma M128 N128 K16 x8, fp32 in TMEM (2 buffers)
+// heads), against KV tiles of 64 keys. Per KV tile j:
+//   S_j  = Q K_j^T        tcgen05.mma M128 N64 K16 x8, fp32 in TMEM (2 buffers)
 //   P_j  = exp2(S_j*scale*log2e - m)  by 4 softmax warps, one thread per row,
 //          written to shared memory as bf16 in the MMA's K-major layout
-//   O   += P_j V_j        tcgen05.mma with V read MN-major, fp32 in TMEM
+//   O   += P_j V_j        tcgen05.mma M128 N128 K16 x4 with V read MN-major,
+//                         fp32 in TMEM
 // The row max is only raised (and O, l rescaled) when a tile's max exceeds the
 // running one by more than 8 (log2 units), so P stays <= 256 and most tiles
 // skip the O rescale. S_{j+1} is issued while softmax works on S_j.
+//
+// Persistent CTAs walk a heaviest-first list of (sequence, kv head, query
+// tile) items. A CTA needs 112 KB of shared memory, 256 TMEM columns and
+// <= 170 registers per thread, so two CTAs share each SM: while one CTA's
+// softmax warps work, the other's MMAs run, and each scheduler has two
+// softmax warps to switch between.
 //
 // Warps: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 = softmax and
 // epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows of that quarter).
@@ -33,16 +40,24 @@ namespace la {
 namespace prefill {
 
 constexpr int kD = 128;
-constexpr int kRows = 128;          // query rows per CTA
-constexpr int kKeys = 128;          // keys per KV tile
-constexpr int kHalf = kRows * 128;  // one 64-wide half of a 128-row tile: 16 KB (SW128 rows)
-constexpr int kTile = 2 * kHalf;    // 32 KB
+constexpr int kRows = 128;            // query rows per CTA
+constexpr int kKeys = 64;             // keys per KV tile
+constexpr int kQHalf = kRows * 128;   // one 64-dim half of the Q tile: 128 rows x 128 B = 16 KB
+constexpr int kQTile = 2 * kQHalf;    // 32 KB
+constexpr int kKVHalf = kKeys * 128;  // one 64-dim half of a K or V tile: 8 KB
+constexpr int kKVTile = 2 * kKVHalf;  // 16 KB
+constexpr int kPTile = kRows * 128;   // P: 128 rows x 64 keys bf16 = 16 KB
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 512;  // S0 [0,128) S1 [128,256) O [256,384)
-constexpr uint32_t kColO = 256;
-constexpr uint32_t kIdescQK = idesc_bf16_f32(128, 128, false, false);
+constexpr uint32_t kTmemCols = 256;  // S0 [0,64) S1 [64,128) O [128,256)
+constexpr uint32_t kColO = 128;
+constexpr uint32_t kIdescQK = idesc_bf16_f32(128, kKeys, false, false);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, false, true);
-constexpr size_t kSmemBytes = 7 * kTile + 1024 /*barriers*/ + 1024 /*align slack*/;
+// Q | K x2 | V x2 | P | barriers. Two CTAs must fit in an SM's 228 KB, so no
+// alignment slack is requested: the kernel checks that the dynamic shared
+// memory base is 1024-byte aligned (the 128-byte swizzle atom) and reports
+// LA_DEVERR_SMEM_ALIGN otherwise.
+constexpr int kBarOffset = kQTile + 4 * kKVTile + kPTile;  // 112 KB
+constexpr size_t kSmemBytes = kBarOffset + 256;
 
 struct Params {
   const int* cu;
@@ -59,16 +74,17 @@ struct Params {
   int* err;
 };
 
-// K-major operand (rows of 128 bytes, SW128): k-step ks covers elements
-// 16ks..16ks+15 of the 128-wide reduction dimension, split into two halves.
-__device__ __forceinline__ uint64_t desc_kmajor(const uint8_t* tile, int ks) {
-  return smem_desc_sw128(smem_u32(tile) + (ks >> 2) * kHalf + (ks & 3) * 32, 16, 1024);
+// K-major operand of 128-byte SW128 rows whose 128-wide reduction dimension is
+// split into two 64-wide halves `half_bytes` apart: k-step ks covers elements
+// 16ks..16ks+15.
+__device__ __forceinline__ uint64_t desc_kmajor(const uint8_t* tile, int half_bytes, int ks) {
+  return smem_desc_sw128(smem_u32(tile) + (ks >> 2) * half_bytes + (ks & 3) * 32, 16, 1024);
 }
-// MN-major operand (V: rows = keys, 128 B = 64 dims per half): k-step ks
-// covers keys 16ks..16ks+15 = two 8-row groups (SBO 1024 B); the second
-// 64-dim half is LBO = 16 KB away.
-__device__ __forceinline__ uint64_t desc_mnmajor(const uint8_t* tile, int ks) {
-  return smem_desc_sw128(smem_u32(tile) + ks * 2048, kHalf, 1024);
+// MN-major V tile (rows = keys, 128 B = 64 dims per half): k-step ks covers
+// keys 16ks..16ks+15 = two 8-row groups (SBO 1024 B); the second 64-dim half
+// is LBO = kKVHalf away.
+__device__ __forceinline__ uint64_t desc_v(const uint8_t* tile, int ks) {
+  return smem_desc_sw128(smem_u32(tile) + ks * 2048, kKVHalf, 1024);
 }
 
 // Work items are (sequence, kv head, query tile), enumerated heaviest query
@@ -100,25 +116,24 @@ __device__ __forceinline__ bool next_item(const Params& p, int& idx, Item& it) {
   return false;
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;              // 2 buffers (items k, k+1)
-  uint8_t* sK = smem + 2 * kTile;  // 2 stages
-  uint8_t* sV = smem + 4 * kTile;  // 2 stages
-  uint8_t* sP = smem + 6 * kTile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 7 * kTile);
-  uint64_t* q_full = bars + 0;    // [2]
-  uint64_t* q_empty = bars + 2;   // [2]
-  uint64_t* kv_full = bars + 4;   // [2]
-  uint64_t* kv_empty = bars + 6;  // [2]
-  uint64_t* s_full = bars + 8;    // [2]
-  uint64_t* s_empty = bars + 10;  // [2]
-  uint64_t* p_full = bars + 12;
-  uint64_t* o_done = bars + 13;
-  uint64_t* o_empty = bars + 14;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* sQ = smem;
+  uint8_t* sK = smem + kQTile;                // 2 stages
+  uint8_t* sV = smem + kQTile + 2 * kKVTile;  // 2 stages
+  uint8_t* sP = smem + kQTile + 4 * kKVTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOffset);
+  uint64_t* q_full = bars + 0;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;   // [2]
+  uint64_t* kv_empty = bars + 4;  // [2]
+  uint64_t* s_full = bars + 6;    // [2]
+  uint64_t* s_empty = bars + 8;   // [2]
+  uint64_t* p_full = bars + 10;
+  uint64_t* o_done = bars + 11;
+  uint64_t* o_empty = bars + 12;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int warp = threadIdx.x >> 5;
@@ -131,10 +146,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     Item it;
     if (!next_item(p, idx, it)) return;
   }
+  if (smem_u32(smem) & 1023u) {  // the swizzled tiles need a 1024-byte aligned base
+    if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, LA_DEVERR_SMEM_ALIGN);
+    return;
+  }
   if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&q_empty[i], 1);
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
@@ -166,23 +185,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       while (ok && next_item(p, idx, it)) {
         if (it.q0 == (p.n_qt - 1) * p.tq && it.L > p.n_qt * p.tq && p.err) atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
-        const int qb = k & 1;
-        if (!mbar_wait(&q_empty[qb], ((k >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
-        mbar_arrive_expect_tx(&q_full[qb], kTile);
+        // Q of item k replaces item k-1's once its last S MMA has completed.
+        if (!mbar_wait(q_empty, (k & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
+        mbar_arrive_expect_tx(q_full, kQTile);
         for (int g = 0; g < p.group; ++g)
           for (int half = 0; half < 2; ++half)
-            tma_load_3d(sQ + qb * kTile + half * kHalf + g * p.tq * 128, &tm_q, &q_full[qb], half * 64,
-                        it.h * p.group + g, it.seq0 + it.q0);
+            tma_load_3d(sQ + half * kQHalf + g * p.tq * 128, &tm_q, q_full, half * 64, it.h * p.group + g,
+                        it.seq0 + it.q0);
         for (int j = 0; j < it.n_kv; ++j, ++t) {
           const int st = t & 1;
           if (!mbar_wait(&kv_empty[st], ((t >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+          mbar_arrive_expect_tx(&kv_full[st], 2 * kKVTile);
           for (int half = 0; half < 2; ++half) {
-            tma_load_3d(sK + st * kTile + half * kHalf, &tm_k, &kv_full[st], half * 64, it.h, it.seq0 + j * kKeys);
-            tma_load_3d(sV + st * kTile + half * kHalf, &tm_v, &kv_full[st], half * 64, it.h, it.seq0 + j * kKeys);
+            tma_load_3d(sK + st * kKVTile + half * kKVHalf, &tm_k, &kv_full[st], half * 64, it.h,
+                        it.seq0 + j * kKeys);
+            tma_load_3d(sV + st * kKVTile + half * kKVHalf, &tm_v, &kv_full[st], half * 64, it.h,
+                        it.seq0 + j * kKeys);
           }
         }
         ++k;
@@ -201,19 +222,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(p_full, u & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)) return false;
         if (ju == 0 && kk >= 1 && !mbar_wait(o_empty, (kk - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)) return false;
         tc_fence_after();
-        const uint8_t* vt = sV + (u & 1) * kTile;
+        const uint8_t* vt = sV + (u & 1) * kKVTile;
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_f16_ss(tmem + kColO, desc_kmajor(sP, ks), desc_mnmajor(vt, ks), kIdescPV,
+        for (int ks = 0; ks < kKeys / 16; ++ks)
+          umma_f16_ss(tmem + kColO, desc_kmajor(sP, kPTile, ks), desc_v(vt, ks), kIdescPV,
                       (ju > 0 || ks > 0) ? 1u : 0u);
         umma_commit(o_done);
         umma_commit(&kv_empty[u & 1]);
         return true;
       };
       while (ok && next_item(p, idx, it)) {
-        const int qb = k & 1;
-        if (!mbar_wait(&q_full[qb], (k >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
-        const uint8_t* qt = sQ + qb * kTile;
+        if (!mbar_wait(q_full, k & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
         const int t0 = t;
         for (int j = 0; j < it.n_kv; ++j, ++t) {
           const int st = t & 1;
@@ -221,12 +240,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                mbar_wait(&s_empty[st], ((t >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT);
           if (!ok) break;
           tc_fence_after();
-          const uint8_t* kt = sK + st * kTile;
+          const uint8_t* kt = sK + st * kKVTile;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            umma_f16_ss(tmem + st * kKeys, desc_kmajor(qt, ks), desc_kmajor(kt, ks), kIdescQK, ks > 0 ? 1u : 0u);
+            umma_f16_ss(tmem + st * kKeys, desc_kmajor(sQ, kQHalf, ks), desc_kmajor(kt, kKVHalf, ks), kIdescQK,
+                        ks > 0 ? 1u : 0u);
           umma_commit(&s_full[st]);
-          if (j == it.n_kv - 1) umma_commit(&q_empty[qb]);  // this item's Q is no longer read
+          if (j == it.n_kv - 1) umma_commit(q_empty);  // this item's Q is no longer read
           if (j >= 1 && !(ok = pv(t - 1, j - 1, k))) break;
         }
         if (!ok || !(ok = pv(t0 + it.n_kv - 1, it.n_kv - 1, k))) break;
@@ -257,9 +277,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        float sv[4][32];
+        constexpr int kC = kKeys / 32;  // 32-column TMEM loads per row
+        float sv[kC][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(taddr + sb * kKeys + c * 32, sv[c]);
+        for (int c = 0; c < kC; ++c) tmem_ld32(taddr + sb * kKeys + c * 32, sv[c]);
         tc_wait_ld();
         tc_fence_before();
         mbar_arrive(&s_empty[sb]);
@@ -272,12 +293,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int a = 0; a < 8; ++a) mx[a] = NEG_INF;
         if (__all_sync(0xffffffffu, nvis >= kKeys)) {  // whole tile visible: no mask
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < kC; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[c][e]);
         } else {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
+          for (int c = 0; c < kC; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               const float x = (c * 32 + e < nvis) ? sv[c][e] : NEG_INF;
@@ -294,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int a = 0; a < 8; ++a) ps[a] = 0.f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < kC; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const float pe = ex2(fmaf(sv[c][e], sl2, neg_m));  // masked: -inf -> 0
@@ -325,17 +346,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         m = m_new;
-        // P row -> shared memory, bf16, K-major SW128 (keys 0-63 | 64-127).
+        // P row -> shared memory, bf16, K-major SW128 (one 128-byte row of 64 keys).
 #pragma unroll
-        for (int ch = 0; ch < 16; ++ch) {
+        for (int ch = 0; ch < kKeys / 8; ++ch) {
           const int c = ch >> 2, e0 = (ch & 3) * 8;
           uint4 u;
           u.x = pack_bf16x2(sv[c][e0 + 0], sv[c][e0 + 1]);
           u.y = pack_bf16x2(sv[c][e0 + 2], sv[c][e0 + 3]);
           u.z = pack_bf16x2(sv[c][e0 + 4], sv[c][e0 + 5]);
           u.w = pack_bf16x2(sv[c][e0 + 6], sv[c][e0 + 7]);
-          const int half = ch >> 3, chunk = ch & 7;
-          *reinterpret_cast<uint4*>(sP + half * kHalf + swz128(row, chunk)) = u;
+          *reinterpret_cast<uint4*>(sP + swz128(row, ch)) = u;
         }
         fence_proxy_async_smem();
         tc_fence_before();
@@ -426,7 +446,7 @@ extern "C" int la_prefill_varlen(const void* q, int64_t q_token_stride, int64_t 
   }
   {
     const uint64_t dims[3] = {128, static_cast<uint64_t>(num_kv_heads), static_cast<uint64_t>(total_tokens)};
-    const uint32_t box[3] = {64, 1, kKeys};
+    const uint32_t box[3] = {64, 1, static_cast<uint32_t>(kKeys)};
     const uint64_t ks[2] = {static_cast<uint64_t>(k_head_stride) * 2, static_cast<uint64_t>(k_token_stride) * 2};
     const uint64_t vs[2] = {static_cast<uint64_t>(v_head_stride) * 2, static_cast<uint64_t>(v_token_stride) * 2};
     if ((stt = encode_tensor_map_bf16(&tk_map, k, 3, dims, ks, box, true)) != LA_OK) return stt;
@@ -453,6 +473,11 @@ extern "C" int la_prefill_varlen(const void* q, int64_t q_token_stride, int64_t 
   const int device = current_device();
   const int sms = device >= 0 ? num_sms(device) : 0;
   if (sms <= 0) return LA_ERR_CUDA;
-  const dim3 grid(static_cast<unsigned>(items < sms ? items : sms));  // persistent: <= one CTA per SM
+  int per_sm = 0;
+  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prefill_kernel, kThreads, kSmemBytes);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (per_sm < 1) per_sm = 1;
+  const long long ctas = static_cast<long long>(sms) * per_sm;
+  const dim3 grid(static_cast<unsigned>(items < ctas ? items : ctas));  // persistent
   return cuda_status(launch_pdl(prefill_kernel, grid, dim3(kThreads), kSmemBytes, stream, tq_map, tk_map, tv_map, p));
 }
