@@ -406,8 +406,12 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 int prefill_init(int device) {
   (void)device;
-  return cuda_status(cudaFuncSetAttribute(prefill::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(prefill::kSmemBytes)));
+  cudaError_t e = cudaFuncSetAttribute(prefill::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(prefill::kSmemBytes));
+  // all of the unified L1/shared storage as shared memory, so two CTAs fit
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(prefill::prefill_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  return cuda_status(e);
 }
 
 }  // namespace la
@@ -473,11 +477,9 @@ extern "C" int la_prefill_varlen(const void* q, int64_t q_token_stride, int64_t 
   const int device = current_device();
   const int sms = device >= 0 ? num_sms(device) : 0;
   if (sms <= 0) return LA_ERR_CUDA;
-  int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, prefill_kernel, kThreads, kSmemBytes);
-  if (e != cudaSuccess) return cuda_status(e);
-  if (per_sm < 1) per_sm = 1;
-  const long long ctas = static_cast<long long>(sms) * per_sm;
+  // Two CTAs per SM by design (registers, shared memory and TMEM are sized
+  // for it); if fewer fit, the extra CTAs simply run as a second wave.
+  const long long ctas = static_cast<long long>(sms) * 2;
   const dim3 grid(static_cast<unsigned>(items < ctas ? items : ctas));  // persistent
   return cuda_status(launch_pdl(prefill_kernel, grid, dim3(kThreads), kSmemBytes, stream, tq_map, tk_map, tv_map, p));
 }
