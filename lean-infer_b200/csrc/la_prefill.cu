@@ -87,33 +87,81 @@ __device__ __forceinline__ uint64_t desc_v(const uint8_t* tile, int ks) {
   return smem_desc_sw128(smem_u32(tile) + ks * 2048, kKVHalf, 1024);
 }
 
-// Work items are (sequence, kv head, query tile), enumerated heaviest query
-// tile first: item i -> qt = n_qt - 1 - i / (S * Hkv), (s, h) from i % (S * Hkv).
-// CTA c (persistent, one per SM) takes items c, c + G, c + 2G, ...; items whose
-// tile starts past the end of its sequence are skipped. Every role walks the
-// same item sequence, so no item descriptors are exchanged.
+// Work items are (sequence, kv head, query tile) in descending cost: query-
+// tile level qt from the top down (a tile's KV length grows with qt), at each
+// level only the sequences long enough to have that tile, then the kv heads.
+// The valid items are ranked in that order and dealt to the G persistent CTAs
+// as a snake over 2G columns (CTA c takes ranks c, 2G-1-c, 2G+c, 4G-1-c, ...),
+// which evens out the summed cost per CTA. Every warp walks its CTA's item
+// list itself (the walk is warp-collective), so no item descriptors are
+// exchanged between roles.
 struct Item {
   int s, h, q0, seq0, L, n_kv;
 };
 
-__device__ __forceinline__ bool next_item(const Params& p, int& idx, Item& it) {
-  const int per_qt = p.num_seqs * p.hkv;
-  const int total = p.n_qt * per_qt;
-  for (idx += gridDim.x; idx < total; idx += gridDim.x) {
-    const int qt = p.n_qt - 1 - idx / per_qt;
-    const int bh = idx - (idx / per_qt) * per_qt;
-    it.s = bh / p.hkv;
-    it.h = bh - it.s * p.hkv;
-    it.seq0 = p.cu[it.s];
-    it.L = p.cu[it.s + 1] - it.seq0;
-    it.q0 = qt * p.tq;
-    if (it.q0 < it.L) {
-      const int kv_end = p.causal ? min(it.q0 + p.tq, it.L) : it.L;
-      it.n_kv = (kv_end + kKeys - 1) / kKeys;
-      return true;
-    }
+struct Walker {
+  int taken;       // items this CTA has taken so far
+  int level;       // current query-tile level
+  long long base;  // rank of the first item of `level`
+  int count;       // items at `level`
+};
+
+__device__ __forceinline__ bool seq_has_tile(const Params& p, int s, int q0) {
+  return s < p.num_seqs && (p.cu[s + 1] - p.cu[s]) > q0;
+}
+
+// Items at one level (warp-collective).
+__device__ int level_count(const Params& p, int level) {
+  const int lane = threadIdx.x & 31;
+  const int q0 = level * p.tq;
+  int n = 0;
+  for (int b = 0; b < p.num_seqs; b += 32) n += __popc(__ballot_sync(0xffffffffu, seq_has_tile(p, b + lane, q0)));
+  return n * p.hkv;
+}
+
+__device__ void walker_init(const Params& p, Walker& w) {
+  w.taken = 0;
+  w.level = p.n_qt - 1;
+  w.base = 0;
+  w.count = level_count(p, w.level);
+}
+
+// Next item of this CTA (warp-collective; identical result in every lane).
+__device__ bool walker_next(const Params& p, Walker& w, Item& it) {
+  const int lane = threadIdx.x & 31;
+  const long long g2 = 2LL * gridDim.x;
+  const long long r = static_cast<long long>(w.taken >> 1) * g2 +
+                      ((w.taken & 1) ? (g2 - 1 - blockIdx.x) : static_cast<long long>(blockIdx.x));
+  while (r >= w.base + w.count) {
+    if (w.level == 0) return false;
+    w.base += w.count;
+    --w.level;
+    w.count = level_count(p, w.level);
   }
-  return false;
+  const int idx = static_cast<int>(r - w.base);
+  const int ord = idx / p.hkv;  // the ord-th sequence (index order) that has this level's tile
+  const int q0 = w.level * p.tq;
+  int seen = 0, s = 0;
+  for (int b = 0; b < p.num_seqs; b += 32) {
+    const unsigned m = __ballot_sync(0xffffffffu, seq_has_tile(p, b + lane, q0));
+    const int c = __popc(m);
+    if (ord < seen + c) {
+      unsigned mm = m;
+      for (int k = seen; k < ord; ++k) mm &= mm - 1;  // drop the lower set bits
+      s = b + __ffs(mm) - 1;
+      break;
+    }
+    seen += c;
+  }
+  it.s = s;
+  it.h = idx - ord * p.hkv;
+  it.seq0 = p.cu[s];
+  it.L = p.cu[s + 1] - it.seq0;
+  it.q0 = q0;
+  const int kv_end = p.causal ? min(q0 + p.tq, it.L) : it.L;
+  it.n_kv = (kv_end + kKeys - 1) / kKeys;
+  ++w.taken;
+  return true;
 }
 
 __global__ void __launch_bounds__(kThreads, 2)
@@ -142,9 +190,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   grid_dependency_wait();
   {  // a CTA without work leaves before touching barriers or TMEM
-    int idx = static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x);
+    Walker w;
+    walker_init(p, w);
     Item it;
-    if (!next_item(p, idx, it)) return;
+    if (!walker_next(p, w, it)) return;
   }
   if (smem_u32(smem) & 1023u) {  // the swizzled tiles need a 1024-byte aligned base
     if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, LA_DEVERR_SMEM_ALIGN);
@@ -174,30 +223,37 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ producer (lane 0 issues)
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      int idx = static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x);
-      Item it;
-      int k = 0, t = 0;  // items and KV tiles issued by this CTA
-      bool ok = true;
-      while (ok && next_item(p, idx, it)) {
-        if (it.q0 == (p.n_qt - 1) * p.tq && it.L > p.n_qt * p.tq && p.err) atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
-        // Q of item k replaces item k-1's once its last S MMA has completed.
-        if (!mbar_wait(q_empty, (k & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
+    }
+    Walker w;
+    walker_init(p, w);
+    Item it;
+    int k = 0, t = 0;  // items and KV tiles issued by this CTA
+    bool ok = true;
+    while (ok && walker_next(p, w, it)) {
+      if (lane == 0 && it.q0 == (p.n_qt - 1) * p.tq && it.L > p.n_qt * p.tq && p.err)
+        atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
+      // Q of item k replaces item k-1's once its last S MMA has completed.
+      if (!__all_sync(0xffffffffu, mbar_wait(q_empty, (k & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT))) break;
+      if (lane == 0) {
         mbar_arrive_expect_tx(q_full, kQTile);
         for (int g = 0; g < p.group; ++g)
           for (int half = 0; half < 2; ++half)
             tma_load_3d(sQ + half * kQHalf + g * p.tq * 128, &tm_q, q_full, half * 64, it.h * p.group + g,
                         it.seq0 + it.q0);
-        for (int j = 0; j < it.n_kv; ++j, ++t) {
-          const int st = t & 1;
-          if (!mbar_wait(&kv_empty[st], ((t >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) {
-            ok = false;
-            break;
-          }
+      }
+      for (int j = 0; j < it.n_kv; ++j, ++t) {
+        const int st = t & 1;
+        if (!__all_sync(0xffffffffu,
+                        mbar_wait(&kv_empty[st], ((t >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
           mbar_arrive_expect_tx(&kv_full[st], 2 * kKVTile);
           for (int half = 0; half < 2; ++half) {
             tma_load_3d(sK + st * kKVTile + half * kKVHalf, &tm_k, &kv_full[st], half * 64, it.h,
@@ -206,22 +262,27 @@ __global__ void __launch_bounds__(kThreads, 2)
                         it.seq0 + j * kKeys);
           }
         }
-        ++k;
       }
-      if (!ok)  // early exit: let the copies already issued land (bounded)
-        for (int u = (t > 2 ? t - 2 : 0); u < t; ++u) mbar_wait(&kv_full[u & 1], (u >> 1) & 1, nullptr, 0);
+      ++k;
     }
+    if (!ok && lane == 0)  // early exit: let the copies already issued land (bounded)
+      for (int u = (t > 2 ? t - 2 : 0); u < t; ++u) mbar_wait(&kv_full[u & 1], (u >> 1) & 1, nullptr, 0);
+    __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      int idx = static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x);
-      Item it;
-      int k = 0, t = 0;
-      bool ok = true;
-      auto pv = [&](int u, int ju, int kk) -> bool {  // O += P V for global tile u (item-local ju)
-        if (!mbar_wait(p_full, u & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)) return false;
-        if (ju == 0 && kk >= 1 && !mbar_wait(o_empty, (kk - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)) return false;
-        tc_fence_after();
+    // ------------------------------------------------------------ MMA issuer (lane 0 issues)
+    Walker w;
+    walker_init(p, w);
+    Item it;
+    int k = 0, t = 0;
+    bool ok = true;
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
+    };
+    auto pv = [&](int u, int ju, int kk) -> bool {  // O += P V for global tile u (item-local ju)
+      if (!wait_all(p_full, u & 1)) return false;
+      if (ju == 0 && kk >= 1 && !wait_all(o_empty, (kk - 1) & 1)) return false;
+      tc_fence_after();
+      if (lane == 0) {
         const uint8_t* vt = sV + (u & 1) * kKVTile;
 #pragma unroll
         for (int ks = 0; ks < kKeys / 16; ++ks)
@@ -229,17 +290,19 @@ __global__ void __launch_bounds__(kThreads, 2)
                       (ju > 0 || ks > 0) ? 1u : 0u);
         umma_commit(o_done);
         umma_commit(&kv_empty[u & 1]);
-        return true;
-      };
-      while (ok && next_item(p, idx, it)) {
-        if (!mbar_wait(q_full, k & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
-        const int t0 = t;
-        for (int j = 0; j < it.n_kv; ++j, ++t) {
-          const int st = t & 1;
-          ok = mbar_wait(&kv_full[st], (t >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT) &&
-               mbar_wait(&s_empty[st], ((t >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT);
-          if (!ok) break;
-          tc_fence_after();
+      }
+      __syncwarp();
+      return true;
+    };
+    while (ok && walker_next(p, w, it)) {
+      if (!wait_all(q_full, k & 1)) break;
+      const int t0 = t;
+      for (int j = 0; j < it.n_kv; ++j, ++t) {
+        const int st = t & 1;
+        ok = wait_all(&kv_full[st], (t >> 1) & 1) && wait_all(&s_empty[st], ((t >> 1) & 1) ^ 1u);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
           const uint8_t* kt = sK + st * kKVTile;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
@@ -247,11 +310,12 @@ __global__ void __launch_bounds__(kThreads, 2)
                         ks > 0 ? 1u : 0u);
           umma_commit(&s_full[st]);
           if (j == it.n_kv - 1) umma_commit(q_empty);  // this item's Q is no longer read
-          if (j >= 1 && !(ok = pv(t - 1, j - 1, k))) break;
         }
-        if (!ok || !(ok = pv(t0 + it.n_kv - 1, it.n_kv - 1, k))) break;
-        ++k;
+        __syncwarp();
+        if (j >= 1 && !(ok = pv(t - 1, j - 1, k))) break;
       }
+      if (!ok || !(ok = pv(t0 + it.n_kv - 1, it.n_kv - 1, k))) break;
+      ++k;
     }
     __syncwarp();
   } else {
@@ -261,11 +325,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const int g = row / p.tq;
     const float sl2 = p.scale_log2;
-    int idx = static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x);
+    Walker w;
+    walker_init(p, w);
     Item it;
     int k = 0, t = 0;
     bool ok = true;
-    while (ok && next_item(p, idx, it)) {
+    while (ok && walker_next(p, w, it)) {
       const int tok = it.q0 + (row - g * p.tq);  // token index within the sequence
       const int lim = p.causal ? min(tok + 1, it.L) : it.L;  // keys [0, lim) are visible
       float m = NEG_INF, l = 0.f;
