@@ -175,14 +175,16 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOffset);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
-  uint64_t* kv_full = bars + 2;   // [2]
-  uint64_t* kv_empty = bars + 4;  // [2]
-  uint64_t* s_full = bars + 6;    // [2]
-  uint64_t* s_empty = bars + 8;   // [2]
-  uint64_t* p_full = bars + 10;
-  uint64_t* o_done = bars + 11;
-  uint64_t* o_empty = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* k_full = bars + 2;    // [2]  K ring: freed once QK^T has read it
+  uint64_t* k_empty = bars + 4;   // [2]
+  uint64_t* v_full = bars + 6;    // [2]  V ring: freed once PV has read it
+  uint64_t* v_empty = bars + 8;   // [2]
+  uint64_t* s_full = bars + 10;   // [2]
+  uint64_t* s_empty = bars + 12;  // [2]
+  uint64_t* p_full = bars + 14;
+  uint64_t* o_done = bars + 15;
+  uint64_t* o_empty = bars + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -203,8 +205,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
     }
@@ -224,49 +228,81 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (lane 0 issues)
+    // Two streams over the CTA's KV tiles in global order: K runs one tile
+    // ahead of V (issue order K(t+1), V(t)), so a K load waits only for the
+    // QK^T two tiles back, never for a PV. Q of a new item is loaded just
+    // before that item's first K.
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
     }
-    Walker w;
-    walker_init(p, w);
-    Item it;
-    int k = 0, t = 0;  // items and KV tiles issued by this CTA
+    Walker wk, wv;
+    walker_init(p, wk);
+    walker_init(p, wv);
+    Item ik, iv;
+    bool k_more = walker_next(p, wk, ik), v_more = walker_next(p, wv, iv);
+    int jk = 0, jv = 0;  // tile index within the K / V stream's current item
+    int tk = 0, tv = 0;  // global tile counters of the two streams
+    int items_q = 0;     // items whose Q has been loaded
     bool ok = true;
-    while (ok && walker_next(p, w, it)) {
-      if (lane == 0 && it.q0 == (p.n_qt - 1) * p.tq && it.L > p.n_qt * p.tq && p.err)
-        atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
-      // Q of item k replaces item k-1's once its last S MMA has completed.
-      if (!__all_sync(0xffffffffu, mbar_wait(q_empty, (k & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT))) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(q_full, kQTile);
-        for (int g = 0; g < p.group; ++g)
-          for (int half = 0; half < 2; ++half)
-            tma_load_3d(sQ + half * kQHalf + g * p.tq * 128, &tm_q, q_full, half * 64, it.h * p.group + g,
-                        it.seq0 + it.q0);
-      }
-      for (int j = 0; j < it.n_kv; ++j, ++t) {
-        const int st = t & 1;
-        if (!__all_sync(0xffffffffu,
-                        mbar_wait(&kv_empty[st], ((t >> 1) & 1) ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
-          ok = false;
-          break;
-        }
+    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
+    };
+    // Issue K tile tk (loading the item's Q first when it is the item's first tile).
+    auto issue_k = [&]() -> bool {
+      if (jk == 0) {
+        if (lane == 0 && ik.q0 == (p.n_qt - 1) * p.tq && ik.L > p.n_qt * p.tq && p.err)
+          atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
+        // Q of item k replaces item k-1's once its last QK^T has completed.
+        if (!wait_all(q_empty, (items_q & 1) ^ 1u)) return false;
         if (lane == 0) {
-          mbar_arrive_expect_tx(&kv_full[st], 2 * kKVTile);
-          for (int half = 0; half < 2; ++half) {
-            tma_load_3d(sK + st * kKVTile + half * kKVHalf, &tm_k, &kv_full[st], half * 64, it.h,
-                        it.seq0 + j * kKeys);
-            tma_load_3d(sV + st * kKVTile + half * kKVHalf, &tm_v, &kv_full[st], half * 64, it.h,
-                        it.seq0 + j * kKeys);
-          }
+          mbar_arrive_expect_tx(q_full, kQTile);
+          for (int g = 0; g < p.group; ++g)
+            for (int half = 0; half < 2; ++half)
+              tma_load_3d(sQ + half * kQHalf + g * p.tq * 128, &tm_q, q_full, half * 64, ik.h * p.group + g,
+                          ik.seq0 + ik.q0);
         }
+        ++items_q;
       }
-      ++k;
+      const int st = tk & 1;
+      if (!wait_all(&k_empty[st], ((tk >> 1) & 1) ^ 1u)) return false;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&k_full[st], kKVTile);
+        for (int half = 0; half < 2; ++half)
+          tma_load_3d(sK + st * kKVTile + half * kKVHalf, &tm_k, &k_full[st], half * 64, ik.h, ik.seq0 + jk * kKeys);
+      }
+      ++tk;
+      if (++jk == ik.n_kv) {
+        jk = 0;
+        k_more = walker_next(p, wk, ik);
+      }
+      return true;
+    };
+    auto issue_v = [&]() -> bool {
+      const int st = tv & 1;
+      if (!wait_all(&v_empty[st], ((tv >> 1) & 1) ^ 1u)) return false;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&v_full[st], kKVTile);
+        for (int half = 0; half < 2; ++half)
+          tma_load_3d(sV + st * kKVTile + half * kKVHalf, &tm_v, &v_full[st], half * 64, iv.h, iv.seq0 + jv * kKeys);
+      }
+      ++tv;
+      if (++jv == iv.n_kv) {
+        jv = 0;
+        v_more = walker_next(p, wv, iv);
+      }
+      return true;
+    };
+    if (k_more) ok = issue_k();  // K(0)
+    while (ok && v_more) {
+      if (k_more && !(ok = issue_k())) break;  // K(t+1)
+      ok = issue_v();                           // V(t)
     }
-    if (!ok && lane == 0)  // early exit: let the copies already issued land (bounded)
-      for (int u = (t > 2 ? t - 2 : 0); u < t; ++u) mbar_wait(&kv_full[u & 1], (u >> 1) & 1, nullptr, 0);
+    if (!ok && lane == 0) {  // early exit: let the copies already issued land (bounded)
+      for (int u = (tk > 2 ? tk - 2 : 0); u < tk; ++u) mbar_wait(&k_full[u & 1], (u >> 1) & 1, nullptr, 0);
+      for (int u = (tv > 2 ? tv - 2 : 0); u < tv; ++u) mbar_wait(&v_full[u & 1], (u >> 1) & 1, nullptr, 0);
+    }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (lane 0 issues)
@@ -279,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
     };
     auto pv = [&](int u, int ju, int kk) -> bool {  // O += P V for global tile u (item-local ju)
-      if (!wait_all(p_full, u & 1)) return false;
+      if (!wait_all(p_full, u & 1) || !wait_all(&v_full[u & 1], (u >> 1) & 1)) return false;
       if (ju == 0 && kk >= 1 && !wait_all(o_empty, (kk - 1) & 1)) return false;
       tc_fence_after();
       if (lane == 0) {
@@ -289,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           umma_f16_ss(tmem + kColO, desc_kmajor(sP, kPTile, ks), desc_v(vt, ks), kIdescPV,
                       (ju > 0 || ks > 0) ? 1u : 0u);
         umma_commit(o_done);
-        umma_commit(&kv_empty[u & 1]);
+        umma_commit(&v_empty[u & 1]);
       }
       __syncwarp();
       return true;
@@ -299,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int t0 = t;
       for (int j = 0; j < it.n_kv; ++j, ++t) {
         const int st = t & 1;
-        ok = wait_all(&kv_full[st], (t >> 1) & 1) && wait_all(&s_empty[st], ((t >> 1) & 1) ^ 1u);
+        ok = wait_all(&k_full[st], (t >> 1) & 1) && wait_all(&s_empty[st], ((t >> 1) & 1) ^ 1u);
         if (!ok) break;
         tc_fence_after();
         if (lane == 0) {
@@ -309,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             umma_f16_ss(tmem + st * kKeys, desc_kmajor(sQ, kQHalf, ks), desc_kmajor(kt, kKVHalf, ks), kIdescQK,
                         ks > 0 ? 1u : 0u);
           umma_commit(&s_full[st]);
+          umma_commit(&k_empty[st]);  // K tile read
           if (j == it.n_kv - 1) umma_commit(q_empty);  // this item's Q is no longer read
         }
         __syncwarp();
