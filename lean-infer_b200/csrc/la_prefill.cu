@@ -228,8 +228,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (lane 0 issues)
-    // Two streams over the CTA's KV tiles in global order: K runs one tile
-    // ahead of V (issue order K(t+1), V(t)), so a K load waits only for the
+    // Two streams over the CTA's KV tiles in global order: K runs two tiles
+    // ahead of V (issue order K(t+2), V(t)), so a K load waits only for the
     // QK^T two tiles back, never for a PV. Q of a new item is loaded just
     // before that item's first K.
     if (lane == 0) {
@@ -294,9 +294,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       return true;
     };
-    if (k_more) ok = issue_k();  // K(0)
+    for (int i = 0; i < 2 && ok && k_more; ++i) ok = issue_k();  // K(0), K(1)
     while (ok && v_more) {
-      if (k_more && !(ok = issue_k())) break;  // K(t+1)
+      if (k_more && !(ok = issue_k())) break;  // K(t+2)
       ok = issue_v();                           // V(t)
     }
     if (!ok && lane == 0) {  // early exit: let the copies already issued land (bounded)
@@ -306,53 +306,71 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (lane 0 issues)
-    Walker w;
-    walker_init(p, w);
-    Item it;
-    int k = 0, t = 0;
+    // Two streams over the CTA's tiles: QK^T runs two tiles ahead of PV
+    // (issue order S(t+2), PV(t)). S(t+2) only needs softmax to have read
+    // S(t) out of TMEM, so it is issued while softmax(t) still computes, and
+    // softmax(t+1) finds its scores ready.
+    Walker ws, wp;
+    walker_init(p, ws);
+    walker_init(p, wp);
+    Item is, ip;
+    bool s_more = walker_next(p, ws, is), p_more = walker_next(p, wp, ip);
+    int js = 0, ts = 0, qs = 0;  // S stream: tile within item, global tile, items started
+    int jp = 0, tp = 0, kp = 0;  // PV stream: tile within item, global tile, items finished
     bool ok = true;
     auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
     };
-    auto pv = [&](int u, int ju, int kk) -> bool {  // O += P V for global tile u (item-local ju)
-      if (!wait_all(p_full, u & 1) || !wait_all(&v_full[u & 1], (u >> 1) & 1)) return false;
-      if (ju == 0 && kk >= 1 && !wait_all(o_empty, (kk - 1) & 1)) return false;
+    auto issue_s = [&]() -> bool {
+      if (js == 0 && !wait_all(q_full, qs & 1)) return false;  // this item's Q has landed
+      const int st = ts & 1;
+      if (!wait_all(&k_full[st], (ts >> 1) & 1) || !wait_all(&s_empty[st], ((ts >> 1) & 1) ^ 1u)) return false;
       tc_fence_after();
       if (lane == 0) {
-        const uint8_t* vt = sV + (u & 1) * kKVTile;
+        const uint8_t* kt = sK + st * kKVTile;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_f16_ss(tmem + st * kKeys, desc_kmajor(sQ, kQHalf, ks), desc_kmajor(kt, kKVHalf, ks), kIdescQK,
+                      ks > 0 ? 1u : 0u);
+        umma_commit(&s_full[st]);
+        umma_commit(&k_empty[st]);                 // K tile read
+        if (js == is.n_kv - 1) umma_commit(q_empty);  // this item's Q is no longer read
+      }
+      __syncwarp();
+      ++ts;
+      if (++js == is.n_kv) {
+        js = 0;
+        ++qs;
+        s_more = walker_next(p, ws, is);
+      }
+      return true;
+    };
+    auto issue_pv = [&]() -> bool {  // O += P V for global tile tp (item-local jp)
+      if (!wait_all(p_full, tp & 1) || !wait_all(&v_full[tp & 1], (tp >> 1) & 1)) return false;
+      if (jp == 0 && kp >= 1 && !wait_all(o_empty, (kp - 1) & 1)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint8_t* vt = sV + (tp & 1) * kKVTile;
 #pragma unroll
         for (int ks = 0; ks < kKeys / 16; ++ks)
           umma_f16_ss(tmem + kColO, desc_kmajor(sP, kPTile, ks), desc_v(vt, ks), kIdescPV,
-                      (ju > 0 || ks > 0) ? 1u : 0u);
+                      (jp > 0 || ks > 0) ? 1u : 0u);
         umma_commit(o_done);
-        umma_commit(&v_empty[u & 1]);
+        umma_commit(&v_empty[tp & 1]);
       }
       __syncwarp();
+      ++tp;
+      if (++jp == ip.n_kv) {
+        jp = 0;
+        ++kp;
+        p_more = walker_next(p, wp, ip);
+      }
       return true;
     };
-    while (ok && walker_next(p, w, it)) {
-      if (!wait_all(q_full, k & 1)) break;
-      const int t0 = t;
-      for (int j = 0; j < it.n_kv; ++j, ++t) {
-        const int st = t & 1;
-        ok = wait_all(&k_full[st], (t >> 1) & 1) && wait_all(&s_empty[st], ((t >> 1) & 1) ^ 1u);
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
-          const uint8_t* kt = sK + st * kKVTile;
-#pragma unroll
-          for (int ks = 0; ks < 8; ++ks)
-            umma_f16_ss(tmem + st * kKeys, desc_kmajor(sQ, kQHalf, ks), desc_kmajor(kt, kKVHalf, ks), kIdescQK,
-                        ks > 0 ? 1u : 0u);
-          umma_commit(&s_full[st]);
-          umma_commit(&k_empty[st]);  // K tile read
-          if (j == it.n_kv - 1) umma_commit(q_empty);  // this item's Q is no longer read
-        }
-        __syncwarp();
-        if (j >= 1 && !(ok = pv(t - 1, j - 1, k))) break;
-      }
-      if (!ok || !(ok = pv(t0 + it.n_kv - 1, it.n_kv - 1, k))) break;
-      ++k;
+    for (int i = 0; i < 2 && ok && s_more; ++i) ok = issue_s();  // S(0), S(1)
+    while (ok && p_more) {
+      if (s_more && !(ok = issue_s())) break;  // S(t+2)
+      ok = issue_pv();                          // PV(t)
     }
     __syncwarp();
   } else {
