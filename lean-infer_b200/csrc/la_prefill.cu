@@ -228,10 +228,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (lane 0 issues)
-    // Two streams over the CTA's KV tiles in global order: K runs two tiles
-    // ahead of V (issue order K(t+2), V(t)), so a K load waits only for the
-    // QK^T two tiles back, never for a PV. Q of a new item is loaded just
-    // before that item's first K.
+    // Two streams over the CTA's KV tiles in global order: K (and, at an
+    // item's first tile, its Q) and V, each issued as soon as its ring slot
+    // is free; K may run up to three tiles ahead of V.
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -294,10 +293,32 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       return true;
     };
-    for (int i = 0; i < 2 && ok && k_more; ++i) ok = issue_k();  // K(0), K(1)
-    while (ok && v_more) {
-      if (k_more && !(ok = issue_k())) break;  // K(t+2)
-      ok = issue_v();                           // V(t)
+    // Dataflow order: issue whichever load has a free slot (V first: PV is
+    // on softmax's critical path), never blocking one stream on the other.
+    uint64_t t_idle = 0;
+    while (ok && (v_more || k_more)) {
+      int pick = 0;  // 1 = V, 2 = K
+      if (lane == 0) {
+        if (v_more && tv < tk && mbar_test(&v_empty[tv & 1], ((tv >> 1) & 1) ^ 1u)) pick = 1;
+        else if (k_more && tk < tv + 3 && mbar_test(&k_empty[tk & 1], ((tk >> 1) & 1) ^ 1u) &&
+                 (jk != 0 || mbar_test(q_empty, (items_q & 1) ^ 1u)))
+          pick = 2;
+      }
+      pick = __shfl_sync(0xffffffffu, pick, 0);
+      if (pick == 1) {
+        ok = issue_v();
+        t_idle = 0;
+      } else if (pick == 2) {
+        ok = issue_k();
+        t_idle = 0;
+      } else {
+        const uint64_t now = globaltimer_ns();
+        if (t_idle == 0) t_idle = now;
+        else if (now - t_idle > LA_WAIT_LIMIT_NS) {
+          if (lane == 0 && p.err) atomicCAS(p.err, 0, LA_DEVERR_WAIT_TIMEOUT);
+          ok = false;
+        }
+      }
     }
     if (!ok && lane == 0) {  // early exit: let the copies already issued land (bounded)
       for (int u = (tk > 2 ? tk - 2 : 0); u < tk; ++u) mbar_wait(&k_full[u & 1], (u >> 1) & 1, nullptr, 0);
@@ -306,10 +327,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (lane 0 issues)
-    // Two streams over the CTA's tiles: QK^T runs two tiles ahead of PV
-    // (issue order S(t+2), PV(t)). S(t+2) only needs softmax to have read
-    // S(t) out of TMEM, so it is issued while softmax(t) still computes, and
-    // softmax(t+1) finds its scores ready.
+    // Two streams over the CTA's tiles: QK^T (into one of two TMEM score
+    // buffers) and PV. S(t+2) only needs softmax to have read S(t) out of
+    // TMEM, so it can be issued while softmax(t) still computes and
+    // softmax(t+1) finds its scores ready; neither stream blocks the other.
     Walker ws, wp;
     walker_init(p, ws);
     walker_init(p, wp);
@@ -367,10 +388,34 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       return true;
     };
-    for (int i = 0; i < 2 && ok && s_more; ++i) ok = issue_s();  // S(0), S(1)
+    // Dataflow order: PV when its P and V are ready (it unblocks softmax),
+    // else the next QK^T when its Q, K and TMEM buffer are ready.
+    uint64_t t_idle = 0;
     while (ok && p_more) {
-      if (s_more && !(ok = issue_s())) break;  // S(t+2)
-      ok = issue_pv();                          // PV(t)
+      int pick = 0;  // 1 = PV, 2 = S
+      if (lane == 0) {
+        if (tp < ts && mbar_test(p_full, tp & 1) && mbar_test(&v_full[tp & 1], (tp >> 1) & 1) &&
+            (jp != 0 || kp == 0 || mbar_test(o_empty, (kp - 1) & 1)))
+          pick = 1;
+        else if (s_more && mbar_test(&k_full[ts & 1], (ts >> 1) & 1) &&
+                 mbar_test(&s_empty[ts & 1], ((ts >> 1) & 1) ^ 1u) && (js != 0 || mbar_test(q_full, qs & 1)))
+          pick = 2;
+      }
+      pick = __shfl_sync(0xffffffffu, pick, 0);
+      if (pick == 1) {
+        ok = issue_pv();
+        t_idle = 0;
+      } else if (pick == 2) {
+        ok = issue_s();
+        t_idle = 0;
+      } else {
+        const uint64_t now = globaltimer_ns();
+        if (t_idle == 0) t_idle = now;
+        else if (now - t_idle > LA_WAIT_LIMIT_NS) {
+          if (lane == 0 && p.err) atomicCAS(p.err, 0, LA_DEVERR_WAIT_TIMEOUT);
+          ok = false;
+        }
+      }
     }
     __syncwarp();
   } else {
