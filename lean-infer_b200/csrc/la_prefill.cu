@@ -311,7 +311,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       } else if (pick == 2) {
         ok = issue_k();
         t_idle = 0;
-      } else {
+      } else {  // nothing ready: back off so the softmax warps keep the issue slots
+        __nanosleep(40);
         const uint64_t now = globaltimer_ns();
         if (t_idle == 0) t_idle = now;
         else if (now - t_idle > LA_WAIT_LIMIT_NS) {
@@ -408,7 +409,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       } else if (pick == 2) {
         ok = issue_s();
         t_idle = 0;
-      } else {
+      } else {  // nothing ready: back off so the softmax warps keep the issue slots
+        __nanosleep(40);
         const uint64_t now = globaltimer_ns();
         if (t_idle == 0) t_idle = now;
         else if (now - t_idle > LA_WAIT_LIMIT_NS) {
