@@ -26,8 +26,9 @@
 // softmax warps work, the other's MMAs run, and each scheduler has two
 // softmax warps to switch between.
 //
-// Warps: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 = softmax and
-// epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows of that quarter).
+// Warps: 0 = TMA producer, 1 = QK^T issuer + TMEM owner, 2..5 = softmax and
+// epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows of that quarter);
+// warp 2 also issues PV once the four softmax warps have written P.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -228,9 +229,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (lane 0 issues)
-    // Two streams over the CTA's KV tiles in global order: K (and, at an
-    // item's first tile, its Q) and V, each issued as soon as its ring slot
-    // is free; K may run up to three tiles ahead of V.
+    // Two streams over the CTA's KV tiles in global order: K runs one tile
+    // ahead of V (issue order K(t+1), V(t)), so a K load waits only for the
+    // QK^T two tiles back, never for a PV. Q of a new item is loaded just
+    // before that item's first K.
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
@@ -293,33 +295,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       return true;
     };
-    // Dataflow order: issue whichever load has a free slot (V first: PV is
-    // on softmax's critical path), never blocking one stream on the other.
-    uint64_t t_idle = 0;
-    while (ok && (v_more || k_more)) {
-      int pick = 0;  // 1 = V, 2 = K
-      if (lane == 0) {
-        if (v_more && tv < tk && mbar_test(&v_empty[tv & 1], ((tv >> 1) & 1) ^ 1u)) pick = 1;
-        else if (k_more && tk < tv + 3 && mbar_test(&k_empty[tk & 1], ((tk >> 1) & 1) ^ 1u) &&
-                 (jk != 0 || mbar_test(q_empty, (items_q & 1) ^ 1u)))
-          pick = 2;
-      }
-      pick = __shfl_sync(0xffffffffu, pick, 0);
-      if (pick == 1) {
-        ok = issue_v();
-        t_idle = 0;
-      } else if (pick == 2) {
-        ok = issue_k();
-        t_idle = 0;
-      } else {  // nothing ready: back off so the softmax warps keep the issue slots
-        __nanosleep(40);
-        const uint64_t now = globaltimer_ns();
-        if (t_idle == 0) t_idle = now;
-        else if (now - t_idle > LA_WAIT_LIMIT_NS) {
-          if (lane == 0 && p.err) atomicCAS(p.err, 0, LA_DEVERR_WAIT_TIMEOUT);
-          ok = false;
-        }
-      }
+    if (k_more) ok = issue_k();  // K(0)
+    while (ok && v_more) {
+      if (k_more && !(ok = issue_k())) break;  // K(t+1)
+      ok = issue_v();                           // V(t)
     }
     if (!ok && lane == 0) {  // early exit: let the copies already issued land (bounded)
       for (int u = (tk > 2 ? tk - 2 : 0); u < tk; ++u) mbar_wait(&k_full[u & 1], (u >> 1) & 1, nullptr, 0);
@@ -327,97 +306,38 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (lane 0 issues)
-    // Two streams over the CTA's tiles: QK^T (into one of two TMEM score
-    // buffers) and PV. S(t+2) only needs softmax to have read S(t) out of
-    // TMEM, so it can be issued while softmax(t) still computes and
-    // softmax(t+1) finds its scores ready; neither stream blocks the other.
-    Walker ws, wp;
-    walker_init(p, ws);
-    walker_init(p, wp);
-    Item is, ip;
-    bool s_more = walker_next(p, ws, is), p_more = walker_next(p, wp, ip);
-    int js = 0, ts = 0, qs = 0;  // S stream: tile within item, global tile, items started
-    int jp = 0, tp = 0, kp = 0;  // PV stream: tile within item, global tile, items finished
+    // ------------------------------------------------------------ QK^T issuer (lane 0 issues)
+    // Only QK^T is issued here; PV is issued by the softmax group as soon as
+    // its P is written. S(t+2) therefore goes out as soon as softmax has read
+    // S(t) from TMEM, while softmax(t) still computes.
+    Walker w;
+    walker_init(p, w);
+    Item it;
+    int k = 0, t = 0;
     bool ok = true;
     auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
     };
-    auto issue_s = [&]() -> bool {
-      if (js == 0 && !wait_all(q_full, qs & 1)) return false;  // this item's Q has landed
-      const int st = ts & 1;
-      if (!wait_all(&k_full[st], (ts >> 1) & 1) || !wait_all(&s_empty[st], ((ts >> 1) & 1) ^ 1u)) return false;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint8_t* kt = sK + st * kKVTile;
+    while (ok && walker_next(p, w, it)) {
+      if (!wait_all(q_full, k & 1)) break;
+      for (int j = 0; j < it.n_kv; ++j, ++t) {
+        const int st = t & 1;
+        ok = wait_all(&k_full[st], (t >> 1) & 1) && wait_all(&s_empty[st], ((t >> 1) & 1) ^ 1u);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint8_t* kt = sK + st * kKVTile;
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_f16_ss(tmem + st * kKeys, desc_kmajor(sQ, kQHalf, ks), desc_kmajor(kt, kKVHalf, ks), kIdescQK,
-                      ks > 0 ? 1u : 0u);
-        umma_commit(&s_full[st]);
-        umma_commit(&k_empty[st]);                 // K tile read
-        if (js == is.n_kv - 1) umma_commit(q_empty);  // this item's Q is no longer read
-      }
-      __syncwarp();
-      ++ts;
-      if (++js == is.n_kv) {
-        js = 0;
-        ++qs;
-        s_more = walker_next(p, ws, is);
-      }
-      return true;
-    };
-    auto issue_pv = [&]() -> bool {  // O += P V for global tile tp (item-local jp)
-      if (!wait_all(p_full, tp & 1) || !wait_all(&v_full[tp & 1], (tp >> 1) & 1)) return false;
-      if (jp == 0 && kp >= 1 && !wait_all(o_empty, (kp - 1) & 1)) return false;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint8_t* vt = sV + (tp & 1) * kKVTile;
-#pragma unroll
-        for (int ks = 0; ks < kKeys / 16; ++ks)
-          umma_f16_ss(tmem + kColO, desc_kmajor(sP, kPTile, ks), desc_v(vt, ks), kIdescPV,
-                      (jp > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(o_done);
-        umma_commit(&v_empty[tp & 1]);
-      }
-      __syncwarp();
-      ++tp;
-      if (++jp == ip.n_kv) {
-        jp = 0;
-        ++kp;
-        p_more = walker_next(p, wp, ip);
-      }
-      return true;
-    };
-    // Dataflow order: PV when its P and V are ready (it unblocks softmax),
-    // else the next QK^T when its Q, K and TMEM buffer are ready.
-    uint64_t t_idle = 0;
-    while (ok && p_more) {
-      int pick = 0;  // 1 = PV, 2 = S
-      if (lane == 0) {
-        if (tp < ts && mbar_test(p_full, tp & 1) && mbar_test(&v_full[tp & 1], (tp >> 1) & 1) &&
-            (jp != 0 || kp == 0 || mbar_test(o_empty, (kp - 1) & 1)))
-          pick = 1;
-        else if (s_more && mbar_test(&k_full[ts & 1], (ts >> 1) & 1) &&
-                 mbar_test(&s_empty[ts & 1], ((ts >> 1) & 1) ^ 1u) && (js != 0 || mbar_test(q_full, qs & 1)))
-          pick = 2;
-      }
-      pick = __shfl_sync(0xffffffffu, pick, 0);
-      if (pick == 1) {
-        ok = issue_pv();
-        t_idle = 0;
-      } else if (pick == 2) {
-        ok = issue_s();
-        t_idle = 0;
-      } else {  // nothing ready: back off so the softmax warps keep the issue slots
-        __nanosleep(40);
-        const uint64_t now = globaltimer_ns();
-        if (t_idle == 0) t_idle = now;
-        else if (now - t_idle > LA_WAIT_LIMIT_NS) {
-          if (lane == 0 && p.err) atomicCAS(p.err, 0, LA_DEVERR_WAIT_TIMEOUT);
-          ok = false;
+          for (int ks = 0; ks < 8; ++ks)
+            umma_f16_ss(tmem + st * kKeys, desc_kmajor(sQ, kQHalf, ks), desc_kmajor(kt, kKVHalf, ks), kIdescQK,
+                        ks > 0 ? 1u : 0u);
+          umma_commit(&s_full[st]);
+          umma_commit(&k_empty[st]);  // K tile read
+          if (j == it.n_kv - 1) umma_commit(q_empty);  // this item's Q is no longer read
         }
+        __syncwarp();
       }
+      ++k;
     }
     __syncwarp();
   } else {
@@ -527,6 +447,28 @@ __global__ void __launch_bounds__(kThreads, 2)
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(p_full);
+        if (warp == 2) {
+          // PV for this tile, issued by warp 2 once all 128 rows of P are in
+          // shared memory (and V(t) has landed; and, at an item's first tile,
+          // the previous item's epilogue has read O).
+          ok = __all_sync(0xffffffffu, mbar_wait(p_full, t & 1, p.err, LA_DEVERR_WAIT_TIMEOUT) &&
+                                           mbar_wait(&v_full[t & 1], (t >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT) &&
+                                           (j != 0 || k == 0 ||
+                                            mbar_wait(o_empty, (k - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)));
+          if (ok) {
+            tc_fence_after();
+            if (lane == 0) {
+              const uint8_t* vt = sV + (t & 1) * kKVTile;
+#pragma unroll
+              for (int ks = 0; ks < kKeys / 16; ++ks)
+                umma_f16_ss(tmem + kColO, desc_kmajor(sP, kPTile, ks), desc_v(vt, ks), kIdescPV,
+                            (j > 0 || ks > 0) ? 1u : 0u);
+              umma_commit(o_done);
+              umma_commit(&v_empty[t & 1]);
+            }
+            __syncwarp();
+          }
+        }
       }
       if (!ok) break;
       // ---------------------------------------------------------- epilogue
