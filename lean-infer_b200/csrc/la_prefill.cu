@@ -26,9 +26,8 @@
 // softmax warps work, the other's MMAs run, and each scheduler has two
 // softmax warps to switch between.
 //
-// Warps: 0 = TMA producer, 1 = QK^T issuer + TMEM owner, 2..5 = softmax and
-// epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows of that quarter);
-// warp 2 also issues PV once the four softmax warps have written P.
+// Warps: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 = softmax and
+// epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows of that quarter).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -74,6 +73,24 @@ struct Params {
   long long total;
   int* err;
 };
+
+// 2^x on the FMA/ALU pipes, for half of the softmax exponentials (the MUFU
+// unit retires only 16 ex2 per clock per SM and is the softmax bottleneck).
+// Cody-Waite split x = j + f with j = round(x) read from the low mantissa bits
+// of x + 1.5*2^23 and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial with
+// coefficients fitted for this kernel by Lawson's iteration for the minimax
+// relative error on [-0.5, 0.5] (max relative error 7.5e-5, far below the
+// bf16 rounding of P); j is then added to the exponent field. Inputs below
+// -126 (masked scores) give ~1e-38 instead of 0, which cannot move a bf16
+// output.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = x + 12582912.f;  // 1.5 * 2^23
+  const int j = __float_as_int(t) - 0x4B400000;
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.05517132f, f, 0.24261054f), f, 0.69326097f), f, 0.99992812f);
+  return __int_as_float(__float_as_int(p) + (j << 23));
+}
 
 // K-major operand of 128-byte SW128 rows whose 128-wide reduction dimension is
 // split into two 64-wide halves `half_bytes` apart: k-step ks covers elements
@@ -306,10 +323,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ QK^T issuer (lane 0 issues)
-    // Only QK^T is issued here; PV is issued by the softmax group as soon as
-    // its P is written. S(t+2) therefore goes out as soon as softmax has read
-    // S(t) from TMEM, while softmax(t) still computes.
+    // ------------------------------------------------------------ MMA issuer (lane 0 issues)
     Walker w;
     walker_init(p, w);
     Item it;
@@ -318,8 +332,25 @@ __global__ void __launch_bounds__(kThreads, 2)
     auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
     };
+    auto pv = [&](int u, int ju, int kk) -> bool {  // O += P V for global tile u (item-local ju)
+      if (!wait_all(p_full, u & 1) || !wait_all(&v_full[u & 1], (u >> 1) & 1)) return false;
+      if (ju == 0 && kk >= 1 && !wait_all(o_empty, (kk - 1) & 1)) return false;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint8_t* vt = sV + (u & 1) * kKVTile;
+#pragma unroll
+        for (int ks = 0; ks < kKeys / 16; ++ks)
+          umma_f16_ss(tmem + kColO, desc_kmajor(sP, kPTile, ks), desc_v(vt, ks), kIdescPV,
+                      (ju > 0 || ks > 0) ? 1u : 0u);
+        umma_commit(o_done);
+        umma_commit(&v_empty[u & 1]);
+      }
+      __syncwarp();
+      return true;
+    };
     while (ok && walker_next(p, w, it)) {
       if (!wait_all(q_full, k & 1)) break;
+      const int t0 = t;
       for (int j = 0; j < it.n_kv; ++j, ++t) {
         const int st = t & 1;
         ok = wait_all(&k_full[st], (t >> 1) & 1) && wait_all(&s_empty[st], ((t >> 1) & 1) ^ 1u);
@@ -336,7 +367,9 @@ __global__ void __launch_bounds__(kThreads, 2)
           if (j == it.n_kv - 1) umma_commit(q_empty);  // this item's Q is no longer read
         }
         __syncwarp();
+        if (j >= 1 && !(ok = pv(t - 1, j - 1, k))) break;
       }
+      if (!ok || !(ok = pv(t0 + it.n_kv - 1, it.n_kv - 1, k))) break;
       ++k;
     }
     __syncwarp();
@@ -405,7 +438,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < kC; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float pe = ex2(fmaf(sv[c][e], sl2, neg_m));  // masked: -inf -> 0
+            const float x = fmaf(sv[c][e], sl2, neg_m);
+            const float pe = (e & 1) ? exp2_fma(x) : ex2(x);  // masked: -inf -> ~0
             sv[c][e] = pe;
             ps[e & 7] += pe;
           }
@@ -447,28 +481,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(p_full);
-        if (warp == 2) {
-          // PV for this tile, issued by warp 2 once all 128 rows of P are in
-          // shared memory (and V(t) has landed; and, at an item's first tile,
-          // the previous item's epilogue has read O).
-          ok = __all_sync(0xffffffffu, mbar_wait(p_full, t & 1, p.err, LA_DEVERR_WAIT_TIMEOUT) &&
-                                           mbar_wait(&v_full[t & 1], (t >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT) &&
-                                           (j != 0 || k == 0 ||
-                                            mbar_wait(o_empty, (k - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT)));
-          if (ok) {
-            tc_fence_after();
-            if (lane == 0) {
-              const uint8_t* vt = sV + (t & 1) * kKVTile;
-#pragma unroll
-              for (int ks = 0; ks < kKeys / 16; ++ks)
-                umma_f16_ss(tmem + kColO, desc_kmajor(sP, kPTile, ks), desc_v(vt, ks), kIdescPV,
-                            (j > 0 || ks > 0) ? 1u : 0u);
-              umma_commit(o_done);
-              umma_commit(&v_empty[t & 1]);
-            }
-            __syncwarp();
-          }
-        }
       }
       if (!ok) break;
       // ---------------------------------------------------------- epilogue
