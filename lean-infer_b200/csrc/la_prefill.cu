@@ -74,24 +74,6 @@ struct Params {
   int* err;
 };
 
-// 2^x on the FMA/ALU pipes, for half of the softmax exponentials (the MUFU
-// unit retires only 16 ex2 per clock per SM and is the softmax bottleneck).
-// Cody-Waite split x = j + f with j = round(x) read from the low mantissa bits
-// of x + 1.5*2^23 and f in [-0.5, 0.5]; 2^f from a degree-3 polynomial with
-// coefficients fitted for this kernel by Lawson's iteration for the minimax
-// relative error on [-0.5, 0.5] (max relative error 7.5e-5, far below the
-// bf16 rounding of P); j is then added to the exponent field. Inputs below
-// -126 (masked scores) give ~1e-38 instead of 0, which cannot move a bf16
-// output.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -126.f);
-  const float t = x + 12582912.f;  // 1.5 * 2^23
-  const int j = __float_as_int(t) - 0x4B400000;
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.05517132f, f, 0.24261054f), f, 0.69326097f), f, 0.99992812f);
-  return __int_as_float(__float_as_int(p) + (j << 23));
-}
-
 // K-major operand of 128-byte SW128 rows whose 128-wide reduction dimension is
 // split into two 64-wide halves `half_bytes` apart: k-step ks covers elements
 // 16ks..16ks+15.
@@ -438,8 +420,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int c = 0; c < kC; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float x = fmaf(sv[c][e], sl2, neg_m);
-            const float pe = (e & 1) ? exp2_fma(x) : ex2(x);  // masked: -inf -> ~0
+            const float pe = ex2(fmaf(sv[c][e], sl2, neg_m));  // masked: -inf -> 0
             sv[c][e] = pe;
             ps[e & 7] += pe;
           }
