@@ -234,6 +234,65 @@ def kv_head_sharded_layer(pkg, dist, world, rank, dev, reps, max_over_ranks):
             "tok_per_s_attention_only": B / (t_layer * 28 * 1e-6)}
 
 
+def measured_peak_bf16():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+def graph_time_us(fn, reps):
+    """Mean device time of fn() over `reps` graph-captured calls (CUDA events)."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) * 1e3 / reps
+
+
+def secondary_metrics(pkg, dev):
+    """The metric's other components, on one GPU: causal varlen prefill
+    TFLOP/s (16 packed prompts, lengths U[512,1024]) and long-context
+    split-KV decode GB/s (B=32, contexts U[8192,32768], 256-token blocks)."""
+    from lean_infer_b200 import workloads as W
+
+    out = {}
+    w = W.prefill_batch(16, CTX_LO, CTX_HI, seed=3, device=dev)
+    mx = int(w.lengths.max())
+    us = graph_time_us(lambda: pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx,
+                                                          causal=True), 20)
+    peak, kind = measured_peak_bf16()
+    tf = w.causal_flops / (us * 1e-6) / 1e12
+    out["prefill_b16"] = {"workload": "16 packed prompts, lengths U[512,1024], causal, 16/8 heads, D=128",
+                          "us": us, "tflops": tf, "peak_tflops": peak, "frac": tf / peak, "peak_source": kind,
+                          "flops": w.causal_flops}
+    del w
+    d = W.decode_batch(32, 8192, 32768, num_blocks=None, block_size=BLOCK_SIZE, seed=40, device=dev)
+    us = graph_time_us(lambda: pkg.flash_attn_with_kvcache(d.q, d.k_cache, d.v_cache, cache_seqlens=d.cache_seqlens,
+                                                           block_table=d.block_table, causal=True), 5)
+    hbm, kind = measured_peak_hbm()
+    gbs = d.kv_bytes / (us * 1e-6) / 1e9
+    out["decode_long_b32"] = {"workload": "B=32, contexts U[8192,32768], 256-token blocks (split-KV)",
+                              "us": us, "gbs": gbs, "peak_gbs": hbm, "frac": gbs / hbm, "kv_bytes": d.kv_bytes}
+    del d
+    torch.cuda.synchronize()
+    pkg.check_device_errors(dev.index)
+    return out
+
+
 def run_reference(args):
     rank = env_int("RANK", 0)
     if rank != 0:
@@ -396,7 +455,10 @@ def run_ours(args):
                      "us_per_launch": us_per_launch},
         "clocks": clk.summary(),
     }
+    if rank == 0:
+        result["secondary"] = secondary_metrics(pkg, dev)
     if world > 1:
+        dist.barrier()
         result["kv_head_sharded"] = kv_head_sharded_layer(pkg, dist, world, rank, dev, max(8, args.steps // 10),
                                                           max_over_ranks)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
