@@ -152,6 +152,57 @@ int la_paged_decode(
     void* workspace, size_t workspace_bytes,
     int* dev_error, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------
+ * KV-head-sharded decode with the all-gather fused in (NVLink peer stores).
+ *
+ * For P ranks (one process per GPU) each holding kv heads
+ * [r*Hkv/P, (r+1)*Hkv/P) of every request: rank r runs la_paged_decode on
+ * its heads (num_q_heads / num_kv_heads = this rank's counts) and stores
+ * each output row into every rank's gather buffer [batch, P*num_q_heads, D]
+ * at heads [r*num_q_heads, (r+1)*num_q_heads), over NVLink; every thread
+ * that stored fences at system scope. la_p2p_barrier, next on the same
+ * stream, completes the exchange: after it the gather buffer holds all
+ * heads. Replaces the NCCL all-gather of the attention outputs before
+ * o_proj (leaninfer/qwen3/model.py:68-69) for the KV-head-sharded variant;
+ * the reference itself is single-GPU.
+ * gather_bufs: host array of `world` device pointers in rank order (own
+ * buffer included; peers' mapped with la_p2p_open). A gather buffer is
+ * written by every rank, so a caller double-buffers it across consecutive
+ * calls (the barrier of call n+1 orders call n+2's stores after call n's
+ * reads on every rank).
+ * ------------------------------------------------------------------------ */
+int la_paged_decode_allgather(
+    const void* q, int64_t q_batch_stride, int64_t q_head_stride,
+    const void* k_cache, const void* v_cache,
+    int64_t kv_block_stride, int64_t kv_token_stride, int64_t kv_head_stride,
+    int64_t num_blocks, int block_size,
+    const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
+    const int32_t* cache_seqlens,
+    int batch, int num_q_heads, int num_kv_heads, int head_dim,
+    float softmax_scale,
+    void* const* gather_bufs, int64_t out_batch_stride, int64_t out_head_stride,
+    int rank, int world,
+    void* workspace, size_t workspace_bytes,
+    int* dev_error, cudaStream_t stream);
+
+/* Device-side barrier of `world` ranks on `stream` (one 32-thread launch):
+ * publishes this rank's next epoch into word [rank] of every rank's signal
+ * words (store-release, system scope), then waits until every peer's epoch in
+ * this rank's words has reached it (bounded: LA_DEVERR_WAIT_TIMEOUT after 2 s,
+ * then returns). Peer stores made earlier on each rank's stream with a
+ * system-scope fence are visible after it. signals: host array of `world`
+ * device pointers to each rank's signal words (world + 1 uint32, zeroed once
+ * by la_p2p_alloc), rank order. */
+int la_p2p_barrier(unsigned int* const* signals, int world, int rank, int* dev_error, cudaStream_t stream);
+
+/* Peer-memory setup (host-side, outside the hot path; these allocate):
+ * la_p2p_alloc: cudaMalloc + zero + CUDA IPC handle (64 bytes) to share;
+ * la_p2p_open: map a peer's handle; la_p2p_close / la_p2p_free undo them. */
+int la_p2p_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int la_p2p_open(const void* ipc_handle, void** peer_ptr);
+int la_p2p_close(void* peer_ptr);
+int la_p2p_free(void* ptr);
+
 /* Allocation-free form of la_paged_decode, for callers that cannot allocate
  * device memory where they run decode: a C/C++ host in the middle of a
  * stream capture (cudaMalloc cannot be captured), a runtime that hands out

@@ -91,6 +91,25 @@ _SIGNATURES = {
         c_void_p,
         c_void_p, c_void_p,
     ],
+    "la_paged_decode_allgather": [
+        c_void_p, c_int64, c_int64,
+        c_void_p, c_void_p,
+        c_int64, c_int64, c_int64,
+        c_int64, c_int,
+        c_void_p, c_int64, c_int,
+        c_void_p,
+        c_int, c_int, c_int, c_int,
+        c_float,
+        c_void_p, c_int64, c_int64,
+        c_int, c_int,
+        c_void_p, c_size_t,
+        c_void_p, c_void_p,
+    ],
+    "la_p2p_barrier": [c_void_p, c_int, c_int, c_void_p, c_void_p],
+    "la_p2p_alloc": [c_size_t, POINTER(c_void_p), c_void_p],
+    "la_p2p_open": [c_void_p, POINTER(c_void_p)],
+    "la_p2p_close": [c_void_p],
+    "la_p2p_free": [c_void_p],
     "la_prefill_varlen": [
         c_void_p, c_int64, c_int64,
         c_void_p, c_int64, c_int64,

@@ -50,6 +50,7 @@ constexpr int kKVBytes = 2 * kKVHalf;           // 32 KB per tensor per stage
 // contiguous run that a single TMA box [64 dims, 16 tokens, Hkv heads] fills.
 constexpr int kMaxStages = 4;
 
+constexpr int kMaxPeers = 8;  // ranks of a KV-head-sharded group
 constexpr int kFlagFirst = 1;  // first stage of this CTA's segment of the sequence
 constexpr int kFlagLast = 2;   // last stage of the segment
 constexpr int kFlagWhole = 4;  // the segment is the whole sequence
@@ -76,6 +77,15 @@ struct Params {
   float scale_log2;
   __nv_bfloat16* out;
   long long out_b_stride, out_h_stride;
+  // The decode pass writes `out` only. The combine pass stores every output
+  // row to outs[0..nouts): `out` alone, or, for the KV-head-sharded
+  // all-gather, every rank's gather buffer (peer pointers over NVLink; rows
+  // the decode pass finished are forwarded from `out` with coalesced 8-byte
+  // stores). With peer_stores set, each combine thread then fences at system
+  // scope, so the epoch a later barrier publishes orders after its stores.
+  __nv_bfloat16* outs[kMaxPeers];
+  int nouts;
+  int peer_stores;
   float* lse_out;
   float* part_o;    // [slots][hq][D]
   float* part_lse;  // [slots][hq] (log2 domain, scaled)
@@ -490,19 +500,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (writer && (d.flags & kFlagWhole)) {
         const float i0 = L0 > 0.f ? 1.f / L0 : 0.f;
         const float i1 = L1 > 0.f ? 1.f / L1 : 0.f;
-        __nv_bfloat16* ob = p.out + static_cast<long long>(d.b) * p.out_b_stride;
+        {
+          __nv_bfloat16* ob = p.out + static_cast<long long>(d.b) * p.out_b_stride;
 #pragma unroll
-        for (int mt = 0; mt < 8; ++mt) {
-          const int d0 = mt * 16 + g;
-          if (c0 < G) {
-            __nv_bfloat16* oh = ob + static_cast<long long>(h * G + c0) * p.out_h_stride;
-            oh[d0] = __float2bfloat16_rn(o[mt][0] * i0);
-            oh[d0 + 8] = __float2bfloat16_rn(o[mt][2] * i0);
-          }
-          if (c1 < G) {
-            __nv_bfloat16* oh = ob + static_cast<long long>(h * G + c1) * p.out_h_stride;
-            oh[d0] = __float2bfloat16_rn(o[mt][1] * i1);
-            oh[d0 + 8] = __float2bfloat16_rn(o[mt][3] * i1);
+          for (int mt = 0; mt < 8; ++mt) {
+            const int d0 = mt * 16 + g;
+            if (c0 < G) {
+              __nv_bfloat16* oh = ob + static_cast<long long>(h * G + c0) * p.out_h_stride;
+              oh[d0] = __float2bfloat16_rn(o[mt][0] * i0);
+              oh[d0 + 8] = __float2bfloat16_rn(o[mt][2] * i0);
+            }
+            if (c1 < G) {
+              __nv_bfloat16* oh = ob + static_cast<long long>(h * G + c1) * p.out_h_stride;
+              oh[d0] = __float2bfloat16_rn(o[mt][1] * i1);
+              oh[d0 + 8] = __float2bfloat16_rn(o[mt][3] * i1);
+            }
           }
         }
         if (p.lse_out && g == 0) {
@@ -569,64 +581,71 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
   }
   const int nb = units_of(seq_ctx(p, b), p.tc);
   const long long Gl = grid;
-  __nv_bfloat16* oh = p.out + static_cast<long long>(b) * p.out_b_stride + static_cast<long long>(hh) * p.out_h_stride +
-                      lane * 4;
+  const long long oofs = static_cast<long long>(b) * p.out_b_stride + static_cast<long long>(hh) * p.out_h_stride +
+                         lane * 4;
   float* lse = p.lse_out ? p.lse_out + static_cast<long long>(b) * p.hq + hh : nullptr;
 
   if (nb == 0) {
-    *reinterpret_cast<uint2*>(oh) = make_uint2(0u, 0u);
+    for (int r = 0; r < p.nouts; ++r) *reinterpret_cast<uint2*>(p.outs[r] + oofs) = make_uint2(0u, 0u);
     if (lse && lane == 0) *lse = NEG_INF;
-    return;
-  }
-  const long long cf = cta_of(Pb, T, Gl);
-  const long long cl = cta_of(Pb + nb - 1, T, Gl);
-  if (cf == cl) return;  // written directly by the decode kernel
-
-  float m = NEG_INF, l = 0.f;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  long long c = cf;
-  while (true) {
-    long long slots[kCombineBatch];
-    int n = 0;
-    while (n < kCombineBatch && c <= cl) {
-      const long long s0 = cta_start(c, T, Gl);
-      if (s0 == cta_start(c + 1, T, Gl)) {  // empty range (T < G): wrote nothing
-        ++c;
-        continue;
+  } else {
+    const long long cf = cta_of(Pb, T, Gl);
+    const long long cl = cta_of(Pb + nb - 1, T, Gl);
+    if (cf == cl) {  // written by the decode pass; forward it to the peers
+      if (p.peer_stores) {
+        const uint2 v = *reinterpret_cast<const uint2*>(p.out + oofs);
+        for (int r = 0; r < p.nouts; ++r)
+          if (p.outs[r] != p.out) *reinterpret_cast<uint2*>(p.outs[r] + oofs) = v;
       }
-      slots[n++] = 2 * c + (s0 >= Pb ? 0 : 1);
-      ++c;
-    }
-    if (n == 0) break;
-    float ls[kCombineBatch];
-    float4 ov[kCombineBatch];
+    } else {
+      float m = NEG_INF, l = 0.f;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      long long c = cf;
+      while (true) {
+        long long slots[kCombineBatch];
+        int n = 0;
+        while (n < kCombineBatch && c <= cl) {
+          const long long s0 = cta_start(c, T, Gl);
+          if (s0 == cta_start(c + 1, T, Gl)) {  // empty range (T < G): wrote nothing
+            ++c;
+            continue;
+          }
+          slots[n++] = 2 * c + (s0 >= Pb ? 0 : 1);
+          ++c;
+        }
+        if (n == 0) break;
+        float ls[kCombineBatch];
+        float4 ov[kCombineBatch];
 #pragma unroll
-    for (int u = 0; u < kCombineBatch; ++u) {
-      if (u < n) {
-        ls[u] = p.part_lse[slots[u] * p.hq + hh];
-        ov[u] = *reinterpret_cast<const float4*>(p.part_o + (slots[u] * p.hq + hh) * kD + lane * 4);
-      }
-    }
+        for (int u = 0; u < kCombineBatch; ++u) {
+          if (u < n) {
+            ls[u] = p.part_lse[slots[u] * p.hq + hh];
+            ov[u] = *reinterpret_cast<const float4*>(p.part_o + (slots[u] * p.hq + hh) * kD + lane * 4);
+          }
+        }
 #pragma unroll
-    for (int u = 0; u < kCombineBatch; ++u) {
-      if (u < n && ls[u] != NEG_INF) {
-        const float mn = fmaxf(m, ls[u]);
-        const float a = ex2(m - mn), w = ex2(ls[u] - mn);
-        acc[0] = acc[0] * a + w * ov[u].x;
-        acc[1] = acc[1] * a + w * ov[u].y;
-        acc[2] = acc[2] * a + w * ov[u].z;
-        acc[3] = acc[3] * a + w * ov[u].w;
-        l = l * a + w;
-        m = mn;
+        for (int u = 0; u < kCombineBatch; ++u) {
+          if (u < n && ls[u] != NEG_INF) {
+            const float mn = fmaxf(m, ls[u]);
+            const float a = ex2(m - mn), w = ex2(ls[u] - mn);
+            acc[0] = acc[0] * a + w * ov[u].x;
+            acc[1] = acc[1] * a + w * ov[u].y;
+            acc[2] = acc[2] * a + w * ov[u].z;
+            acc[3] = acc[3] * a + w * ov[u].w;
+            l = l * a + w;
+            m = mn;
+          }
+        }
       }
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint2 v;
+      v.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+      v.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+      for (int r = 0; r < p.nouts; ++r) *reinterpret_cast<uint2*>(p.outs[r] + oofs) = v;
+      if (lse && lane == 0) *lse = l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
     }
   }
-  const float inv = l > 0.f ? 1.f / l : 0.f;
-  uint2 v;
-  v.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
-  v.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
-  *reinterpret_cast<uint2*>(oh) = v;
-  if (lse && lane == 0) *lse = l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
+  if (p.peer_stores) __threadfence_system();
 }
 
 // ------------------------------------------------------------------ host
@@ -678,16 +697,23 @@ extern "C" int la_paged_decode_workspace_size(int device, int num_q_heads, int n
   return LA_OK;
 }
 
-extern "C" int la_paged_decode(const void* q, int64_t q_batch_stride, int64_t q_head_stride, const void* k_cache,
-                               const void* v_cache, int64_t kv_block_stride, int64_t kv_token_stride,
-                               int64_t kv_head_stride, int64_t num_blocks, int block_size,
-                               const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
-                               const int32_t* cache_seqlens, int batch, int num_q_heads, int num_kv_heads,
-                               int head_dim, float softmax_scale, void* out, int64_t out_batch_stride,
-                               int64_t out_head_stride, float* softmax_lse, void* workspace,
-                               size_t workspace_bytes, int* dev_error, cudaStream_t stream) {
-  using namespace la;
-  using namespace la::decode;
+namespace la {
+namespace decode {
+
+// Peer outputs of the KV-head-sharded all-gather (nullptr: local output only).
+struct PeerOut {
+  void* const* outs;  // [npeers] gather buffers, rank order (own included)
+  int npeers;
+};
+
+static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_head_stride, const void* k_cache,
+                             const void* v_cache, int64_t kv_block_stride, int64_t kv_token_stride,
+                             int64_t kv_head_stride, int64_t num_blocks, int block_size,
+                             const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
+                             const int32_t* cache_seqlens, int batch, int num_q_heads, int num_kv_heads,
+                             int head_dim, float softmax_scale, void* out, int64_t out_batch_stride,
+                             int64_t out_head_stride, float* softmax_lse, void* workspace, size_t workspace_bytes,
+                             int* dev_error, cudaStream_t stream, const PeerOut* peers) {
   if (!q || !k_cache || !v_cache || !block_table || !cache_seqlens || !out) return LA_ERR_INVALID_ARGUMENT;
   if (batch < 0 || num_blocks <= 0 || block_size <= 0 || max_blocks_per_seq <= 0) return LA_ERR_INVALID_ARGUMENT;
   if (batch == 0) return LA_OK;
@@ -765,6 +791,18 @@ extern "C" int la_paged_decode(const void* q, int64_t q_batch_stride, int64_t q_
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_b_stride = out_batch_stride;
   p.out_h_stride = out_head_stride;
+  p.nouts = 1;
+  p.outs[0] = p.out;
+  p.peer_stores = 0;
+  if (peers) {
+    if (peers->npeers < 1 || peers->npeers > kMaxPeers || !peers->outs) return LA_ERR_INVALID_ARGUMENT;
+    p.nouts = peers->npeers;
+    for (int r = 0; r < peers->npeers; ++r) {
+      if (!peers->outs[r] || !aligned(peers->outs[r], 8)) return LA_ERR_INVALID_ARGUMENT;
+      p.outs[r] = static_cast<__nv_bfloat16*>(peers->outs[r]);
+    }
+    p.peer_stores = 1;
+  }
   p.lse_out = softmax_lse;
   const size_t slots = static_cast<size_t>(2) * grid;
   const size_t o_bytes = (slots * num_q_heads * kD * sizeof(float) + 255) & ~size_t(255);
@@ -788,4 +826,48 @@ extern "C" int la_paged_decode(const void* q, int64_t q_batch_stride, int64_t q_
   if (e != cudaSuccess) return cuda_status(e);
   e = launch_pdl(paged_decode_combine_kernel, dim3(batch, num_q_heads), dim3(32), 0, stream, p, grid);
   return cuda_status(e);
+}
+
+}  // namespace decode
+}  // namespace la
+
+extern "C" int la_paged_decode(const void* q, int64_t q_batch_stride, int64_t q_head_stride, const void* k_cache,
+                               const void* v_cache, int64_t kv_block_stride, int64_t kv_token_stride,
+                               int64_t kv_head_stride, int64_t num_blocks, int block_size,
+                               const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
+                               const int32_t* cache_seqlens, int batch, int num_q_heads, int num_kv_heads,
+                               int head_dim, float softmax_scale, void* out, int64_t out_batch_stride,
+                               int64_t out_head_stride, float* softmax_lse, void* workspace,
+                               size_t workspace_bytes, int* dev_error, cudaStream_t stream) {
+  return la::decode::paged_decode_impl(q, q_batch_stride, q_head_stride, k_cache, v_cache, kv_block_stride,
+                                       kv_token_stride, kv_head_stride, num_blocks, block_size, block_table,
+                                       bt_seq_stride, max_blocks_per_seq, cache_seqlens, batch, num_q_heads,
+                                       num_kv_heads, head_dim, softmax_scale, out, out_batch_stride, out_head_stride,
+                                       softmax_lse, workspace, workspace_bytes, dev_error, stream, nullptr);
+}
+
+extern "C" int la_paged_decode_allgather(
+    const void* q, int64_t q_batch_stride, int64_t q_head_stride, const void* k_cache, const void* v_cache,
+    int64_t kv_block_stride, int64_t kv_token_stride, int64_t kv_head_stride, int64_t num_blocks, int block_size,
+    const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq, const int32_t* cache_seqlens,
+    int batch, int num_q_heads, int num_kv_heads, int head_dim, float softmax_scale, void* const* gather_bufs,
+    int64_t out_batch_stride, int64_t out_head_stride, int rank, int world, void* workspace,
+    size_t workspace_bytes, int* dev_error, cudaStream_t stream) {
+  if (!gather_bufs || world < 1 || world > la::decode::kMaxPeers || rank < 0 || rank >= world)
+    return LA_ERR_INVALID_ARGUMENT;
+  // This rank's query heads sit at [rank * Hq_local, (rank + 1) * Hq_local) of
+  // every gather buffer.
+  void* outs[la::decode::kMaxPeers];
+  const int64_t head0 = static_cast<int64_t>(rank) * num_q_heads * out_head_stride;
+  for (int r = 0; r < world; ++r) {
+    if (!gather_bufs[r]) return LA_ERR_INVALID_ARGUMENT;
+    outs[r] = static_cast<__nv_bfloat16*>(gather_bufs[r]) + head0;
+  }
+  la::decode::PeerOut peers{outs, world};
+  return la::decode::paged_decode_impl(q, q_batch_stride, q_head_stride, k_cache, v_cache, kv_block_stride,
+                                       kv_token_stride, kv_head_stride, num_blocks, block_size, block_table,
+                                       bt_seq_stride, max_blocks_per_seq, cache_seqlens, batch, num_q_heads,
+                                       num_kv_heads, head_dim, softmax_scale, outs[rank], out_batch_stride,
+                                       out_head_stride, nullptr, workspace, workspace_bytes, dev_error, stream,
+                                       &peers);
 }

@@ -108,3 +108,119 @@ def shard_pool(k_cache: torch.Tensor, v_cache: torch.Tensor, shard: HeadShard):
     (contiguous copies, as a rank would hold them)."""
     return (k_cache[:, :, shard.kv_lo:shard.kv_hi].contiguous(),
             v_cache[:, :, shard.kv_lo:shard.kv_hi].contiguous())
+
+
+class _CudaBuffer:
+    """A device pointer exposed through __cuda_array_interface__ (int16 words)."""
+
+    def __init__(self, ptr: int, n_words: int):
+        self.__cuda_array_interface__ = {"shape": (n_words,), "typestr": "<i2", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class NVLinkAllGatherDecode:
+    """KV-head-sharded decode with the all-gather fused into the decode
+    kernels: every rank's decode/combine kernels store its heads' outputs
+    straight into every rank's gather buffer over NVLink (CUDA IPC peer
+    mappings); a one-warp device barrier on the same stream (publish this
+    rank's epoch, wait bounded for the peers') makes the gathered
+    [B, 1, Hq, D] output safe to read. No NCCL call and no copy kernel.
+
+    The gather buffer has `slots` slots used in turn (slot = call index mod
+    slots, chosen by the caller, e.g. layer index mod 2): a peer may already
+    be writing call n+1 while this rank still reads call n.
+    """
+
+    SIG_BYTES = 256
+
+    def __init__(self, shard: HeadShard, max_batch: int, group=None, slots: int = 2, head_dim: int = 128):
+        import ctypes
+
+        import torch.distributed as dist
+
+        from . import _lib
+
+        self._ct = ctypes
+        self._lib = _lib
+        self.shard, self.group, self.slots = shard, group, slots
+        self.P, self.rank = shard.world, shard.rank
+        self.hq_total = shard.num_q_heads * shard.world
+        self.D = head_dim
+        self.max_batch = max_batch
+        slot_elems = max_batch * self.hq_total * head_dim
+        self.slot_bytes = (slot_elems * 2 + 255) // 256 * 256
+        nbytes = self.SIG_BYTES + slots * self.slot_bytes
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        _lib.call("la_p2p_alloc", nbytes, ctypes.byref(ptr), handle)
+        self._own = ptr
+        handles = [None] * self.P
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        bases = []
+        for r in range(self.P):
+            if r == self.rank:
+                bases.append(ptr.value)
+            else:
+                pp = ctypes.c_void_p()
+                _lib.call("la_p2p_open", ctypes.create_string_buffer(handles[r], 64), ctypes.byref(pp))
+                self._opened.append(pp)
+                bases.append(pp.value)
+        self._bases = bases
+        self._signals = (ctypes.c_void_p * self.P)(*bases)
+        self._slot_ptrs = [(ctypes.c_void_p * self.P)(*[b + self.SIG_BYTES + s * self.slot_bytes for b in bases])
+                           for s in range(slots)]
+        words = torch.as_tensor(_CudaBuffer(ptr.value + self.SIG_BYTES, slots * self.slot_bytes // 2),
+                                device=torch.device("cuda", torch.cuda.current_device()))
+        per = self.slot_bytes // 2
+        self.local = [words[s * per: s * per + slot_elems].view(torch.bfloat16).view(max_batch, self.hq_total, head_dim)
+                      for s in range(slots)]
+        self._ws = None
+
+    def __call__(self, q_local: torch.Tensor, k_cache_local: torch.Tensor, v_cache_local: torch.Tensor,
+                 cache_seqlens: torch.Tensor, block_table: torch.Tensor, slot: int = 0,
+                 softmax_scale: Optional[float] = None) -> torch.Tensor:
+        """q_local [B, 1, Hq/P, D] -> gathered [B, 1, Hq, D] (a view of this
+        rank's gather slot, valid until the slot is reused)."""
+        from . import flash_attn_interface as fai
+
+        ct, lib = self._ct, self._lib
+        B, _, hq, D = q_local.shape
+        if B > self.max_batch or hq != self.shard.num_q_heads or D != self.D:
+            raise RuntimeError("q_local does not match the gather buffer")
+        dev = q_local.device.index
+        fai.ensure_init(dev)
+        need = fai.decode_workspace_bytes(dev, hq, k_cache_local.shape[2], D)
+        ws = fai._workspace(dev, need)
+        err = fai.error_word(dev)
+        stream = ct.c_void_p(torch.cuda.current_stream(q_local.device).cuda_stream)
+        scale = D ** -0.5 if softmax_scale is None else float(softmax_scale)
+        kc = k_cache_local
+        lib.call("la_paged_decode_allgather",
+                 ct.c_void_p(q_local.data_ptr()), q_local.stride(0), q_local.stride(2),
+                 ct.c_void_p(kc.data_ptr()), ct.c_void_p(v_cache_local.data_ptr()),
+                 kc.stride(0), kc.stride(1), kc.stride(2), kc.shape[0], kc.shape[1],
+                 ct.c_void_p(block_table.data_ptr()), block_table.stride(0), block_table.shape[1],
+                 ct.c_void_p(cache_seqlens.data_ptr()),
+                 B, hq, kc.shape[2], D, ct.c_float(scale),
+                 self._slot_ptrs[slot], self.hq_total * D, D,
+                 self.rank, self.P,
+                 ct.c_void_p(ws.data_ptr()), ws.numel(),
+                 ct.c_void_p(err.data_ptr()), stream)
+        lib.call("la_p2p_barrier", self._signals, self.P, self.rank, ct.c_void_p(err.data_ptr()), stream)
+        return self.local[slot][:B].view(B, 1, self.hq_total, D)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective)."""
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for pp in self._opened:
+            self._lib.call("la_p2p_close", pp)
+        self._opened = []
+        dist.barrier(group=self.group)
+        self.local = []
+        if self._own is not None:
+            self._lib.call("la_p2p_free", self._own)
+            self._own = None
