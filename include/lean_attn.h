@@ -259,6 +259,39 @@ int la_prefill_varlen(
     float* softmax_lse,
     int* dev_error, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Chunked prefill over the paged cache (kernel (c) with paged keys).
+ * Replaces flash_attn_with_kvcache with q_len > 1 at its call site
+ * (leaninfer/qwen3/model.py:60-67; the chunked prefill of README.md:112-124)
+ * and flash-attn's varlen call with a block_table.
+ *
+ * Sequence s has queries at packed rows [cu_seqlens_q[s], cu_seqlens_q[s+1])
+ * of q [total_q, Hq, D] — or, with cu_seqlens_q == NULL, q_len queries at rows
+ * [s*q_len, (s+1)*q_len) (total_q = num_seqs*q_len; max_seqlen_q ignored) —
+ * and cache_seqlens[s] keys in the pool [num_blocks, block_size, Hkv, D]
+ * through block_table row s (the chunk's own keys already written there, e.g.
+ * by la_qk_norm_rope_paged_write). Causal masking is bottom-right aligned:
+ * query i of n sees key j iff j <= i + cache_seqlens[s] - n; a row that sees
+ * no key is written as zeros (lse -inf). block_size: a multiple of 64, or 16
+ * or 32. Pool slots past a sequence's last key are never used (they may hold
+ * anything, NaN included). out [total_q, Hq, D]; softmax_lse (nullable)
+ * [Hq, total_q], natural log. Block ids outside [0, num_blocks) and keys past
+ * the block table are reported on dev_error and read as zeros.
+ * ------------------------------------------------------------------------ */
+int la_prefill_paged(
+    const void* q, int64_t q_token_stride, int64_t q_head_stride,
+    const void* k_cache, const void* v_cache,
+    int64_t kv_block_stride, int64_t kv_token_stride, int64_t kv_head_stride,
+    int64_t num_blocks, int block_size,
+    const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
+    const int32_t* cache_seqlens,
+    const int32_t* cu_seqlens_q, int q_len, int num_seqs, int max_seqlen_q, int64_t total_q,
+    int num_q_heads, int num_kv_heads, int head_dim,
+    float softmax_scale, int causal,
+    void* out, int64_t out_token_stride, int64_t out_head_stride,
+    float* softmax_lse,
+    int* dev_error, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

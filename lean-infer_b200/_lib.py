@@ -121,6 +121,20 @@ _SIGNATURES = {
         c_void_p,
         c_void_p, c_void_p,
     ],
+    "la_prefill_paged": [
+        c_void_p, c_int64, c_int64,
+        c_void_p, c_void_p,
+        c_int64, c_int64, c_int64,
+        c_int64, c_int,
+        c_void_p, c_int64, c_int,
+        c_void_p,
+        c_void_p, c_int, c_int, c_int, c_int64,
+        c_int, c_int, c_int,
+        c_float, c_int,
+        c_void_p, c_int64, c_int64,
+        c_void_p,
+        c_void_p, c_void_p,
+    ],
 }
 
 _lib = None

@@ -60,7 +60,8 @@ constexpr int kBarOffset = kQTile + 4 * kKVTile + kPTile;  // 112 KB
 constexpr size_t kSmemBytes = kBarOffset + 256;
 
 struct Params {
-  const int* cu;
+  const int* cu;  // query starts [num_seqs + 1], or null: sequence s has q_len queries from token s * q_len
+  int q_len;
   int num_seqs;
   int n_qt;  // query tiles of the longest sequence
   int tq;    // tokens per query tile (128 / group)
@@ -72,6 +73,19 @@ struct Params {
   float* lse;  // [hq, total] natural log, or null
   long long total;
   int* err;
+  // Keys. Contiguous (paged == 0): the sequence's own tokens, at the same
+  // packed rows as its queries. Paged: k_lens[s] keys of sequence s in the
+  // pool [num_blocks, bs, hkv, D] through block-table row s; causal masking
+  // is then bottom-right aligned (query i sees key j iff
+  // j <= i + k_lens[s] - q_count).
+  int paged;
+  const int* k_lens;
+  const int* bt;
+  long long bt_stride;
+  int max_blocks;
+  int bs;         // block size
+  int box_keys;   // keys per TMA box: min(bs, kKeys)
+  int num_blocks;
 };
 
 // K-major operand of 128-byte SW128 rows whose 128-wide reduction dimension is
@@ -97,6 +111,7 @@ __device__ __forceinline__ uint64_t desc_v(const uint8_t* tile, int ks) {
 // exchanged between roles.
 struct Item {
   int s, h, q0, seq0, L, n_kv;
+  int K, off;  // keys of the sequence; causal offset K - L (0 for contiguous keys)
 };
 
 struct Walker {
@@ -106,8 +121,11 @@ struct Walker {
   int count;       // items at `level`
 };
 
+__device__ __forceinline__ int q_start(const Params& p, int s) { return p.cu ? p.cu[s] : s * p.q_len; }
+__device__ __forceinline__ int q_count(const Params& p, int s) { return p.cu ? p.cu[s + 1] - p.cu[s] : p.q_len; }
+
 __device__ __forceinline__ bool seq_has_tile(const Params& p, int s, int q0) {
-  return s < p.num_seqs && (p.cu[s + 1] - p.cu[s]) > q0;
+  return s < p.num_seqs && q_count(p, s) > q0;
 }
 
 // Items at one level (warp-collective).
@@ -155,11 +173,15 @@ __device__ bool walker_next(const Params& p, Walker& w, Item& it) {
   }
   it.s = s;
   it.h = idx - ord * p.hkv;
-  it.seq0 = p.cu[s];
-  it.L = p.cu[s + 1] - it.seq0;
+  it.seq0 = q_start(p, s);
+  it.L = q_count(p, s);
+  it.K = p.paged ? max(p.k_lens[s], 0) : it.L;
+  it.off = it.K - it.L;
   it.q0 = q0;
-  const int kv_end = p.causal ? min(q0 + p.tq, it.L) : it.L;
-  it.n_kv = (kv_end + kKeys - 1) / kKeys;
+  const int kv_end = p.causal ? min(q0 + p.tq + it.off, it.K) : it.K;
+  // At least one tile, so every item runs the same pipeline (rows that see
+  // no key come out as zeros).
+  it.n_kv = max((kv_end + kKeys - 1) / kKeys, 1);
   ++w.taken;
   return true;
 }
@@ -249,6 +271,36 @@ __global__ void __launch_bounds__(kThreads, 2)
     auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
     };
+    // One 64-key K or V tile (both 64-dim halves) of item `it`, tile j. Paged:
+    // one box per run of box_keys keys, through the block table; keys at or
+    // past the sequence's end, and ids outside the table or the pool (also
+    // reported), load from block `num_blocks`, outside the tensor map, which
+    // the copy engine fills with zeros. Either way the full tile's bytes land.
+    auto load_kv = [&](uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, const Item& it, int j) {
+      if (!p.paged) {
+        for (int half = 0; half < 2; ++half)
+          tma_load_3d(dst + half * kKVHalf, tm, bar, half * 64, it.h, it.seq0 + j * kKeys);
+        return;
+      }
+      for (int b = 0; b < kKeys; b += p.box_keys) {
+        const int key = j * kKeys + b;
+        const int lb = key / p.bs;
+        int blk = p.num_blocks;
+        if (key < it.K) {
+          if (lb >= p.max_blocks) {
+            if (p.err) atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
+          } else {
+            const int id = __ldg(p.bt + static_cast<long long>(it.s) * p.bt_stride + lb);
+            if (id >= 0 && id < p.num_blocks)
+              blk = id;
+            else if (p.err)
+              atomicCAS(p.err, 0, LA_DEVERR_BLOCK_ID);
+          }
+        }
+        for (int half = 0; half < 2; ++half)
+          tma_load_4d(dst + half * kKVHalf + b * 128, tm, bar, half * 64, key - lb * p.bs, it.h, blk);
+      }
+    };
     // Issue K tile tk (loading the item's Q first when it is the item's first tile).
     auto issue_k = [&]() -> bool {
       if (jk == 0) {
@@ -269,8 +321,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!wait_all(&k_empty[st], ((tk >> 1) & 1) ^ 1u)) return false;
       if (lane == 0) {
         mbar_arrive_expect_tx(&k_full[st], kKVTile);
-        for (int half = 0; half < 2; ++half)
-          tma_load_3d(sK + st * kKVTile + half * kKVHalf, &tm_k, &k_full[st], half * 64, ik.h, ik.seq0 + jk * kKeys);
+        load_kv(sK + st * kKVTile, &tm_k, &k_full[st], ik, jk);
       }
       ++tk;
       if (++jk == ik.n_kv) {
@@ -284,8 +335,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (!wait_all(&v_empty[st], ((tv >> 1) & 1) ^ 1u)) return false;
       if (lane == 0) {
         mbar_arrive_expect_tx(&v_full[st], kKVTile);
-        for (int half = 0; half < 2; ++half)
-          tma_load_3d(sV + st * kKVTile + half * kKVHalf, &tm_v, &v_full[st], half * 64, iv.h, iv.seq0 + jv * kKeys);
+        load_kv(sV + st * kKVTile, &tm_v, &v_full[st], iv, jv);
       }
       ++tv;
       if (++jv == iv.n_kv) {
@@ -317,6 +367,20 @@ __global__ void __launch_bounds__(kThreads, 2)
     auto pv = [&](int u, int ju, int kk) -> bool {  // O += P V for global tile u (item-local ju)
       if (!wait_all(p_full, u & 1) || !wait_all(&v_full[u & 1], (u >> 1) & 1)) return false;
       if (ju == 0 && kk >= 1 && !wait_all(o_empty, (kk - 1) & 1)) return false;
+      const int vrows = it.K - ju * kKeys;  // valid V rows of this tile
+      if (p.paged && vrows < kKeys) {
+        // Pool slots past the sequence's last key hold whatever was there
+        // (possibly NaN); P is 0 for them but 0 * NaN is not, so zero them.
+        uint8_t* vt = sV + (u & 1) * kKVTile;
+        const int r0 = max(vrows, 0);
+        const int n16 = (kKeys - r0) * 8;  // 16-byte chunks per half
+        for (int i = lane; i < 2 * n16; i += 32) {
+          const int half = i / n16, c = i - half * n16;
+          *reinterpret_cast<uint4*>(vt + half * kKVHalf + r0 * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
       tc_fence_after();
       if (lane == 0) {
         const uint8_t* vt = sV + (u & 1) * kKVTile;
@@ -369,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     bool ok = true;
     while (ok && walker_next(p, w, it)) {
       const int tok = it.q0 + (row - g * p.tq);  // token index within the sequence
-      const int lim = p.causal ? min(tok + 1, it.L) : it.L;  // keys [0, lim) are visible
+      const int lim = p.causal ? min(max(tok + 1 + it.off, 0), it.K) : it.K;  // keys [0, lim) are visible
       float m = NEG_INF, l = 0.f;
       for (int j = 0; j < it.n_kv; ++j, ++t) {
         const int sb = t & 1;
@@ -411,8 +475,11 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
                                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
         const float m_new = (mt > m + 8.f) ? mt : m;
-        const float alpha = ex2(m - m_new);  // 0 on the first tile, 1 when m is kept
-        const float neg_m = -m_new;
+        // A row that has seen no key yet keeps m = -inf: use 0 as its
+        // reference so P and alpha come out 0 instead of NaN.
+        const float m_ref = (m_new == NEG_INF) ? 0.f : m_new;
+        const float alpha = ex2(m - m_ref);  // 0 on the first tile, 1 when m is kept
+        const float neg_m = -m_ref;
         float ps[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) ps[a] = 0.f;
@@ -518,6 +585,61 @@ int prefill_init(int device) {
 
 }  // namespace la
 
+namespace la {
+namespace prefill {
+
+// Common tail of the two entry points: the persistent grid over the items.
+static int launch(const CUtensorMap& tq_map, const CUtensorMap& tk_map, const CUtensorMap& tv_map, const Params& p,
+                  cudaStream_t stream) {
+  const long long items = static_cast<long long>(p.n_qt) * p.num_seqs * p.hkv;
+  if (items > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
+  const int device = current_device();
+  const int sms = device >= 0 ? num_sms(device) : 0;
+  if (sms <= 0) return LA_ERR_CUDA;
+  // Two CTAs per SM by design (registers, shared memory and TMEM are sized
+  // for it); if fewer fit, the extra CTAs simply run as a second wave.
+  const long long ctas = static_cast<long long>(sms) * 2;
+  const dim3 grid(static_cast<unsigned>(items < ctas ? items : ctas));  // persistent
+  return cuda_status(launch_pdl(prefill_kernel, grid, dim3(kThreads), kSmemBytes, stream, tq_map, tk_map, tv_map, p));
+}
+
+// Q map [total, Hq, D] with a (64 dims, 1 head, tq tokens) box, and the
+// checks shared by both entry points.
+static int common_setup(const void* q, int64_t q_token_stride, int64_t q_head_stride, int64_t total_tokens,
+                        int num_q_heads, int num_kv_heads, int head_dim, float softmax_scale, void* out,
+                        int64_t out_token_stride, int64_t out_head_stride, CUtensorMap* tq_map, Params* p) {
+  if (head_dim != kD) return LA_ERR_UNSUPPORTED;
+  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return LA_ERR_INVALID_ARGUMENT;
+  const int group = num_q_heads / num_kv_heads;
+  if (group != 1 && group != 2 && group != 4 && group != 8) return LA_ERR_UNSUPPORTED;
+  if (!(softmax_scale > 0.f)) return LA_ERR_INVALID_ARGUMENT;
+  if (total_tokens > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
+  if (!aligned(q, 16) || !aligned(out, 16)) return LA_ERR_ALIGNMENT;
+  const long long st[] = {q_token_stride, q_head_stride, out_token_stride, out_head_stride};
+  for (long long x : st)
+    if (x <= 0 || x % 8) return LA_ERR_ALIGNMENT;
+  const int tq = kRows / group;
+  const uint64_t dims[3] = {128, static_cast<uint64_t>(num_q_heads), static_cast<uint64_t>(total_tokens)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(q_head_stride) * 2, static_cast<uint64_t>(q_token_stride) * 2};
+  const uint32_t box[3] = {64, 1, static_cast<uint32_t>(tq)};
+  const int stt = encode_tensor_map_bf16(tq_map, q, 3, dims, strides, box, true);
+  if (stt != LA_OK) return stt;
+  *p = Params{};
+  p->tq = tq;
+  p->hq = num_q_heads;
+  p->hkv = num_kv_heads;
+  p->group = group;
+  p->scale_log2 = softmax_scale * 1.4426950408889634f;
+  p->out = static_cast<__nv_bfloat16*>(out);
+  p->out_ts = out_token_stride;
+  p->out_hs = out_head_stride;
+  p->total = total_tokens;
+  return LA_OK;
+}
+
+}  // namespace prefill
+}  // namespace la
+
 extern "C" int la_prefill_varlen(const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k,
                                  int64_t k_token_stride, int64_t k_head_stride, const void* v, int64_t v_token_stride,
                                  int64_t v_head_stride, const int32_t* cu_seqlens, int num_seqs, int max_seqlen,
@@ -529,27 +651,15 @@ extern "C" int la_prefill_varlen(const void* q, int64_t q_token_stride, int64_t 
   if (!q || !k || !v || !cu_seqlens || !out) return LA_ERR_INVALID_ARGUMENT;
   if (num_seqs < 0 || max_seqlen < 0 || total_tokens < 0) return LA_ERR_INVALID_ARGUMENT;
   if (num_seqs == 0 || max_seqlen == 0 || total_tokens == 0) return LA_OK;
-  if (head_dim != kD) return LA_ERR_UNSUPPORTED;
-  if (num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return LA_ERR_INVALID_ARGUMENT;
-  const int group = num_q_heads / num_kv_heads;
-  if (group != 1 && group != 2 && group != 4 && group != 8) return LA_ERR_UNSUPPORTED;
-  if (!(softmax_scale > 0.f)) return LA_ERR_INVALID_ARGUMENT;
-  if (total_tokens > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
-  if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16)) return LA_ERR_ALIGNMENT;
-  const long long st[] = {q_token_stride, q_head_stride, k_token_stride, k_head_stride, v_token_stride, v_head_stride,
-                          out_token_stride, out_head_stride};
-  for (long long x : st)
+  if (!aligned(k, 16) || !aligned(v, 16)) return LA_ERR_ALIGNMENT;
+  const long long kst[] = {k_token_stride, k_head_stride, v_token_stride, v_head_stride};
+  for (long long x : kst)
     if (x <= 0 || x % 8) return LA_ERR_ALIGNMENT;
-
-  const int tq = kRows / group;
   CUtensorMap tq_map, tk_map, tv_map;
-  int stt;
-  {
-    const uint64_t dims[3] = {128, static_cast<uint64_t>(num_q_heads), static_cast<uint64_t>(total_tokens)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(q_head_stride) * 2, static_cast<uint64_t>(q_token_stride) * 2};
-    const uint32_t box[3] = {64, 1, static_cast<uint32_t>(tq)};
-    if ((stt = encode_tensor_map_bf16(&tq_map, q, 3, dims, strides, box, true)) != LA_OK) return stt;
-  }
+  Params p;
+  int stt = common_setup(q, q_token_stride, q_head_stride, total_tokens, num_q_heads, num_kv_heads, head_dim,
+                         softmax_scale, out, out_token_stride, out_head_stride, &tq_map, &p);
+  if (stt != LA_OK) return stt;
   {
     const uint64_t dims[3] = {128, static_cast<uint64_t>(num_kv_heads), static_cast<uint64_t>(total_tokens)};
     const uint32_t box[3] = {64, 1, static_cast<uint32_t>(kKeys)};
@@ -558,30 +668,73 @@ extern "C" int la_prefill_varlen(const void* q, int64_t q_token_stride, int64_t 
     if ((stt = encode_tensor_map_bf16(&tk_map, k, 3, dims, ks, box, true)) != LA_OK) return stt;
     if ((stt = encode_tensor_map_bf16(&tv_map, v, 3, dims, vs, box, true)) != LA_OK) return stt;
   }
-  Params p;
   p.cu = cu_seqlens;
   p.num_seqs = num_seqs;
-  p.tq = tq;
-  p.n_qt = (max_seqlen + tq - 1) / tq;
-  p.hq = num_q_heads;
-  p.hkv = num_kv_heads;
-  p.group = group;
+  p.n_qt = (max_seqlen + p.tq - 1) / p.tq;
   p.causal = causal ? 1 : 0;
-  p.scale_log2 = softmax_scale * 1.4426950408889634f;
-  p.out = static_cast<__nv_bfloat16*>(out);
-  p.out_ts = out_token_stride;
-  p.out_hs = out_head_stride;
   p.lse = softmax_lse;
-  p.total = total_tokens;
   p.err = dev_error;
-  const long long items = static_cast<long long>(p.n_qt) * num_seqs * num_kv_heads;
-  if (items > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
-  const int device = current_device();
-  const int sms = device >= 0 ? num_sms(device) : 0;
-  if (sms <= 0) return LA_ERR_CUDA;
-  // Two CTAs per SM by design (registers, shared memory and TMEM are sized
-  // for it); if fewer fit, the extra CTAs simply run as a second wave.
-  const long long ctas = static_cast<long long>(sms) * 2;
-  const dim3 grid(static_cast<unsigned>(items < ctas ? items : ctas));  // persistent
-  return cuda_status(launch_pdl(prefill_kernel, grid, dim3(kThreads), kSmemBytes, stream, tq_map, tk_map, tv_map, p));
+  return launch(tq_map, tk_map, tv_map, p, stream);
+}
+
+extern "C" int la_prefill_paged(const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k_cache,
+                                const void* v_cache, int64_t kv_block_stride, int64_t kv_token_stride,
+                                int64_t kv_head_stride, int64_t num_blocks, int block_size,
+                                const int32_t* block_table, int64_t bt_seq_stride, int max_blocks_per_seq,
+                                const int32_t* cache_seqlens, const int32_t* cu_seqlens_q, int q_len, int num_seqs,
+                                int max_seqlen_q, int64_t total_q, int num_q_heads, int num_kv_heads, int head_dim,
+                                float softmax_scale, int causal, void* out, int64_t out_token_stride,
+                                int64_t out_head_stride, float* softmax_lse, int* dev_error, cudaStream_t stream) {
+  using namespace la;
+  using namespace la::prefill;
+  if (!q || !k_cache || !v_cache || !block_table || !cache_seqlens || !out) return LA_ERR_INVALID_ARGUMENT;
+  if (num_seqs < 0 || total_q < 0 || num_blocks <= 0 || max_blocks_per_seq <= 0 || bt_seq_stride < 0)
+    return LA_ERR_INVALID_ARGUMENT;
+  if (cu_seqlens_q) {
+    if (max_seqlen_q < 0) return LA_ERR_INVALID_ARGUMENT;
+  } else {
+    if (q_len < 0 || total_q != static_cast<int64_t>(q_len) * num_seqs) return LA_ERR_INVALID_ARGUMENT;
+    max_seqlen_q = q_len;
+  }
+  if (num_seqs == 0 || max_seqlen_q == 0 || total_q == 0) return LA_OK;
+  if (num_blocks > 0x7ffffffeLL) return LA_ERR_UNSUPPORTED;
+  // 64-key tiles must not straddle blocks, or be whole blocks of 16 / 32.
+  if (block_size <= 0 || block_size % 16 || (block_size % kKeys && kKeys % block_size)) return LA_ERR_UNSUPPORTED;
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return LA_ERR_ALIGNMENT;
+  const long long kst[] = {kv_block_stride, kv_token_stride, kv_head_stride};
+  for (long long x : kst)
+    if (x <= 0 || x % 8) return LA_ERR_ALIGNMENT;
+  CUtensorMap tq_map, tk_map, tv_map;
+  Params p;
+  int stt = common_setup(q, q_token_stride, q_head_stride, total_q, num_q_heads, num_kv_heads, head_dim,
+                         softmax_scale, out, out_token_stride, out_head_stride, &tq_map, &p);
+  if (stt != LA_OK) return stt;
+  const int box_keys = block_size < kKeys ? block_size : kKeys;
+  {
+    // Pool [NB, BS, Hkv, D] as a 4-D map (D, BS, Hkv, NB): one box is
+    // (64 dims, box_keys tokens, 1 head, 1 block).
+    const uint64_t dims[4] = {128, static_cast<uint64_t>(block_size), static_cast<uint64_t>(num_kv_heads),
+                              static_cast<uint64_t>(num_blocks)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(kv_token_stride) * 2, static_cast<uint64_t>(kv_head_stride) * 2,
+                                 static_cast<uint64_t>(kv_block_stride) * 2};
+    const uint32_t box[4] = {64, static_cast<uint32_t>(box_keys), 1, 1};
+    if ((stt = encode_tensor_map_bf16(&tk_map, k_cache, 4, dims, strides, box, true)) != LA_OK) return stt;
+    if ((stt = encode_tensor_map_bf16(&tv_map, v_cache, 4, dims, strides, box, true)) != LA_OK) return stt;
+  }
+  p.cu = cu_seqlens_q;
+  p.q_len = q_len;
+  p.num_seqs = num_seqs;
+  p.n_qt = (max_seqlen_q + p.tq - 1) / p.tq;
+  p.causal = causal ? 1 : 0;
+  p.lse = softmax_lse;
+  p.err = dev_error;
+  p.paged = 1;
+  p.k_lens = cache_seqlens;
+  p.bt = block_table;
+  p.bt_stride = bt_seq_stride;
+  p.max_blocks = max_blocks_per_seq;
+  p.bs = block_size;
+  p.box_keys = box_keys;
+  p.num_blocks = static_cast<int>(num_blocks);
+  return launch(tq_map, tk_map, tv_map, p, stream);
 }

@@ -131,12 +131,18 @@ def flash_attn_with_kvcache(
     num_splits: int = 0,
     return_softmax_lse: bool = False,
 ):
-    """Paged GQA decode attention (one query token per sequence).
+    """Paged GQA attention over the KV cache.
 
-    q: [B, 1, Hq, D] bf16. k_cache / v_cache: [num_blocks, block_size, Hkv, D]
+    One query token per sequence (decode, q [B, 1, Hq, D]) runs the split-KV
+    decode kernel. q_len > 1 (chunked prefill, q [B, Sq, Hq, D], the chunk's
+    keys already in the cache) runs the tcgen05 prefill kernel over the paged
+    keys, causal masking bottom-right aligned (query i sees keys
+    0..cache_seqlens[b] - Sq + i); block_size then a multiple of 64, or 16/32.
+
+    q: [B, Sq, Hq, D] bf16. k_cache / v_cache: [num_blocks, block_size, Hkv, D]
     bf16 with block_table [B, max_blocks] int32, or [B, S, Hkv, D] without a
     block table. cache_seqlens: [B] int32 (or an int for all rows).
-    Returns out [B, 1, Hq, D] (and softmax_lse [B, Hq, 1] fp32 when asked).
+    Returns out [B, Sq, Hq, D] (and softmax_lse [B, Hq, Sq] fp32 when asked).
 
     causal is accepted and has no effect at one query token (bottom-right
     alignment lets the query see all cache_seqlens[b] keys). num_splits is a
@@ -154,8 +160,6 @@ def flash_attn_with_kvcache(
         raise NotImplementedError("sliding window / softcap / alibi")
     _check(q.dim() == 4, "q must be [batch, seqlen_q, num_heads, head_dim]")
     B, Sq, Hq, D = q.shape
-    if Sq != 1:
-        raise NotImplementedError("paged decode takes one query token per sequence (seqlen_q == 1)")
     _check(q.dtype == torch.bfloat16 and k_cache.dtype == torch.bfloat16 and v_cache.dtype == torch.bfloat16,
            "q, k_cache and v_cache must be bfloat16")
     _check(k_cache.shape == v_cache.shape and k_cache.stride() == v_cache.stride(),
@@ -183,6 +187,17 @@ def flash_attn_with_kvcache(
     _check(cache_seqlens.device == q.device, "cache_seqlens must be on q's device")
 
     scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    if Sq != 1:
+        if q.stride(0) != Sq * q.stride(1):
+            q = q.contiguous()
+        out = torch.empty((B, Sq, Hq, D), dtype=q.dtype, device=q.device)
+        lse = torch.empty((Hq, B * Sq), dtype=torch.float32, device=q.device) if return_softmax_lse else None
+        if B > 0 and Sq > 0:
+            _prefill_paged(dev, q.stride(1), q.stride(2), q, k_cache, v_cache, block_table, cache_seqlens, None, Sq, B,
+                           Sq, B * Sq, Hq, Hkv, D, scale, causal, out, out.stride(1), out.stride(2), lse)
+        if return_softmax_lse:
+            return out, lse.view(Hq, B, Sq).permute(1, 0, 2)
+        return out
     out = torch.empty((B, 1, Hq, D), dtype=q.dtype, device=q.device)
     lse = torch.empty((B, Hq, 1), dtype=torch.float32, device=q.device) if return_softmax_lse else None
     if B == 0:
@@ -209,6 +224,28 @@ def flash_attn_with_kvcache(
             _ptr(err), _stream(q.device),
         )
     return (out, lse) if return_softmax_lse else out
+
+
+def _prefill_paged(dev, q_ts, q_hs, q, k_cache, v_cache, block_table, k_lens, cu_q, q_len, S, max_q, T, Hq, Hkv, D,
+                   scale, causal, out, o_ts, o_hs, lse):
+    """la_prefill_paged on q's stream (chunked prefill over the paged cache)."""
+    with torch.cuda.device(dev):
+        ensure_init(dev)
+        _lib.call(
+            "la_prefill_paged",
+            _ptr(q), q_ts, q_hs,
+            _ptr(k_cache), _ptr(v_cache),
+            k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+            k_cache.shape[0], k_cache.shape[1],
+            _ptr(block_table), block_table.stride(0), block_table.shape[1],
+            _ptr(k_lens),
+            _ptr(cu_q), q_len, S, max_q, T,
+            Hq, Hkv, D,
+            ctypes.c_float(scale), 1 if causal else 0,
+            _ptr(out), o_ts, o_hs,
+            _ptr(lse),
+            _ptr(error_word(dev)), _stream(q.device),
+        )
 
 
 _identity_tables: dict[tuple, torch.Tensor] = {}
@@ -404,17 +441,23 @@ def flash_attn_varlen_func(
     block_table: Optional[torch.Tensor] = None,
     return_softmax_lse: bool = False,
 ):
-    """Packed self-attention over varlen sequences (flash-attn 2.8.3 varlen
-    signature): q [T, Hq, D], k/v [T, Hkv, D] bf16, cu_seqlens int32 [S+1].
-    Query and key sequences are the same tokens (prefill): cu_seqlens_k must
-    be cu_seqlens_q. Returns out [T, Hq, D] (and lse [Hq, T] fp32 when
-    return_softmax_lse)."""
+    """Packed attention over varlen sequences (flash-attn 2.8.3 varlen
+    signature): q [T, Hq, D] bf16, cu_seqlens_q int32 [S+1].
+
+    Without block_table, k/v [T, Hkv, D] are the same tokens as the queries
+    (prefill self-attention): cu_seqlens_k must be cu_seqlens_q. With
+    block_table [S, max_blocks] int32, k/v are the paged caches
+    [num_blocks, block_size, Hkv, D] and sequence s has
+    cu_seqlens_k[s+1] - cu_seqlens_k[s] keys there (chunked prefill: causal
+    masking bottom-right aligned). Returns out [T, Hq, D] (and lse [Hq, T]
+    fp32 when return_softmax_lse)."""
     if dropout_p != 0.0 or tuple(window_size) != (-1, -1) or softcap != 0.0 or alibi_slopes is not None:
         raise NotImplementedError("dropout / sliding window / softcap / alibi")
     if return_attn_probs:
         raise NotImplementedError("return_attn_probs")
     if block_table is not None:
-        raise NotImplementedError("paged KV in prefill: pass the fresh k/v")
+        return _varlen_paged(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, softmax_scale, causal, block_table,
+                             return_softmax_lse)
     if cu_seqlens_k is not cu_seqlens_q and cu_seqlens_k.data_ptr() != cu_seqlens_q.data_ptr():
         # distinct tensors: compare the values (a device sync; pass one tensor
         # twice, as prefill does, to avoid it)
@@ -447,6 +490,30 @@ def flash_attn_varlen_func(
             _ptr(error_word(dev)), _stream(q.device),
         )
     return (out, lse) if return_softmax_lse else out
+
+
+def _varlen_paged(q, k_cache, v_cache, cu_q, cu_k, max_seqlen_q, softmax_scale, causal, block_table, return_lse):
+    _check(q.dim() == 3 and k_cache.dim() == 4 and v_cache.shape == k_cache.shape
+           and k_cache.stride() == v_cache.stride(), "paged varlen: q [T, Hq, D], k/v caches [NB, BS, Hkv, D]")
+    T, Hq, D = q.shape
+    Hkv = k_cache.shape[2]
+    for name, t in (("q", q), ("k_cache", k_cache), ("v_cache", v_cache)):
+        _check(t.dtype == torch.bfloat16 and t.stride(-1) == 1, f"{name} must be bf16 with a contiguous last axis")
+    _check(k_cache.shape[3] == D and Hq % Hkv == 0, "head_dim / head counts of q and the caches do not fit")
+    _check(cu_q.dtype == torch.int32 and cu_q.is_contiguous() and cu_k.dtype == torch.int32
+           and cu_k.shape == cu_q.shape, "cu_seqlens must be int32 [S+1]")
+    S = cu_q.numel() - 1
+    _check(block_table.dtype == torch.int32 and block_table.dim() == 2 and block_table.shape[0] == S
+           and block_table.stride(1) == 1, "block_table must be int32 [S, max_blocks], row-contiguous")
+    dev = _device_index(q)
+    k_lens = (cu_k[1:] - cu_k[:-1]).to(torch.int32)
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else float(softmax_scale)
+    out = torch.empty((T, Hq, D), dtype=q.dtype, device=q.device)
+    lse = torch.empty((Hq, T), dtype=torch.float32, device=q.device) if return_lse else None
+    if S > 0 and T > 0:
+        _prefill_paged(dev, q.stride(0), q.stride(1), q, k_cache, v_cache, block_table, k_lens, cu_q, 0, S,
+                       int(max_seqlen_q), T, Hq, Hkv, D, scale, causal, out, out.stride(0), out.stride(1), lse)
+    return (out, lse) if return_lse else out
 
 
 _uniform_cu: dict[tuple, torch.Tensor] = {}

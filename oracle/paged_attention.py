@@ -107,3 +107,38 @@ def varlen_causal_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_
             sc = sc.masked_fill(~causal, float("-inf"))
             lse[a:b] = torch.logsumexp(sc, dim=-1).transpose(0, 1)
     return (out, lse) if return_lse else out
+
+
+def paged_chunk_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+                        cache_seqlens: torch.Tensor, cu_seqlens_q: torch.Tensor, softmax_scale: float | None = None,
+                        causal: bool = True, return_lse: bool = False):
+    """Chunked prefill over the paged cache: sequence s has the n_s query
+    tokens q[cu_seqlens_q[s]:cu_seqlens_q[s+1]] ([T, Hq, D] packed) and the
+    K_s = cache_seqlens[s] keys 0..K_s-1 gathered through its block-table row
+    (the chunk's own keys already written there). Causal masking is
+    bottom-right aligned, the flash_attn_with_kvcache contract for q_len > 1
+    at model.py:60-67: query i sees key j iff j <= i + K_s - n_s. A row that
+    sees no key yields zeros (lse -inf). fp32; returns [T, Hq, D] (and lse
+    [T, Hq])."""
+    T, Hq, D = q.shape
+    Hkv = k_cache.shape[2]
+    scale = 1.0 / math.sqrt(D) if softmax_scale is None else softmax_scale
+    out = torch.zeros(T, Hq, D, dtype=torch.float32)
+    lse = torch.full((T, Hq), float("-inf"))
+    for s in range(cu_seqlens_q.numel() - 1):
+        a, b = int(cu_seqlens_q[s]), int(cu_seqlens_q[s + 1])
+        n, K = b - a, int(cache_seqlens[s])
+        if n <= 0 or K <= 0:
+            continue
+        k, v = gather_kv(k_cache, v_cache, block_table[s], K)
+        kr = k.float().transpose(0, 1).repeat_interleave(Hq // Hkv, dim=0)  # [Hq, K, D]
+        vr = v.float().transpose(0, 1).repeat_interleave(Hq // Hkv, dim=0)
+        sc = torch.einsum("ihd,hjd->hij", q[a:b].float(), kr) * scale  # [Hq, n, K]
+        if causal:
+            vis = torch.arange(K)[None, :] <= (torch.arange(n)[:, None] + (K - n))
+            sc = sc.masked_fill(~vis[None], float("-inf"))
+        rl = torch.logsumexp(sc, dim=-1)  # [Hq, n]
+        pr = torch.exp(sc - torch.where(torch.isfinite(rl), rl, torch.zeros_like(rl))[..., None])
+        out[a:b] = torch.einsum("hij,hjd->ihd", pr, vr)
+        lse[a:b] = rl.transpose(0, 1)
+    return (out, lse) if return_lse else out

@@ -63,7 +63,7 @@ def test_unsupported_arguments_raise(pkg):
         pkg.flash_attn_with_kvcache(q, kc, kc, k=q, v=q)
     with pytest.raises(NotImplementedError):
         pkg.flash_attn_with_kvcache(q, kc, kc, window_size=(8, 0))
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(RuntimeError):  # q_len > 1 is chunked prefill: supported, but only on CUDA tensors
         pkg.flash_attn_with_kvcache(torch.zeros(1, 2, 16, 128, dtype=torch.bfloat16), kc, kc)
 
 
@@ -79,3 +79,16 @@ def test_argument_errors_before_launch(pkg):
     rc = lib.la_paged_decode(null, 0, 0, null, null, 0, 0, 0, 1, 256, null, 0, 1, null, 1, 16, 8, 128,
                              ctypes.c_float(0.1), null, 0, 0, null, null, 0, null, null)
     assert rc == 1
+    # chunked prefill over the paged cache: null pointers, a block size that
+    # 64-key tiles cannot walk, and an inconsistent uniform q_len
+    fake = ctypes.c_void_p(1 << 20)
+
+    def paged(q=fake, bs=256, q_len=4, T=8):
+        return lib.la_prefill_paged(q, 2048, 128, fake, fake, 256 * 1024, 1024, 128, 4, bs, fake, 2, 2, fake, null,
+                                    q_len, 2, 4, T, 16, 8, 128, ctypes.c_float(0.1), 1, fake, 2048, 128, null, null,
+                                    null)
+
+    assert paged(q=null) == 1
+    assert paged(bs=48) == 2
+    assert paged(T=9) == 1
+    assert paged(q_len=0, T=0) == 0  # nothing to do

@@ -154,3 +154,46 @@ def test_decode_oracle_empty_rows_zero():
                            torch.tensor([0, 5], dtype=torch.int32))
     assert torch.count_nonzero(out[0]) == 0
     assert torch.count_nonzero(out[1]) > 0
+
+
+@pytest.mark.parametrize("block_size,chunk", [(16, 32), (16, 7), (256, 80), (64, 33)])
+def test_chunk_prefill_oracle_pinned_by_reference_prefill(block_size, chunk):
+    """A prompt processed in chunks over the paged cache (each chunk's keys
+    already in the cache, bottom-right causal) gives the rows of the
+    reference's full causal prefill; NaN-filled pool slots past the written
+    keys never reach the result."""
+    g = _load("attention_prefill.npz")
+    q = torch.from_numpy(g["q"]).transpose(0, 1)
+    k = torch.from_numpy(g["k"]).transpose(0, 1)
+    v = torch.from_numpy(g["v"]).transpose(0, 1)
+    o = torch.from_numpy(g["o"]).transpose(0, 1)
+    L = q.shape[0]
+    nblk = -(-L // block_size)
+    NB = nblk + 2
+    perm = torch.randperm(NB - 1, generator=torch.Generator().manual_seed(9))[:nblk] + 1
+    kc = torch.full((NB, block_size, 8, 128), float("nan"))
+    vc = torch.full((NB, block_size, 8, 128), float("nan"))
+    for t in range(L):
+        kc[perm[t // block_size], t % block_size] = k[t]
+        vc[perm[t // block_size], t % block_size] = v[t]
+    bt = perm.view(1, -1).int()
+    # all chunks of the prompt packed as one call: sequence c = chunk c with its own prefix
+    starts = list(range(0, L, chunk))
+    ends = [min(L, s + chunk) for s in starts]
+    cu = torch.tensor([0] + list(np.cumsum([e - s for s, e in zip(starts, ends)])), dtype=torch.int32)
+    out, lse = opa.paged_chunk_prefill(q, kc, vc, bt.expand(len(starts), -1), torch.tensor(ends, dtype=torch.int32),
+                                       cu, return_lse=True)
+    torch.testing.assert_close(out, o, rtol=1e-5, atol=1e-5)
+    _, lse_p = opa.varlen_causal_prefill(q, k, v, torch.tensor([0, L], dtype=torch.int32), return_lse=True)
+    torch.testing.assert_close(lse, lse_p, rtol=1e-5, atol=1e-5)
+
+
+def test_chunk_prefill_oracle_rows_without_keys():
+    """Fewer keys than queries: the first n-K rows see no key (zeros, lse -inf)."""
+    kc = torch.randn(4, 16, 8, 128)
+    q = torch.randn(6, 16, 128)
+    out, lse = opa.paged_chunk_prefill(q, kc, kc, torch.tensor([[1, 2]], dtype=torch.int32),
+                                       torch.tensor([4], dtype=torch.int32), torch.tensor([0, 6], dtype=torch.int32),
+                                       return_lse=True)
+    assert torch.count_nonzero(out[:2]) == 0 and torch.isinf(lse[:2]).all()
+    assert torch.isfinite(out[2:]).all() and torch.count_nonzero(out[2]) > 0
