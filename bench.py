@@ -309,6 +309,15 @@ def secondary_metrics(pkg, dev):
                           "us": us, "tflops": tf, "peak_tflops": peak, "frac": tf / peak, "peak_source": kind,
                           "flops": w.causal_flops}
     del w
+    c = W.chunk_batch(16, 512, 512, 1536, seed=4, device=dev)
+    us = graph_time_us(lambda: pkg.flash_attn_with_kvcache(c.q, c.k_cache, c.v_cache, cache_seqlens=c.cache_seqlens,
+                                                           block_table=c.block_table, causal=True), 20)
+    tf = c.causal_flops / (us * 1e-6) / 1e12
+    out["chunk_prefill_b16"] = {"workload": "16 chunks of 512 tokens over cached prefixes U[512,1536] (paged, "
+                                            "256-token blocks, bottom-right causal)",
+                                "us": us, "tflops": tf, "peak_tflops": peak, "frac": tf / peak, "peak_source": kind,
+                                "flops": c.causal_flops}
+    del c
     d = W.decode_batch(32, 8192, 32768, num_blocks=None, block_size=BLOCK_SIZE, seed=40, device=dev)
     us = graph_time_us(lambda: pkg.flash_attn_with_kvcache(d.q, d.k_cache, d.v_cache, cache_seqlens=d.cache_seqlens,
                                                            block_table=d.block_table, causal=True), 5)
@@ -503,7 +512,7 @@ def run_ours(args):
 def run_case(args):
     """Single-kernel cases for profilers (ncu): run one op a few times on a
     small, fixed input and exit. --case decode-b128 | decode-long |
-    prefill-b16 | prefill-b1 | pre-attn-b128."""
+    prefill-b16 | prefill-b1 | chunk-prefill-b16 | pre-attn-b128."""
     import __graft_entry__
 
     pkg = __graft_entry__.load_package()
@@ -527,6 +536,12 @@ def run_case(args):
         for _ in range(reps):
             pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx, causal=True)
         info = {"causal_flops": w.causal_flops}
+    elif args.case == "chunk-prefill-b16":  # 16 chunks of 512 over cached prefixes U[512, 1536]
+        c = W.chunk_batch(16, 512, 512, 1536, seed=4, device=dev)
+        for _ in range(reps):
+            pkg.flash_attn_with_kvcache(c.q, c.k_cache, c.v_cache, cache_seqlens=c.cache_seqlens,
+                                        block_table=c.block_table, causal=True)
+        info = {"causal_flops": c.causal_flops}
     elif args.case == "pre-attn-b128":
         from lean_infer_b200 import qwen3
 

@@ -13,9 +13,11 @@
 // heads), against KV tiles of 64 keys. Per KV tile j:
 //   S_j  = Q K_j^T        tcgen05.mma M128 N64 K16 x8, fp32 in TMEM (2 buffers)
 //   P_j  = exp2(S_j*scale*log2e - m)  by 4 softmax warps, one thread per row,
-//          written to shared memory as bf16 in the MMA's K-major layout
-//   O   += P_j V_j        tcgen05.mma M128 N128 K16 x4 with V read MN-major,
-//                         fp32 in TMEM
+//          written back as bf16 over the first half of S_j's TMEM columns
+//   O   += P_j V_j        tcgen05.mma M128 N128 K16 x4, A = P from TMEM, B = V
+//                         read MN-major from its TMA tile, fp32 in TMEM
+// S_j's buffer is released by the completion of PV_j, so P is double-buffered
+// with S and softmax of tile j waits for PV_{j-1} only to rescale O.
 // The row max is only raised (and O, l rescaled) when a tile's max exceeds the
 // running one by more than 8 (log2 units), so P stays <= 256 and most tiles
 // skip the O rescale. S_{j+1} is issued while softmax works on S_j.
@@ -46,17 +48,18 @@ constexpr int kQHalf = kRows * 128;   // one 64-dim half of the Q tile: 128 rows
 constexpr int kQTile = 2 * kQHalf;    // 32 KB
 constexpr int kKVHalf = kKeys * 128;  // one 64-dim half of a K or V tile: 8 KB
 constexpr int kKVTile = 2 * kKVHalf;  // 16 KB
-constexpr int kPTile = kRows * 128;   // P: 128 rows x 64 keys bf16 = 16 KB
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;  // S0 [0,64) S1 [64,128) O [128,256)
+constexpr uint32_t kTmemCols = 256;  // S0/P0 [0,64) S1/P1 [64,128) O [128,256)
 constexpr uint32_t kColO = 128;
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, kKeys, false, false);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, false, true);
-// Q | K x2 | V x2 | P | barriers. Two CTAs must fit in an SM's 228 KB, so no
-// alignment slack is requested: the kernel checks that the dynamic shared
-// memory base is 1024-byte aligned (the 128-byte swizzle atom) and reports
-// LA_DEVERR_SMEM_ALIGN otherwise.
-constexpr int kBarOffset = kQTile + 4 * kKVTile + kPTile;  // 112 KB
+// Q | K x2 | V x2 | O staging (4 KB per softmax warp) | barriers. Two CTAs
+// must fit in an SM's 228 KB, so no alignment slack is requested: the kernel
+// checks that the dynamic shared memory base is 1024-byte aligned (the
+// 128-byte swizzle atom) and reports LA_DEVERR_SMEM_ALIGN otherwise.
+constexpr int kStageOffset = kQTile + 4 * kKVTile;     // 96 KB
+constexpr int kStageBytes = 32 * 128;                  // 32 rows x 64 dims bf16 per warp
+constexpr int kBarOffset = kStageOffset + 4 * kStageBytes;  // 112 KB
 constexpr size_t kSmemBytes = kBarOffset + 256;
 
 struct Params {
@@ -193,7 +196,6 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint8_t* sQ = smem;
   uint8_t* sK = smem + kQTile;                // 2 stages
   uint8_t* sV = smem + kQTile + 2 * kKVTile;  // 2 stages
-  uint8_t* sP = smem + kQTile + 4 * kKVTile;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOffset);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
@@ -201,11 +203,11 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* k_empty = bars + 4;   // [2]
   uint64_t* v_full = bars + 6;    // [2]  V ring: freed once PV has read it
   uint64_t* v_empty = bars + 8;   // [2]
-  uint64_t* s_full = bars + 10;   // [2]
-  uint64_t* s_empty = bars + 12;  // [2]
-  uint64_t* p_full = bars + 14;
-  uint64_t* o_done = bars + 15;
-  uint64_t* o_empty = bars + 16;
+  uint64_t* s_full = bars + 10;   // [2]  S_j in TMEM buffer j%2
+  uint64_t* s_empty = bars + 12;  // [2]  buffer j%2 free: PV_j (which read P_j from it) done
+  uint64_t* p_full = bars + 14;   // [2]  P_j written over S_j
+  uint64_t* o_done = bars + 16;   // [2]  PV_j done (barrier j%2: a parity wait is never 2 phases behind)
+  uint64_t* o_empty = bars + 18;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
 
   const int warp = threadIdx.x >> 5;
@@ -232,10 +234,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
+      mbar_init(&s_empty[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
     mbar_init(o_empty, 128);
     fence_barrier_init();
   }
@@ -365,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
     };
     auto pv = [&](int u, int ju, int kk) -> bool {  // O += P V for global tile u (item-local ju)
-      if (!wait_all(p_full, u & 1) || !wait_all(&v_full[u & 1], (u >> 1) & 1)) return false;
+      if (!wait_all(&p_full[u & 1], (u >> 1) & 1) || !wait_all(&v_full[u & 1], (u >> 1) & 1)) return false;
       if (ju == 0 && kk >= 1 && !wait_all(o_empty, (kk - 1) & 1)) return false;
       const int vrows = it.K - ju * kKeys;  // valid V rows of this tile
       if (p.paged && vrows < kKeys) {
@@ -384,12 +386,13 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_after();
       if (lane == 0) {
         const uint8_t* vt = sV + (u & 1) * kKVTile;
+        const uint32_t pt = tmem + (u & 1) * kKeys;  // P_u: 16 keys per 8 columns
 #pragma unroll
         for (int ks = 0; ks < kKeys / 16; ++ks)
-          umma_f16_ss(tmem + kColO, desc_kmajor(sP, kPTile, ks), desc_v(vt, ks), kIdescPV,
-                      (ju > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(o_done);
+          umma_f16_ts(tmem + kColO, pt + ks * 8, desc_v(vt, ks), kIdescPV, (ju > 0 || ks > 0) ? 1u : 0u);
+        umma_commit(&o_done[u & 1]);
         umma_commit(&v_empty[u & 1]);
+        umma_commit(&s_empty[u & 1]);  // S/P buffer u%2 may take S_{u+2}
       }
       __syncwarp();
       return true;
@@ -448,8 +451,6 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int c = 0; c < kC; ++c) tmem_ld32(taddr + sb * kKeys + c * 32, sv[c]);
         tc_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&s_empty[sb]);
 
         // Row max of the raw scores with 8 independent partial maxima (short
         // dependency chains: one warp per scheduler cannot hide a 128-long one).
@@ -493,46 +494,43 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         l = l * alpha + rs;
-        // The P buffer and O are free once PV of the previous tile is done; for
-        // an item's first tile this thread already waited for it (epilogue).
-        if (j >= 1) {
-          if (!__all_sync(0xffffffffu, mbar_wait(o_done, (t - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
+        // O is rescaled only when a row of this warp raised its max; then
+        // PV of the previous tile must be complete first. (An item's first
+        // tile needs neither: its PV overwrites O.)
+        if (j >= 1 && __any_sync(0xffffffffu, m_new != m)) {
+          const int u = t - 1;
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[u & 1], (u >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          if (__any_sync(0xffffffffu, m_new != m)) {
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              float o[32];
-              tmem_ld32(taddr + kColO + c * 32, o);
-              tc_wait_ld();
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tmem_ld32(taddr + kColO + c * 32, o);
+            tc_wait_ld();
 #pragma unroll
-              for (int e = 0; e < 32; ++e) o[e] *= alpha;
-              tmem_st32(taddr + kColO + c * 32, o);
-            }
-            tc_wait_st();
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(taddr + kColO + c * 32, o);
           }
         }
         m = m_new;
-        // P row -> shared memory, bf16, K-major SW128 (one 128-byte row of 64 keys).
+        // P row -> TMEM over the first 32 columns of S's buffer, bf16 pairs.
+        {
+          float pk[32];
 #pragma unroll
-        for (int ch = 0; ch < kKeys / 8; ++ch) {
-          const int c = ch >> 2, e0 = (ch & 3) * 8;
-          uint4 u;
-          u.x = pack_bf16x2(sv[c][e0 + 0], sv[c][e0 + 1]);
-          u.y = pack_bf16x2(sv[c][e0 + 2], sv[c][e0 + 3]);
-          u.z = pack_bf16x2(sv[c][e0 + 4], sv[c][e0 + 5]);
-          u.w = pack_bf16x2(sv[c][e0 + 6], sv[c][e0 + 7]);
-          *reinterpret_cast<uint4*>(sP + swz128(row, ch)) = u;
+          for (int i = 0; i < 32; ++i) pk[i] = __uint_as_float(pack_bf16x2(sv[i >> 4][(i & 15) * 2], sv[i >> 4][(i & 15) * 2 + 1]));
+          tmem_st32(taddr + sb * kKeys, pk);
         }
-        fence_proxy_async_smem();
+        tc_wait_st();
         tc_fence_before();
-        mbar_arrive(p_full);
+        mbar_arrive(&p_full[sb]);
       }
       if (!ok) break;
       // ---------------------------------------------------------- epilogue
-      if (!__all_sync(0xffffffffu, mbar_wait(o_done, (t - 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) break;
+      if (!__all_sync(0xffffffffu, mbar_wait(&o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, p.err,
+                                             LA_DEVERR_WAIT_TIMEOUT)))
+        break;
       tc_fence_after();
       float o[4][32];
 #pragma unroll
@@ -542,23 +540,39 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(o_empty);  // O may now be overwritten by the next item's first PV
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const int qh = it.h * p.group + g;
-      if (tok < it.L) {
-        __nv_bfloat16* orow =
-            p.out + static_cast<long long>(it.seq0 + tok) * p.out_ts + static_cast<long long>(qh) * p.out_hs;
+      if (p.lse && tok < it.L)
+        p.lse[static_cast<long long>(qh) * p.total + it.seq0 + tok] =
+            l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
+      // O rows -> global through this warp's staging buffer, one 64-dim half
+      // at a time: each thread writes its row (8 chunks of 16 B, XOR-swizzled
+      // by row), then each store instruction writes 4 rows x 128 contiguous
+      // bytes. Rows past the sequence's end are not stored.
+      uint8_t* stage = smem + kStageOffset + quarter * kStageBytes;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+      for (int h2 = 0; h2 < 2; ++h2) {
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint4 u;
-            u.x = pack_bf16x2(o[c][q4 * 8 + 0] * inv, o[c][q4 * 8 + 1] * inv);
-            u.y = pack_bf16x2(o[c][q4 * 8 + 2] * inv, o[c][q4 * 8 + 3] * inv);
-            u.z = pack_bf16x2(o[c][q4 * 8 + 4] * inv, o[c][q4 * 8 + 5] * inv);
-            u.w = pack_bf16x2(o[c][q4 * 8 + 6] * inv, o[c][q4 * 8 + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + q4 * 8) = u;
-          }
-        if (p.lse)
-          p.lse[static_cast<long long>(qh) * p.total + it.seq0 + tok] =
-              l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
+        for (int ch = 0; ch < 8; ++ch) {
+          const int c = 2 * h2 + (ch >> 2), e0 = (ch & 3) * 8;
+          uint4 u;
+          u.x = pack_bf16x2(o[c][e0 + 0] * inv, o[c][e0 + 1] * inv);
+          u.y = pack_bf16x2(o[c][e0 + 2] * inv, o[c][e0 + 3] * inv);
+          u.z = pack_bf16x2(o[c][e0 + 4] * inv, o[c][e0 + 5] * inv);
+          u.w = pack_bf16x2(o[c][e0 + 6] * inv, o[c][e0 + 7] * inv);
+          *reinterpret_cast<uint4*>(stage + lane * 128 + ((ch ^ (lane & 7)) << 4)) = u;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = i * 4 + (lane >> 3), ch = lane & 7;
+          const int rrow = quarter * 32 + r;
+          const int rg = rrow / p.tq;
+          const int rtok = it.q0 + rrow - rg * p.tq;
+          const uint4 u = *reinterpret_cast<const uint4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4));
+          if (rtok < it.L)
+            *reinterpret_cast<uint4*>(p.out + static_cast<long long>(it.seq0 + rtok) * p.out_ts +
+                                      static_cast<long long>(it.h * p.group + rg) * p.out_hs + h2 * 64 + ch * 8) = u;
+        }
+        __syncwarp();
       }
       ++k;
     }

@@ -114,3 +114,37 @@ def prefill_batch(batch: int, lo: int, hi: int, *, block_size: int = 256, num_q_
     k = torch.randn((T, num_kv_heads, head_dim), generator=g, device=dev).to(torch.bfloat16)
     v = torch.randn((T, num_kv_heads, head_dim), generator=g, device=dev).to(torch.bfloat16)
     return PrefillBatch(q, k, v, cu.to(dev), lengths, bt.to(dev), nb)
+
+
+@dataclass
+class ChunkBatch:
+    q: torch.Tensor              # [B, chunk, Hq, D] bf16
+    k_cache: torch.Tensor        # [NB, BS, Hkv, D] bf16 (prefix + chunk keys written)
+    v_cache: torch.Tensor
+    block_table: torch.Tensor    # [B, max_blocks] int32
+    cache_seqlens: torch.Tensor  # [B] int32: prefix + chunk
+
+    @property
+    def causal_flops(self) -> float:
+        """4 * Hq * D * sum over queries of the keys each sees (bottom-right
+        causal: query i of n sees K - n + i + 1 keys)."""
+        B, n, Hq, D = self.q.shape
+        K = self.cache_seqlens.double().cpu()
+        seen = (K - n) * n + n * (n + 1) / 2
+        return float(4 * Hq * D * seen.sum())
+
+
+def chunk_batch(batch: int, chunk: int, prefix_lo: int, prefix_hi: int, *, block_size: int = 256,
+                num_q_heads: int = 16, num_kv_heads: int = 8, head_dim: int = 128, seed: int = 0,
+                device="cpu") -> ChunkBatch:
+    """Chunked prefill step: every sequence has a prefix of U[prefix_lo,
+    prefix_hi] tokens already cached and a `chunk`-token chunk whose keys are
+    written too (cache_seqlens = prefix + chunk)."""
+    dev = torch.device(device)
+    k_lens = seq_lengths(batch, prefix_lo, prefix_hi, seed) + chunk
+    bt, nb = deal_blocks(k_lens, block_size, None, seed)
+    g = torch.Generator(device=dev).manual_seed(seed + 3)
+    kc = _randn_bf16((nb, block_size, num_kv_heads, head_dim), g, dev)
+    vc = _randn_bf16((nb, block_size, num_kv_heads, head_dim), g, dev)
+    q = torch.randn((batch, chunk, num_q_heads, head_dim), generator=g, device=dev).to(torch.bfloat16)
+    return ChunkBatch(q, kc, vc, bt.to(dev), k_lens.to(torch.int32).to(dev))
