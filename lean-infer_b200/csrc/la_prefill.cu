@@ -1,35 +1,40 @@
 // (c) Causal varlen prefill attention on the 5th-generation tensor cores
 // (tcgen05.mma, accumulators in TMEM, operands staged by TMA), sm_100a.
 //
-// Semantics: for every packed sequence s (tokens cu_seqlens[s] ..
+// Semantics: for every packed sequence s (queries cu_seqlens[s] ..
 // cu_seqlens[s+1]-1) and query head h, softmax(scale * Q K^T) V over the keys of
-// the same sequence and kv head h / G, causal (key j visible to query i iff
-// j <= i) — the reference's F.scaled_dot_product_attention(q, k, v,
-// is_causal=True, enable_gqa=True) at leaninfer/qwen3/model.py:56-57, applied
-// to many prompts at once (flash-attn varlen contract).
+// the same sequence and kv head h / G, causal — the reference's
+// F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True) at
+// leaninfer/qwen3/model.py:56-57, applied to many prompts at once (flash-attn
+// varlen contract). With paged keys (la_prefill_paged) the keys come from the
+// block-table pool and causal masking is bottom-right aligned (chunked
+// prefill).
 //
-// CTA tile: 128 query rows = the tq = 128/G consecutive tokens of the G query
-// heads that share one kv head (GQA packing: every K/V tile feeds all G
-// heads), against KV tiles of 64 keys. Per KV tile j:
-//   S_j  = Q K_j^T        tcgen05.mma M128 N64 K16 x8, fp32 in TMEM (2 buffers)
-//   P_j  = exp2(S_j*scale*log2e - m)  by 4 softmax warps, one thread per row,
-//          written back as bf16 over the first half of S_j's TMEM columns
-//   O   += P_j V_j        tcgen05.mma M128 N128 K16 x4, A = P from TMEM, B = V
-//                         read MN-major from its TMA tile, fp32 in TMEM
-// S_j's buffer is released by the completion of PV_j, so P is double-buffered
-// with S and softmax of tile j waits for PV_{j-1} only to rescale O.
-// The row max is only raised (and O, l rescaled) when a tile's max exceeds the
-// running one by more than 8 (log2 units), so P stays <= 256 and most tiles
-// skip the O rescale. S_{j+1} is issued while softmax works on S_j.
+// One persistent CTA per SM. A work item is a pair of query tiles of the same
+// (sequence, kv head): each tile is 128 rows = the tq = 128/G consecutive
+// tokens of the G query heads that share the kv head (GQA packing), and the
+// two tiles are consecutive in the sequence. Both tiles read the same K/V
+// tiles of 128 keys, staged once by TMA in a 4-stage ring. TMEM (512 columns):
+//   S0 [0,128)   S1 [128,256)   O0 [256,384)   O1 [384,512)
+// Per KV tile j and tile i:
+//   S_i  = Q_i K_j^T    tcgen05.mma M128 N128 K16 x8, fp32 into S_i
+//   P_i  = exp2(S_i*scale*log2e - m)  by softmax warpgroup i (one thread per
+//          row), written back as bf16 over the first 64 columns of S_i
+//   O_i += P_i V_j      tcgen05.mma M128 N128 K16 x8, A = P_i from TMEM, B = V
+//                       read MN-major from its TMA tile
+// The MMA warp interleaves the two tiles (PV_0(j), S_0(j+1), PV_1(j),
+// S_1(j+1)) so the tensor core computes one tile's products while the other
+// tile's softmax runs. S_i(j+1) overwrites P_i(j), so it waits for PV_i(j);
+// in exchange, when softmax i sees S_i(j+1), O_i is complete and can be
+// rescaled in place. The row max is raised (and O, l rescaled) only when a
+// tile's max exceeds the running one by more than 8 (log2 units), so most
+// tiles skip the rescale.
 //
-// Persistent CTAs walk a heaviest-first list of (sequence, kv head, query
-// tile) items. A CTA needs 112 KB of shared memory, 256 TMEM columns and
-// <= 170 registers per thread, so two CTAs share each SM: while one CTA's
-// softmax warps work, the other's MMAs run, and each scheduler has two
-// softmax warps to switch between.
-//
-// Warps: 0 = TMA producer, 1 = MMA issuer + TMEM owner, 2..5 = softmax and
-// epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. rows of that quarter).
+// Warps (16): 0-3 softmax of tile 0, 4-7 softmax of tile 1, 8-11 epilogue
+// (normalise O_i, store it through shared memory with coalesced rows, lse),
+// 12 MMA issuer + TMEM owner, 13 TMA producer, 14-15 idle. Warp w reads TMEM
+// lanes 32*(w%4)..+31. Registers are moved between warpgroups with
+// setmaxnreg: the softmax warpgroups hold a 128-column S row per thread.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -42,32 +47,39 @@ namespace la {
 namespace prefill {
 
 constexpr int kD = 128;
-constexpr int kRows = 128;            // query rows per CTA
-constexpr int kKeys = 64;             // keys per KV tile
-constexpr int kQHalf = kRows * 128;   // one 64-dim half of the Q tile: 128 rows x 128 B = 16 KB
-constexpr int kQTile = 2 * kQHalf;    // 32 KB
-constexpr int kKVHalf = kKeys * 128;  // one 64-dim half of a K or V tile: 8 KB
-constexpr int kKVTile = 2 * kKVHalf;  // 16 KB
-constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;  // S0/P0 [0,64) S1/P1 [64,128) O [128,256)
-constexpr uint32_t kColO = 128;
+constexpr int kRows = 128;             // query rows per Q tile
+constexpr int kKeys = 128;             // keys per KV tile
+constexpr int kQHalf = kRows * 128;    // one 64-dim half of a Q tile: 128 rows x 128 B = 16 KB
+constexpr int kQTile = 2 * kQHalf;     // 32 KB
+constexpr int kKVHalf = kKeys * 128;   // one 64-dim half of a K or V tile: 16 KB
+constexpr int kKVTile = 2 * kKVHalf;   // 32 KB
+constexpr int kStages = 4;             // K/V ring (K(j) and V(j) take one stage each)
+constexpr int kThreads = 512;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 256;        // O_i at kColO + 128 i; S_i at 128 i
 constexpr uint32_t kIdescQK = idesc_bf16_f32(128, kKeys, false, false);
 constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, false, true);
-// Q | K x2 | V x2 | O staging (4 KB per softmax warp) | barriers. Two CTAs
-// must fit in an SM's 228 KB, so no alignment slack is requested: the kernel
-// checks that the dynamic shared memory base is 1024-byte aligned (the
-// 128-byte swizzle atom) and reports LA_DEVERR_SMEM_ALIGN otherwise.
-constexpr int kStageOffset = kQTile + 4 * kKVTile;     // 96 KB
-constexpr int kStageBytes = 32 * 128;                  // 32 rows x 64 dims bf16 per warp
-constexpr int kBarOffset = kStageOffset + 4 * kStageBytes;  // 112 KB
-constexpr size_t kSmemBytes = kBarOffset + 256;
+// Per-thread registers after the split (the launch gives 512 x 128).
+constexpr int kRegSoftmax = 160, kRegEpilogue = 88, kRegOther = 104;
+static_assert(256 * kRegSoftmax + 128 * kRegEpilogue + 128 * kRegOther <= kThreads * 128,
+              "the register split must fit in the registers the CTA is launched with");
+// Shared memory: Q0 Q1 | K/V ring | O staging (4 KB per epilogue warp) |
+// row statistics (l, m of both tiles) | barriers; base aligned to 1024 B (the
+// 128-byte swizzle atom) at run time.
+constexpr int kOffKV = 2 * kQTile;                         // 64 KB
+constexpr int kOffStage = kOffKV + kStages * kKVTile;      // 192 KB
+constexpr int kStageBytes = 32 * 128;                      // 32 rows x 64 dims bf16
+constexpr int kOffStats = kOffStage + 4 * kStageBytes;     // 208 KB
+constexpr int kOffBar = kOffStats + 2 * 2 * kRows * 4;     // + 2 KB
+constexpr size_t kSmemBytes = kOffBar + 256 + 1024;
 
 struct Params {
   const int* cu;  // query starts [num_seqs + 1], or null: sequence s has q_len queries from token s * q_len
   int q_len;
   int num_seqs;
-  int n_qt;  // query tiles of the longest sequence
+  int n_qp;  // query-tile pairs of the longest sequence
   int tq;    // tokens per query tile (128 / group)
+  int tq_shift;  // log2(tq)
   int hq, hkv, group;
   int causal;
   float scale_log2;
@@ -104,22 +116,33 @@ __device__ __forceinline__ uint64_t desc_v(const uint8_t* tile, int ks) {
   return smem_desc_sw128(smem_u32(tile) + ks * 2048, kKVHalf, 1024);
 }
 
-// Work items are (sequence, kv head, query tile) in descending cost: query-
-// tile level qt from the top down (a tile's KV length grows with qt), at each
-// level only the sequences long enough to have that tile, then the kv heads.
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Work items are (sequence, kv head, query-tile pair) in descending cost:
+// pair level qp from the top down (a pair's KV length grows with qp), at each
+// level only the sequences long enough to have that pair, then the kv heads.
 // The valid items are ranked in that order and dealt to the G persistent CTAs
 // as a snake over 2G columns (CTA c takes ranks c, 2G-1-c, 2G+c, 4G-1-c, ...),
 // which evens out the summed cost per CTA. Every warp walks its CTA's item
 // list itself (the walk is warp-collective), so no item descriptors are
 // exchanged between roles.
 struct Item {
-  int s, h, q0, seq0, L, n_kv;
-  int K, off;  // keys of the sequence; causal offset K - L (0 for contiguous keys)
+  int s, h, q0, seq0, L;
+  int K, off;       // keys of the sequence; causal offset K - L (0 for contiguous keys)
+  int has1;         // the pair's second tile holds queries
+  int n0, n1, n;    // KV tiles of tile 0, tile 1 (0 if absent), and their max
 };
 
 struct Walker {
   int taken;       // items this CTA has taken so far
-  int level;       // current query-tile level
+  int level;       // current pair level
   long long base;  // rank of the first item of `level`
   int count;       // items at `level`
 };
@@ -127,28 +150,35 @@ struct Walker {
 __device__ __forceinline__ int q_start(const Params& p, int s) { return p.cu ? p.cu[s] : s * p.q_len; }
 __device__ __forceinline__ int q_count(const Params& p, int s) { return p.cu ? p.cu[s + 1] - p.cu[s] : p.q_len; }
 
-__device__ __forceinline__ bool seq_has_tile(const Params& p, int s, int q0) {
+__device__ __forceinline__ bool seq_has_pair(const Params& p, int s, int q0) {
   return s < p.num_seqs && q_count(p, s) > q0;
 }
 
 // Items at one level (warp-collective).
-__device__ int level_count(const Params& p, int level) {
+__device__ __forceinline__ int level_count(const Params& p, int level) {
   const int lane = threadIdx.x & 31;
-  const int q0 = level * p.tq;
+  const int q0 = level * 2 * p.tq;
   int n = 0;
-  for (int b = 0; b < p.num_seqs; b += 32) n += __popc(__ballot_sync(0xffffffffu, seq_has_tile(p, b + lane, q0)));
+  for (int b = 0; b < p.num_seqs; b += 32) n += __popc(__ballot_sync(0xffffffffu, seq_has_pair(p, b + lane, q0)));
   return n * p.hkv;
 }
 
-__device__ void walker_init(const Params& p, Walker& w) {
+__device__ __forceinline__ void walker_init(const Params& p, Walker& w) {
   w.taken = 0;
-  w.level = p.n_qt - 1;
+  w.level = p.n_qp - 1;
   w.base = 0;
   w.count = level_count(p, w.level);
 }
 
+// KV tiles a query tile starting at token q0 needs (at least one, so every
+// item runs the same pipeline; rows that see no key come out as zeros).
+__device__ __forceinline__ int kv_tiles(const Params& p, const Item& it, int q0) {
+  const int kv_end = p.causal ? min(q0 + p.tq + it.off, it.K) : it.K;
+  return max((kv_end + kKeys - 1) / kKeys, 1);
+}
+
 // Next item of this CTA (warp-collective; identical result in every lane).
-__device__ bool walker_next(const Params& p, Walker& w, Item& it) {
+__device__ __forceinline__ bool walker_next(const Params& p, Walker& w, Item& it) {
   const int lane = threadIdx.x & 31;
   const long long g2 = 2LL * gridDim.x;
   const long long r = static_cast<long long>(w.taken >> 1) * g2 +
@@ -160,11 +190,11 @@ __device__ bool walker_next(const Params& p, Walker& w, Item& it) {
     w.count = level_count(p, w.level);
   }
   const int idx = static_cast<int>(r - w.base);
-  const int ord = idx / p.hkv;  // the ord-th sequence (index order) that has this level's tile
-  const int q0 = w.level * p.tq;
+  const int ord = idx / p.hkv;  // the ord-th sequence (index order) that has this level's pair
+  const int q0 = w.level * 2 * p.tq;
   int seen = 0, s = 0;
   for (int b = 0; b < p.num_seqs; b += 32) {
-    const unsigned m = __ballot_sync(0xffffffffu, seq_has_tile(p, b + lane, q0));
+    const unsigned m = __ballot_sync(0xffffffffu, seq_has_pair(p, b + lane, q0));
     const int c = __popc(m);
     if (ord < seen + c) {
       unsigned mm = m;
@@ -181,37 +211,38 @@ __device__ bool walker_next(const Params& p, Walker& w, Item& it) {
   it.K = p.paged ? max(p.k_lens[s], 0) : it.L;
   it.off = it.K - it.L;
   it.q0 = q0;
-  const int kv_end = p.causal ? min(q0 + p.tq + it.off, it.K) : it.K;
-  // At least one tile, so every item runs the same pipeline (rows that see
-  // no key come out as zeros).
-  it.n_kv = max((kv_end + kKeys - 1) / kKeys, 1);
+  it.has1 = it.L > q0 + p.tq;
+  it.n0 = kv_tiles(p, it, q0);
+  it.n1 = it.has1 ? kv_tiles(p, it, q0 + p.tq) : 0;
+  it.n = max(it.n0, it.n1);
   ++w.taken;
   return true;
 }
 
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const Params p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t* sQ = smem;
-  uint8_t* sK = smem + kQTile;                // 2 stages
-  uint8_t* sV = smem + kQTile + 2 * kKVTile;  // 2 stages
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOffset);
-  uint64_t* q_full = bars + 0;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;    // [2]  K ring: freed once QK^T has read it
-  uint64_t* k_empty = bars + 4;   // [2]
-  uint64_t* v_full = bars + 6;    // [2]  V ring: freed once PV has read it
-  uint64_t* v_empty = bars + 8;   // [2]
-  uint64_t* s_full = bars + 10;   // [2]  S_j in TMEM buffer j%2
-  uint64_t* s_empty = bars + 12;  // [2]  buffer j%2 free: PV_j (which read P_j from it) done
-  uint64_t* p_full = bars + 14;   // [2]  P_j written over S_j
-  uint64_t* o_done = bars + 16;   // [2]  PV_j done (barrier j%2: a parity wait is never 2 phases behind)
-  uint64_t* o_empty = bars + 18;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;            // Q0, Q1
+  uint8_t* sKV = smem + kOffKV;  // ring
+  float* stats = reinterpret_cast<float*>(smem + kOffStats);  // [tile][l | m][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars + 0;        // both Q tiles of an item landed
+  uint64_t* q_empty = bars + 1;       // an item's last S issued and done
+  uint64_t* kv_full = bars + 2;       // [kStages]
+  uint64_t* kv_empty = bars + 6;      // [kStages]
+  uint64_t* s_full = bars + 10;       // [2] S_i written
+  uint64_t* s_free = bars + 12;       // [2] PV_i done: S_i/P_i columns free, O_i complete
+  uint64_t* p_full = bars + 14;       // [2] P_i written (128 arrivals)
+  uint64_t* o_empty = bars + 16;      // [2] the epilogue has read O_i (128 arrivals)
+  uint64_t* st_full = bars + 18;      // [2] row statistics of tile i written (128)
+  uint64_t* st_empty = bars + 20;     // [2] ... read by the epilogue (128)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int wg = warp >> 2;
   const float NEG_INF = -__int_as_float(0x7f800000);
 
   grid_dependency_wait();
@@ -221,27 +252,24 @@ __global__ void __launch_bounds__(kThreads, 2)
     Item it;
     if (!walker_next(p, w, it)) return;
   }
-  if (smem_u32(smem) & 1023u) {  // the swizzled tiles need a 1024-byte aligned base
-    if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, LA_DEVERR_SMEM_ALIGN);
-    return;
-  }
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&k_full[i], 1);
-      mbar_init(&k_empty[i], 1);
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 1);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&o_done[i], 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
     }
-    mbar_init(o_empty, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_empty[i], 128);
+      mbar_init(&st_full[i], 128);
+      mbar_init(&st_empty[i], 128);
+    }
     fence_barrier_init();
   }
-  if (warp == 1) {
+  if (warp == 12) {
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
@@ -250,222 +278,312 @@ __global__ void __launch_bounds__(kThreads, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer (lane 0 issues)
-    // Two streams over the CTA's KV tiles in global order: K runs one tile
-    // ahead of V (issue order K(t+1), V(t)), so a K load waits only for the
-    // QK^T two tiles back, never for a PV. Q of a new item is loaded just
-    // before that item's first K.
-    if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-    }
-    Walker wk, wv;
-    walker_init(p, wk);
-    walker_init(p, wv);
-    Item ik, iv;
-    bool k_more = walker_next(p, wk, ik), v_more = walker_next(p, wv, iv);
-    int jk = 0, jv = 0;  // tile index within the K / V stream's current item
-    int tk = 0, tv = 0;  // global tile counters of the two streams
-    int items_q = 0;     // items whose Q has been loaded
-    bool ok = true;
-    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
-    };
-    // One 64-key K or V tile (both 64-dim halves) of item `it`, tile j. Paged:
-    // one box per run of box_keys keys, through the block table; keys at or
-    // past the sequence's end, and ids outside the table or the pool (also
-    // reported), load from block `num_blocks`, outside the tensor map, which
-    // the copy engine fills with zeros. Either way the full tile's bytes land.
-    auto load_kv = [&](uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, const Item& it, int j) {
-      if (!p.paged) {
-        for (int half = 0; half < 2; ++half)
-          tma_load_3d(dst + half * kKVHalf, tm, bar, half * 64, it.h, it.seq0 + j * kKeys);
-        return;
+  auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
+  };
+
+  if (wg == 3) {
+    regs_dec<kRegOther>();
+    if (warp == 13) {
+      // ---------------------------------------------------------- TMA producer (lane 0 issues)
+      // Per item: Q0 (+ Q1), then K(j), V(j) for j = 0..n-1 into the ring, in
+      // the order the MMA warp consumes them.
+      if (lane == 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
       }
-      for (int b = 0; b < kKeys; b += p.box_keys) {
-        const int key = j * kKeys + b;
-        const int lb = key / p.bs;
-        int blk = p.num_blocks;
-        if (key < it.K) {
-          if (lb >= p.max_blocks) {
-            if (p.err) atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
-          } else {
-            const int id = __ldg(p.bt + static_cast<long long>(it.s) * p.bt_stride + lb);
-            if (id >= 0 && id < p.num_blocks)
-              blk = id;
-            else if (p.err)
-              atomicCAS(p.err, 0, LA_DEVERR_BLOCK_ID);
+      // One 128-key K or V tile (both 64-dim halves) of item `it`, tile j.
+      // Paged: one box per run of box_keys keys, through the block table;
+      // keys at or past the sequence's end, and ids outside the table or the
+      // pool (also reported), load from block `num_blocks`, outside the
+      // tensor map, which the copy engine fills with zeros. Either way the
+      // full tile's bytes land.
+      auto load_kv = [&](uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, const Item& it, int j) {
+        if (!p.paged) {
+          for (int half = 0; half < 2; ++half)
+            tma_load_3d(dst + half * kKVHalf, tm, bar, half * 64, it.h, it.seq0 + j * kKeys);
+          return;
+        }
+        for (int b = 0; b < kKeys; b += p.box_keys) {
+          const int key = j * kKeys + b;
+          const int lb = key / p.bs;
+          int blk = p.num_blocks;
+          if (key < it.K) {
+            if (lb >= p.max_blocks) {
+              if (p.err) atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
+            } else {
+              const int id = __ldg(p.bt + static_cast<long long>(it.s) * p.bt_stride + lb);
+              if (id >= 0 && id < p.num_blocks)
+                blk = id;
+              else if (p.err)
+                atomicCAS(p.err, 0, LA_DEVERR_BLOCK_ID);
+            }
+          }
+          for (int half = 0; half < 2; ++half)
+            tma_load_4d(dst + half * kKVHalf + b * 128, tm, bar, half * 64, key - lb * p.bs, it.h, blk);
+        }
+      };
+      Walker w;
+      walker_init(p, w);
+      Item it;
+      int kq = 0;
+      long long nld = 0;  // K/V tiles loaded
+      bool ok = true;
+      while (ok && walker_next(p, w, it)) {
+        if (lane == 0 && it.q0 + 2 * p.tq >= p.n_qp * 2 * p.tq && it.L > p.n_qp * 2 * p.tq && p.err)
+          atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);  // longer than max_seqlen: the tail is not computed
+        if (!(ok = wait_all(q_empty, (kq & 1) ^ 1u))) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(q_full, (it.has1 ? 2 : 1) * kQTile);
+          for (int t = 0; t < 1 + it.has1; ++t)
+            for (int g = 0; g < p.group; ++g)
+              for (int half = 0; half < 2; ++half)
+                tma_load_3d(sQ + t * kQTile + half * kQHalf + g * p.tq * 128, &tm_q, q_full, half * 64,
+                            it.h * p.group + g, it.seq0 + it.q0 + t * p.tq);
+        }
+        ++kq;
+        for (int j = 0; j < it.n && ok; ++j) {
+          for (int kv = 0; kv < 2; ++kv, ++nld) {
+            const int st = static_cast<int>(nld % kStages);
+            const uint32_t use = static_cast<uint32_t>(nld / kStages);
+            if (!(ok = wait_all(&kv_empty[st], (use & 1) ^ 1u))) break;
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&kv_full[st], kKVTile);
+              load_kv(sKV + st * kKVTile, kv ? &tm_v : &tm_k, &kv_full[st], it, j);
+            }
           }
         }
-        for (int half = 0; half < 2; ++half)
-          tma_load_4d(dst + half * kKVHalf + b * 128, tm, bar, half * 64, key - lb * p.bs, it.h, blk);
       }
-    };
-    // Issue K tile tk (loading the item's Q first when it is the item's first tile).
-    auto issue_k = [&]() -> bool {
-      if (jk == 0) {
-        if (lane == 0 && ik.q0 == (p.n_qt - 1) * p.tq && ik.L > p.n_qt * p.tq && p.err)
-          atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
-        // Q of item k replaces item k-1's once its last QK^T has completed.
-        if (!wait_all(q_empty, (items_q & 1) ^ 1u)) return false;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(q_full, kQTile);
-          for (int g = 0; g < p.group; ++g)
-            for (int half = 0; half < 2; ++half)
-              tma_load_3d(sQ + half * kQHalf + g * p.tq * 128, &tm_q, q_full, half * 64, ik.h * p.group + g,
-                          ik.seq0 + ik.q0);
-        }
-        ++items_q;
-      }
-      const int st = tk & 1;
-      if (!wait_all(&k_empty[st], ((tk >> 1) & 1) ^ 1u)) return false;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&k_full[st], kKVTile);
-        load_kv(sK + st * kKVTile, &tm_k, &k_full[st], ik, jk);
-      }
-      ++tk;
-      if (++jk == ik.n_kv) {
-        jk = 0;
-        k_more = walker_next(p, wk, ik);
-      }
-      return true;
-    };
-    auto issue_v = [&]() -> bool {
-      const int st = tv & 1;
-      if (!wait_all(&v_empty[st], ((tv >> 1) & 1) ^ 1u)) return false;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&v_full[st], kKVTile);
-        load_kv(sV + st * kKVTile, &tm_v, &v_full[st], iv, jv);
-      }
-      ++tv;
-      if (++jv == iv.n_kv) {
-        jv = 0;
-        v_more = walker_next(p, wv, iv);
-      }
-      return true;
-    };
-    if (k_more) ok = issue_k();  // K(0)
-    while (ok && v_more) {
-      if (k_more && !(ok = issue_k())) break;  // K(t+1)
-      ok = issue_v();                           // V(t)
-    }
-    if (!ok && lane == 0) {  // early exit: let the copies already issued land (bounded)
-      for (int u = (tk > 2 ? tk - 2 : 0); u < tk; ++u) mbar_wait(&k_full[u & 1], (u >> 1) & 1, nullptr, 0);
-      for (int u = (tv > 2 ? tv - 2 : 0); u < tv; ++u) mbar_wait(&v_full[u & 1], (u >> 1) & 1, nullptr, 0);
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (lane 0 issues)
-    Walker w;
-    walker_init(p, w);
-    Item it;
-    int k = 0, t = 0;
-    bool ok = true;
-    auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
-    };
-    auto pv = [&](int u, int ju, int kk) -> bool {  // O += P V for global tile u (item-local ju)
-      if (!wait_all(&p_full[u & 1], (u >> 1) & 1) || !wait_all(&v_full[u & 1], (u >> 1) & 1)) return false;
-      if (ju == 0 && kk >= 1 && !wait_all(o_empty, (kk - 1) & 1)) return false;
-      const int vrows = it.K - ju * kKeys;  // valid V rows of this tile
-      if (p.paged && vrows < kKeys) {
-        // Pool slots past the sequence's last key hold whatever was there
-        // (possibly NaN); P is 0 for them but 0 * NaN is not, so zero them.
-        uint8_t* vt = sV + (u & 1) * kKVTile;
-        const int r0 = max(vrows, 0);
-        const int n16 = (kKeys - r0) * 8;  // 16-byte chunks per half
-        for (int i = lane; i < 2 * n16; i += 32) {
-          const int half = i / n16, c = i - half * n16;
-          *reinterpret_cast<uint4*>(vt + half * kKVHalf + r0 * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-      }
-      tc_fence_after();
-      if (lane == 0) {
-        const uint8_t* vt = sV + (u & 1) * kKVTile;
-        const uint32_t pt = tmem + (u & 1) * kKeys;  // P_u: 16 keys per 8 columns
-#pragma unroll
-        for (int ks = 0; ks < kKeys / 16; ++ks)
-          umma_f16_ts(tmem + kColO, pt + ks * 8, desc_v(vt, ks), kIdescPV, (ju > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(&o_done[u & 1]);
-        umma_commit(&v_empty[u & 1]);
-        umma_commit(&s_empty[u & 1]);  // S/P buffer u%2 may take S_{u+2}
+      if (!ok && lane == 0) {  // early exit: let the copies already issued land (bounded)
+        for (long long u = (nld > kStages ? nld - kStages : 0); u < nld; ++u)
+          mbar_wait(&kv_full[u % kStages], static_cast<uint32_t>(u / kStages) & 1, nullptr, 0);
+        if (kq > 0) mbar_wait(q_full, (kq - 1) & 1, nullptr, 0);
       }
       __syncwarp();
-      return true;
-    };
-    while (ok && walker_next(p, w, it)) {
-      if (!wait_all(q_full, k & 1)) break;
-      const int t0 = t;
-      for (int j = 0; j < it.n_kv; ++j, ++t) {
-        const int st = t & 1;
-        ok = wait_all(&k_full[st], (t >> 1) & 1) && wait_all(&s_empty[st], ((t >> 1) & 1) ^ 1u);
-        if (!ok) break;
+    } else if (warp == 12) {
+      // ---------------------------------------------------------- MMA issuer (lane 0 issues)
+      Walker w;
+      walker_init(p, w);
+      Item it;
+      int kq = 0;
+      long long nld = 0;               // K/V ring position of the item's K(0)
+      uint32_t cs[2] = {0, 0};         // S_i issued
+      uint32_t cp[2] = {0, 0};         // PV_i issued
+      uint32_t items_i[2] = {0, 0};    // items in which tile i ran
+      bool ok = true;
+      auto issue_s = [&](int i, const uint8_t* kt) -> bool {
+        if (!wait_all(&s_free[i], (cs[i] & 1) ^ 1u)) return false;  // PV_i of the previous tile done
         tc_fence_after();
         if (lane == 0) {
-          const uint8_t* kt = sK + st * kKVTile;
+          const uint8_t* qt = sQ + i * kQTile;
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            umma_f16_ss(tmem + st * kKeys, desc_kmajor(sQ, kQHalf, ks), desc_kmajor(kt, kKVHalf, ks), kIdescQK,
+            umma_f16_ss(tmem + i * 128, desc_kmajor(qt, kQHalf, ks), desc_kmajor(kt, kKVHalf, ks), kIdescQK,
                         ks > 0 ? 1u : 0u);
-          umma_commit(&s_full[st]);
-          umma_commit(&k_empty[st]);  // K tile read
-          if (j == it.n_kv - 1) umma_commit(q_empty);  // this item's Q is no longer read
+          umma_commit(&s_full[i]);
         }
         __syncwarp();
-        if (j >= 1 && !(ok = pv(t - 1, j - 1, k))) break;
+        ++cs[i];
+        return true;
+      };
+      auto issue_pv = [&](int i, int j, const uint8_t* vt) -> bool {
+        if (!wait_all(&p_full[i], cp[i] & 1)) return false;
+        if (j == 0) {  // O_i is overwritten: the epilogue must have read the previous item's
+          if (items_i[i] > 0 && !wait_all(&o_empty[i], (items_i[i] - 1) & 1)) return false;
+          ++items_i[i];
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t pt = tmem + i * 128;  // P_i: 16 keys per 8 columns
+#pragma unroll
+          for (int ks = 0; ks < kKeys / 16; ++ks)
+            umma_f16_ts(tmem + kColO + i * 128, pt + ks * 8, desc_v(vt, ks), kIdescPV, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&s_free[i]);
+        }
+        __syncwarp();
+        ++cp[i];
+        return true;
+      };
+      auto slot_of = [&](long long idx) -> int { return static_cast<int>(idx % kStages); };
+      auto wait_full = [&](long long idx) -> bool {
+        return wait_all(&kv_full[slot_of(idx)], static_cast<uint32_t>(idx / kStages) & 1);
+      };
+      while (ok && walker_next(p, w, it)) {
+        if (!(ok = wait_all(q_full, kq & 1))) break;
+        const long long base = nld;  // K(j) at base + 2j, V(j) at base + 2j + 1
+        nld += 2LL * it.n;
+        // S_0(0), S_1(0)
+        if (!(ok = wait_full(base))) break;
+        {
+          const uint8_t* kt = sKV + slot_of(base) * kKVTile;
+          if (!(ok = issue_s(0, kt))) break;
+          if (it.n1 > 0 && !(ok = issue_s(1, kt))) break;
+          if (lane == 0) {
+            umma_commit(&kv_empty[slot_of(base)]);
+            if (it.n == 1) umma_commit(q_empty);
+          }
+          __syncwarp();
+        }
+        for (int j = 0; j < it.n && ok; ++j) {
+          const long long vi = base + 2 * j + 1, ki = vi + 1;  // V(j), K(j+1)
+          const bool a0 = j < it.n0, a1 = j < it.n1;
+          const bool nx0 = j + 1 < it.n0, nx1 = j + 1 < it.n1;
+          if (!(ok = wait_full(vi))) break;
+          uint8_t* vt = sKV + slot_of(vi) * kKVTile;
+          const int vrows = it.K - j * kKeys;  // valid V rows of this tile
+          if (p.paged && vrows < kKeys) {
+            // Pool slots past the sequence's last key hold whatever was there
+            // (possibly NaN); P is 0 for them but 0 * NaN is not, so zero them.
+            const int r0 = max(vrows, 0);
+            const int n16 = (kKeys - r0) * 8;  // 16-byte chunks per half
+            for (int x = lane; x < 2 * n16; x += 32) {
+              const int half = x / n16, c = x - half * n16;
+              *reinterpret_cast<uint4*>(vt + half * kKVHalf + r0 * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+          }
+          if ((nx0 || nx1) && !(ok = wait_full(ki))) break;
+          const uint8_t* kt = sKV + slot_of(ki) * kKVTile;
+          if (a0 && !(ok = issue_pv(0, j, vt))) break;
+          if (nx0 && !(ok = issue_s(0, kt))) break;
+          if (a1 && !(ok = issue_pv(1, j, vt))) break;
+          if (lane == 0) umma_commit(&kv_empty[slot_of(vi)]);  // V(j) read once both PVs are done
+          __syncwarp();
+          if (nx1 && !(ok = issue_s(1, kt))) break;
+          if (j + 1 < it.n) {
+            if (lane == 0) {
+              umma_commit(&kv_empty[slot_of(ki)]);
+              if (j + 2 == it.n) umma_commit(q_empty);  // this item's last S
+            }
+            __syncwarp();
+          }
+        }
+        ++kq;
       }
-      if (!ok || !(ok = pv(t0 + it.n_kv - 1, it.n_kv - 1, k))) break;
-      ++k;
+      __syncwarp();
     }
-    __syncwarp();
-  } else {
-    // ------------------------------------------------------------ softmax + epilogue
+    // warps 14, 15: no role
+  } else if (wg == 2) {
+    regs_dec<kRegEpilogue>();
+    // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const int g = row / p.tq;
+    uint8_t* stage = smem + kOffStage + quarter * kStageBytes;
+    Walker w;
+    walker_init(p, w);
+    Item it;
+    uint32_t cp[2] = {0, 0};       // PV_i so far (through this item)
+    uint32_t items_i[2] = {0, 0};  // items in which tile i ran
+    bool ok = true;
+    while (ok && walker_next(p, w, it)) {
+      for (int i = 0; i < 2 && ok; ++i) {
+        const int ni = i ? it.n1 : it.n0;
+        if (ni == 0) continue;
+        cp[i] += ni;
+        if (!(ok = wait_all(&st_full[i], items_i[i] & 1))) break;
+        const float l = stats[(i * 2 + 0) * kRows + row];
+        const float m = stats[(i * 2 + 1) * kRows + row];
+        mbar_arrive(&st_empty[i]);
+        if (!(ok = wait_all(&s_free[i], (cp[i] - 1) & 1))) break;  // the item's last PV_i
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const int qt0 = it.q0 + i * p.tq;
+        {
+          const int g = row >> p.tq_shift;
+          const int tok = qt0 + (row & (p.tq - 1));
+          if (p.lse && tok < it.L)
+            p.lse[static_cast<long long>(it.h * p.group + g) * p.total + it.seq0 + tok] =
+                l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
+        }
+        // O_i rows -> global through this warp's staging buffer, one 64-dim
+        // half at a time: each thread writes its row (8 chunks of 16 B,
+        // XOR-swizzled by row), then each store instruction writes 4 rows x
+        // 128 contiguous bytes. Rows past the sequence's end are not stored.
+#pragma unroll 1
+        for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float o[32];
+            tmem_ld32(taddr + kColO + i * 128 + h2 * 64 + c * 32, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint4 u;
+              u.x = pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv);
+              u.y = pack_bf16x2(o[q4 * 8 + 2] * inv, o[q4 * 8 + 3] * inv);
+              u.z = pack_bf16x2(o[q4 * 8 + 4] * inv, o[q4 * 8 + 5] * inv);
+              u.w = pack_bf16x2(o[q4 * 8 + 6] * inv, o[q4 * 8 + 7] * inv);
+              const int ch = c * 4 + q4;
+              *reinterpret_cast<uint4*>(stage + lane * 128 + ((ch ^ (lane & 7)) << 4)) = u;
+            }
+          }
+          if (h2 == 1) {  // all of O_i is in registers or staged: the next item may overwrite it
+            tc_fence_before();
+            mbar_arrive(&o_empty[i]);
+          }
+          __syncwarp();
+#pragma unroll 1
+          for (int x = 0; x < 8; ++x) {
+            const int r = x * 4 + (lane >> 3), ch = lane & 7;
+            const int rrow = quarter * 32 + r;
+            const int rg = rrow >> p.tq_shift;
+            const int rtok = qt0 + (rrow & (p.tq - 1));
+            const uint4 u = *reinterpret_cast<const uint4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4));
+            if (rtok < it.L)
+              *reinterpret_cast<uint4*>(p.out + static_cast<long long>(it.seq0 + rtok) * p.out_ts +
+                                        static_cast<long long>(it.h * p.group + rg) * p.out_hs + h2 * 64 + ch * 8) = u;
+          }
+          __syncwarp();
+        }
+        ++items_i[i];
+      }
+    }
+  } else {
+    regs_inc<kRegSoftmax>();
+    // ------------------------------------------------------------ softmax of tile i = wg
+    const int i = wg;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t colS = i * 128, colO = kColO + i * 128;
     const float sl2 = p.scale_log2;
     Walker w;
     walker_init(p, w);
     Item it;
-    int k = 0, t = 0;
+    uint32_t t = 0;      // S_i tiles seen
+    uint32_t nst = 0;    // items whose statistics were written
     bool ok = true;
     while (ok && walker_next(p, w, it)) {
-      const int tok = it.q0 + (row - g * p.tq);  // token index within the sequence
+      const int ni = i ? it.n1 : it.n0;
+      if (ni == 0) continue;
+      const int tok = it.q0 + i * p.tq + (row & (p.tq - 1));        // token index within the sequence
       const int lim = p.causal ? min(max(tok + 1 + it.off, 0), it.K) : it.K;  // keys [0, lim) are visible
       float m = NEG_INF, l = 0.f;
-      for (int j = 0; j < it.n_kv; ++j, ++t) {
-        const int sb = t & 1;
+      for (int j = 0; j < ni; ++j, ++t) {
         // tcgen05.ld is warp-collective: keep the decision to continue warp-uniform
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[sb], (t >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
-          ok = false;
-          break;
-        }
+        if (!(ok = wait_all(&s_full[i], t & 1))) break;
         tc_fence_after();
-        constexpr int kC = kKeys / 32;  // 32-column TMEM loads per row
-        float sv[kC][32];
+        float sv[4][32];
 #pragma unroll
-        for (int c = 0; c < kC; ++c) tmem_ld32(taddr + sb * kKeys + c * 32, sv[c]);
+        for (int c = 0; c < 4; ++c) tmem_ld32(taddr + colS + c * 32, sv[c]);
         tc_wait_ld();
 
-        // Row max of the raw scores with 8 independent partial maxima (short
-        // dependency chains: one warp per scheduler cannot hide a 128-long one).
+        // Row max of the raw scores with 8 independent partial maxima.
         const int nvis = lim - j * kKeys;  // visible columns of this tile
         float mx[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) mx[a] = NEG_INF;
         if (__all_sync(0xffffffffu, nvis >= kKeys)) {  // whole tile visible: no mask
 #pragma unroll
-          for (int c = 0; c < kC; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[c][e]);
         } else {
 #pragma unroll
-          for (int c = 0; c < kC; ++c)
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               const float x = (c * 32 + e < nvis) ? sv[c][e] : NEG_INF;
@@ -481,105 +599,58 @@ __global__ void __launch_bounds__(kThreads, 2)
         const float m_ref = (m_new == NEG_INF) ? 0.f : m_new;
         const float alpha = ex2(m - m_ref);  // 0 on the first tile, 1 when m is kept
         const float neg_m = -m_ref;
+        // P = exp2(S*scale*log2e - m) -> bf16 pairs over the first 64 columns
+        // of S_i, one 64-key half at a time (S values become packed P as
+        // they are used, which keeps the live registers near one S row).
         float ps[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) ps[a] = 0.f;
 #pragma unroll
-        for (int c = 0; c < kC; ++c)
+        for (int c2 = 0; c2 < 2; ++c2) {
+          float pk[32];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float pe = ex2(fmaf(sv[c][e], sl2, neg_m));  // masked: -inf -> 0
-            sv[c][e] = pe;
-            ps[e & 7] += pe;
+          for (int x = 0; x < 32; ++x) {
+            const float e0 = ex2(fmaf(sv[2 * c2 + (x >> 4)][(x & 15) * 2], sl2, neg_m));  // masked: -inf -> 0
+            const float e1 = ex2(fmaf(sv[2 * c2 + (x >> 4)][(x & 15) * 2 + 1], sl2, neg_m));
+            ps[(2 * x) & 7] += e0;
+            ps[(2 * x + 1) & 7] += e1;
+            pk[x] = __uint_as_float(pack_bf16x2(e0, e1));
           }
+          tmem_st32(taddr + colS + c2 * 32, pk);
+        }
         const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         l = l * alpha + rs;
-        // O is rescaled only when a row of this warp raised its max; then
-        // PV of the previous tile must be complete first. (An item's first
-        // tile needs neither: its PV overwrites O.)
+        // O_i holds PV of tiles < j (S_i(j) was issued after PV_i(j-1)
+        // completed) and PV_i(j) waits for P_i(j): rescale it in place when a
+        // row of this warp raised its max. (A first tile's PV overwrites O.)
         if (j >= 1 && __any_sync(0xffffffffu, m_new != m)) {
-          const int u = t - 1;
-          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[u & 1], (u >> 1) & 1, p.err, LA_DEVERR_WAIT_TIMEOUT))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
+#pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             float o[32];
-            tmem_ld32(taddr + kColO + c * 32, o);
+            tmem_ld32(taddr + colO + c * 32, o);
             tc_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] *= alpha;
-            tmem_st32(taddr + kColO + c * 32, o);
+            tmem_st32(taddr + colO + c * 32, o);
           }
         }
         m = m_new;
-        // P row -> TMEM over the first 32 columns of S's buffer, bf16 pairs.
-        {
-          float pk[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) pk[i] = __uint_as_float(pack_bf16x2(sv[i >> 4][(i & 15) * 2], sv[i >> 4][(i & 15) * 2 + 1]));
-          tmem_st32(taddr + sb * kKeys, pk);
-        }
         tc_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[sb]);
+        mbar_arrive(&p_full[i]);
       }
       if (!ok) break;
-      // ---------------------------------------------------------- epilogue
-      if (!__all_sync(0xffffffffu, mbar_wait(&o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, p.err,
-                                             LA_DEVERR_WAIT_TIMEOUT)))
-        break;
-      tc_fence_after();
-      float o[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(taddr + kColO + c * 32, o[c]);
-      tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(o_empty);  // O may now be overwritten by the next item's first PV
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const int qh = it.h * p.group + g;
-      if (p.lse && tok < it.L)
-        p.lse[static_cast<long long>(qh) * p.total + it.seq0 + tok] =
-            l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
-      // O rows -> global through this warp's staging buffer, one 64-dim half
-      // at a time: each thread writes its row (8 chunks of 16 B, XOR-swizzled
-      // by row), then each store instruction writes 4 rows x 128 contiguous
-      // bytes. Rows past the sequence's end are not stored.
-      uint8_t* stage = smem + kStageOffset + quarter * kStageBytes;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          const int c = 2 * h2 + (ch >> 2), e0 = (ch & 3) * 8;
-          uint4 u;
-          u.x = pack_bf16x2(o[c][e0 + 0] * inv, o[c][e0 + 1] * inv);
-          u.y = pack_bf16x2(o[c][e0 + 2] * inv, o[c][e0 + 3] * inv);
-          u.z = pack_bf16x2(o[c][e0 + 4] * inv, o[c][e0 + 5] * inv);
-          u.w = pack_bf16x2(o[c][e0 + 6] * inv, o[c][e0 + 7] * inv);
-          *reinterpret_cast<uint4*>(stage + lane * 128 + ((ch ^ (lane & 7)) << 4)) = u;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = i * 4 + (lane >> 3), ch = lane & 7;
-          const int rrow = quarter * 32 + r;
-          const int rg = rrow / p.tq;
-          const int rtok = it.q0 + rrow - rg * p.tq;
-          const uint4 u = *reinterpret_cast<const uint4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4));
-          if (rtok < it.L)
-            *reinterpret_cast<uint4*>(p.out + static_cast<long long>(it.seq0 + rtok) * p.out_ts +
-                                      static_cast<long long>(it.h * p.group + rg) * p.out_hs + h2 * 64 + ch * 8) = u;
-        }
-        __syncwarp();
-      }
-      ++k;
+      // Row statistics for the epilogue.
+      if (!(ok = wait_all(&st_empty[i], (nst & 1) ^ 1u))) break;
+      stats[(i * 2 + 0) * kRows + row] = l;
+      stats[(i * 2 + 1) * kRows + row] = m;
+      mbar_arrive(&st_full[i]);
+      ++nst;
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 12) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -591,9 +662,6 @@ int prefill_init(int device) {
   (void)device;
   cudaError_t e = cudaFuncSetAttribute(prefill::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(prefill::kSmemBytes));
-  // all of the unified L1/shared storage as shared memory, so two CTAs fit
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(prefill::prefill_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   return cuda_status(e);
 }
 
@@ -605,15 +673,13 @@ namespace prefill {
 // Common tail of the two entry points: the persistent grid over the items.
 static int launch(const CUtensorMap& tq_map, const CUtensorMap& tk_map, const CUtensorMap& tv_map, const Params& p,
                   cudaStream_t stream) {
-  const long long items = static_cast<long long>(p.n_qt) * p.num_seqs * p.hkv;
+  const long long items = static_cast<long long>(p.n_qp) * p.num_seqs * p.hkv;
   if (items > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
   const int device = current_device();
   const int sms = device >= 0 ? num_sms(device) : 0;
   if (sms <= 0) return LA_ERR_CUDA;
-  // Two CTAs per SM by design (registers, shared memory and TMEM are sized
-  // for it); if fewer fit, the extra CTAs simply run as a second wave.
-  const long long ctas = static_cast<long long>(sms) * 2;
-  const dim3 grid(static_cast<unsigned>(items < ctas ? items : ctas));  // persistent
+  const long long ctas = sms;  // one persistent CTA per SM (all of its TMEM and most of its shared memory)
+  const dim3 grid(static_cast<unsigned>(items < ctas ? items : ctas));
   return cuda_status(launch_pdl(prefill_kernel, grid, dim3(kThreads), kSmemBytes, stream, tq_map, tk_map, tv_map, p));
 }
 
@@ -640,6 +706,7 @@ static int common_setup(const void* q, int64_t q_token_stride, int64_t q_head_st
   if (stt != LA_OK) return stt;
   *p = Params{};
   p->tq = tq;
+  p->tq_shift = __builtin_ctz(static_cast<unsigned>(tq));
   p->hq = num_q_heads;
   p->hkv = num_kv_heads;
   p->group = group;
@@ -684,7 +751,7 @@ extern "C" int la_prefill_varlen(const void* q, int64_t q_token_stride, int64_t 
   }
   p.cu = cu_seqlens;
   p.num_seqs = num_seqs;
-  p.n_qt = (max_seqlen + p.tq - 1) / p.tq;
+  p.n_qp = ((max_seqlen + p.tq - 1) / p.tq + 1) / 2;
   p.causal = causal ? 1 : 0;
   p.lse = softmax_lse;
   p.err = dev_error;
@@ -712,7 +779,7 @@ extern "C" int la_prefill_paged(const void* q, int64_t q_token_stride, int64_t q
   }
   if (num_seqs == 0 || max_seqlen_q == 0 || total_q == 0) return LA_OK;
   if (num_blocks > 0x7ffffffeLL) return LA_ERR_UNSUPPORTED;
-  // 64-key tiles must not straddle blocks, or be whole blocks of 16 / 32.
+  // 128-key tiles must not straddle blocks, or be whole blocks of 16 / 32 / 64.
   if (block_size <= 0 || block_size % 16 || (block_size % kKeys && kKeys % block_size)) return LA_ERR_UNSUPPORTED;
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16)) return LA_ERR_ALIGNMENT;
   const long long kst[] = {kv_block_stride, kv_token_stride, kv_head_stride};
@@ -738,7 +805,7 @@ extern "C" int la_prefill_paged(const void* q, int64_t q_token_stride, int64_t q
   p.cu = cu_seqlens_q;
   p.q_len = q_len;
   p.num_seqs = num_seqs;
-  p.n_qt = (max_seqlen_q + p.tq - 1) / p.tq;
+  p.n_qp = ((max_seqlen_q + p.tq - 1) / p.tq + 1) / 2;
   p.causal = causal ? 1 : 0;
   p.lse = softmax_lse;
   p.err = dev_error;
