@@ -512,7 +512,7 @@ def run_ours(args):
 def run_case(args):
     """Single-kernel cases for profilers (ncu): run one op a few times on a
     small, fixed input and exit. --case decode-b128 | decode-long |
-    prefill-b16 | prefill-b1 | chunk-prefill-b16 | pre-attn-b128."""
+    prefill-b16 | prefill-b1 | prefill-long | chunk-prefill-b16 | pre-attn-b128."""
     import __graft_entry__
 
     pkg = __graft_entry__.load_package()
@@ -529,9 +529,11 @@ def run_case(args):
             pkg.flash_attn_with_kvcache(w.q, w.k_cache, w.v_cache, cache_seqlens=w.cache_seqlens,
                                         block_table=w.block_table, causal=True)
         info = {"kv_bytes": w.kv_bytes}
-    elif args.case in ("prefill-b16", "prefill-b1"):
-        B = 16 if args.case == "prefill-b16" else 1
-        w = W.prefill_batch(B, CTX_LO, CTX_HI, seed=3, device=dev)
+    elif args.case in ("prefill-b16", "prefill-b1", "prefill-long"):
+        if args.case == "prefill-long":  # 4 prompts of 8192 tokens: the steady state of the kernel
+            w = W.prefill_batch(4, 8192, 8192, seed=5, device=dev)
+        else:
+            w = W.prefill_batch(16 if args.case == "prefill-b16" else 1, CTX_LO, CTX_HI, seed=3, device=dev)
         mx = int(w.lengths.max())
         for _ in range(reps):
             pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx, causal=True)

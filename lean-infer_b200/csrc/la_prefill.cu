@@ -376,11 +376,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!wait_all(&s_free[i], (cs[i] & 1) ^ 1u)) return false;  // PV_i of the previous tile done
         tc_fence_after();
         if (lane == 0) {
-          const uint8_t* qt = sQ + i * kQTile;
+          // k-step ks: descriptor start address + (64-dim half, 32-byte step) / 16
+          const uint64_t ad = desc_kmajor(sQ + i * kQTile, kQHalf, 0), bd = desc_kmajor(kt, kKVHalf, 0);
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks)
-            umma_f16_ss(tmem + i * 128, desc_kmajor(qt, kQHalf, ks), desc_kmajor(kt, kKVHalf, ks), kIdescQK,
-                        ks > 0 ? 1u : 0u);
+            umma_f16_ss(tmem + i * 128, ad + (((ks >> 2) * kQHalf + (ks & 3) * 32) >> 4),
+                        bd + (((ks >> 2) * kKVHalf + (ks & 3) * 32) >> 4), kIdescQK, ks > 0 ? 1u : 0u);
           umma_commit(&s_full[i]);
         }
         __syncwarp();
@@ -396,9 +397,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         if (lane == 0) {
           const uint32_t pt = tmem + i * 128;  // P_i: 16 keys per 8 columns
+          const uint64_t vd = desc_v(vt, 0);   // k-step ks: + 2048 B / 16
 #pragma unroll
           for (int ks = 0; ks < kKeys / 16; ++ks)
-            umma_f16_ts(tmem + kColO + i * 128, pt + ks * 8, desc_v(vt, ks), kIdescPV, (j > 0 || ks > 0) ? 1u : 0u);
+            umma_f16_ts(tmem + kColO + i * 128, pt + ks * 8, vd + ks * 128, kIdescPV, (j > 0 || ks > 0) ? 1u : 0u);
           umma_commit(&s_free[i]);
         }
         __syncwarp();
@@ -576,23 +578,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         float mx[8];
 #pragma unroll
         for (int a = 0; a < 8; ++a) mx[a] = NEG_INF;
-        if (__all_sync(0xffffffffu, nvis >= kKeys)) {  // whole tile visible: no mask
+        const bool whole = __all_sync(0xffffffffu, nvis >= kKeys);  // whole tile visible: no mask
+        if (whole) {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[c][e]);
+            for (int e = 0; e < 32; e += 2) mx[(e >> 1) & 7] = fmax3(mx[(e >> 1) & 7], sv[c][e], sv[c][e + 1]);
         } else {
 #pragma unroll
           for (int c = 0; c < 4; ++c)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float x = (c * 32 + e < nvis) ? sv[c][e] : NEG_INF;
-              sv[c][e] = x;
-              mx[e & 7] = fmaxf(mx[e & 7], x);
+            for (int e = 0; e < 32; e += 2) {
+              const float x0 = (c * 32 + e < nvis) ? sv[c][e] : NEG_INF;
+              const float x1 = (c * 32 + e + 1 < nvis) ? sv[c][e + 1] : NEG_INF;
+              sv[c][e] = x0;
+              sv[c][e + 1] = x1;
+              mx[(e >> 1) & 7] = fmax3(mx[(e >> 1) & 7], x0, x1);
             }
         }
-        const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * sl2;
+        const float mt = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7])) * sl2;
         const float m_new = (mt > m + 8.f) ? mt : m;
         // A row that has seen no key yet keeps m = -inf: use 0 as its
         // reference so P and alpha come out 0 instead of NaN.
@@ -602,22 +606,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         // P = exp2(S*scale*log2e - m) -> bf16 pairs over the first 64 columns
         // of S_i, one 64-key half at a time (S values become packed P as
         // they are used, which keeps the live registers near one S row).
-        float ps[8];
+        // Scale and shift (and later sum) in packed pairs; 2^x on the MUFU
+        // unit. (Moving part of the exponentials to an FMA-pipe polynomial
+        // was measured slower: the softmax is issue-bound, not MUFU-bound.)
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(neg_m, neg_m);
+        uint64_t acc2[4];
 #pragma unroll
-        for (int a = 0; a < 8; ++a) ps[a] = 0.f;
+        for (int a = 0; a < 4; ++a) acc2[a] = 0ull;
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2) {
           float pk[32];
 #pragma unroll
           for (int x = 0; x < 32; ++x) {
-            const float e0 = ex2(fmaf(sv[2 * c2 + (x >> 4)][(x & 15) * 2], sl2, neg_m));  // masked: -inf -> 0
-            const float e1 = ex2(fmaf(sv[2 * c2 + (x >> 4)][(x & 15) * 2 + 1], sl2, neg_m));
-            ps[(2 * x) & 7] += e0;
-            ps[(2 * x + 1) & 7] += e1;
+            const uint64_t y2 =
+                f2_fma(f2_pack(sv[2 * c2 + (x >> 4)][(x & 15) * 2], sv[2 * c2 + (x >> 4)][(x & 15) * 2 + 1]), sl2x2, negm2);
+            float e0, e1;
+            f2_unpack(y2, e0, e1);
+            e0 = ex2(e0);  // masked: -inf -> 0
+            e1 = ex2(e1);
+            acc2[x & 3] = f2_add(acc2[x & 3], f2_pack(e0, e1));
             pk[x] = __uint_as_float(pack_bf16x2(e0, e1));
           }
           tmem_st32(taddr + colS + c2 * 32, pk);
         }
+        float ps[8];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) f2_unpack(acc2[a], ps[2 * a], ps[2 * a + 1]);
         const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         l = l * alpha + rs;
         // O_i holds PV of tiles < j (S_i(j) was issued after PV_i(j-1)
