@@ -272,8 +272,8 @@ int la_prefill_varlen(
  * through block_table row s (the chunk's own keys already written there, e.g.
  * by la_qk_norm_rope_paged_write). Causal masking is bottom-right aligned:
  * query i of n sees key j iff j <= i + cache_seqlens[s] - n; a row that sees
- * no key is written as zeros (lse -inf). block_size: a multiple of 64, or 16
- * or 32. Pool slots past a sequence's last key are never used (they may hold
+ * no key is written as zeros (lse -inf). block_size: a multiple of 128, or
+ * 16, 32 or 64. Pool slots past a sequence's last key are never used (they may hold
  * anything, NaN included). out [total_q, Hq, D]; softmax_lse (nullable)
  * [Hq, total_q], natural log. Block ids outside [0, num_blocks) and keys past
  * the block table are reported on dev_error and read as zeros.

@@ -137,7 +137,8 @@ def flash_attn_with_kvcache(
     decode kernel. q_len > 1 (chunked prefill, q [B, Sq, Hq, D], the chunk's
     keys already in the cache) runs the tcgen05 prefill kernel over the paged
     keys, causal masking bottom-right aligned (query i sees keys
-    0..cache_seqlens[b] - Sq + i); block_size then a multiple of 64, or 16/32.
+    0..cache_seqlens[b] - Sq + i); block_size then a multiple of 128, or
+    16, 32 or 64.
 
     q: [B, Sq, Hq, D] bf16. k_cache / v_cache: [num_blocks, block_size, Hkv, D]
     bf16 with block_table [B, max_blocks] int32, or [B, S, Hkv, D] without a
