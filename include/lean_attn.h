@@ -88,6 +88,11 @@ int la_init(int device);
  * to k_cache / v_cache at block_table[s][col / block_size], col % block_size.
  * k_out (nullable) also receives the normed, rotated k as [num_tokens, Hkv, D]
  * (the fresh keys a prefill attends to, model.py:56-57).
+ * A sequence whose seq_start_pos is negative is idle: nothing is written to
+ * the cache, its rows of q_out (and k_out) are zeros and no error is raised.
+ * With cache_seqlens 0 for such a row, la_paged_decode returns zeros for it,
+ * so idle batch rows need no trash block (the reference points them at block
+ * 0 with position 0 and context 1, llm_engine.py:67-69, which also works).
  * ------------------------------------------------------------------------ */
 int la_qk_norm_rope_paged_write(
     const void* q, int64_t q_token_stride, int64_t q_head_stride,

@@ -144,6 +144,15 @@ __global__ void __launch_bounds__(kWarps * 32) qk_norm_rope_write_kernel(const P
   }
   const long long col = p.pos[s] + t;
   const int d0 = lane * 4;
+  if (p.pos[s] < 0) {  // idle sequence: no cache write, zero outputs, no error
+    const float z[4] = {0.f, 0.f, 0.f, 0.f};
+    if (r < p.hq) {
+      store4(p.qo + tok * p.qo_ts + r * p.qo_hs + d0, z);
+    } else if (r < p.hq + p.hkv && p.ko) {
+      store4(p.ko + tok * p.ko_ts + (r - p.hq) * p.ko_hs + d0, z);
+    }
+    return;
+  }
 
   if (r < p.hq) {  // q row: norm + rope -> q_out
     float c[4], sn[4], w[4], x[4];

@@ -227,3 +227,103 @@ class DecodeGraph:
 
     def release(self) -> None:
         self.graph = None
+
+
+class BucketedDecodeGraph:
+    """Decode steps captured for several batch sizes over one set of static
+    buffers. The reference captures a single graph at B = n_slots and points
+    idle rows at the trash block 0 with position 0 and context 1
+    (llm_engine.py:23-86); here a step replays the smallest captured bucket
+    that holds the active rows, and the idle rows inside that bucket are
+    masked — start position -1 and context 0 — so they write no cache slot
+    (la_qk_norm_rope_paged_write skips them) and attend to nothing
+    (la_paged_decode returns zeros): no trash block is needed and a small
+    batch does not pay for n_slots rows."""
+
+    def __init__(self, model: Qwen3ForCausalLM, cache: BlockCache, buckets, max_blocks: int) -> None:
+        self.model, self.cache = model, cache
+        self.buckets = sorted({int(b) for b in buckets})
+        if not self.buckets or self.buckets[0] <= 0:
+            raise ValueError("buckets must be positive batch sizes")
+        n = self.buckets[-1]
+        dev = cache.device
+        self.host_ids = torch.zeros(n, 1, dtype=torch.long, pin_memory=True)
+        self.host_pos = torch.full((n,), -1, dtype=torch.long, pin_memory=True)
+        self.host_bt = torch.zeros(n, max_blocks, dtype=torch.int32, pin_memory=True)
+        self.host_ctx = torch.zeros(n, dtype=torch.int32, pin_memory=True)
+        self.ids = torch.zeros(n, 1, dtype=torch.long, device=dev)
+        self.pos = torch.full((n,), -1, dtype=torch.long, device=dev)
+        self.bt = torch.zeros(n, max_blocks, dtype=torch.int32, device=dev)
+        self.ctx = torch.zeros(n, dtype=torch.int32, device=dev)
+        self.graphs: dict[int, tuple] = {}
+        self.bucket = n
+        self.active = 0
+        model.rope(max_blocks * cache.block_size)
+
+    def bucket_for(self, rows: int) -> int:
+        for b in self.buckets:
+            if b >= rows:
+                return b
+        raise ValueError(f"{rows} active rows exceed the largest bucket {self.buckets[-1]}")
+
+    def h2d_bytes(self, bucket: int) -> int:
+        return bucket * (8 + 8 + 4 + self.host_bt.shape[1] * 4)
+
+    def _forward(self, b: int):
+        logits = self.model(self.ids[:b], self.cache, self.bt[:b], self.pos[:b], self.ctx[:b])
+        return logits, logits[:, -1].argmax(-1)
+
+    def capture(self) -> None:
+        """Three warm-up forwards per bucket on a side stream, then one graph
+        per bucket (all rows idle while capturing: nothing is written)."""
+        self.pos.fill_(-1)
+        self.ctx.zero_()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for b in self.buckets:
+                for _ in range(3):
+                    self._forward(b)
+        torch.cuda.current_stream().wait_stream(side)
+        for b in self.buckets:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                logits, nxt = self._forward(b)
+            self.graphs[b] = (g, logits, nxt)
+
+    def stage(self, ids, pos, bt, ctx) -> int:
+        """Stage the active rows (the first len(ids) rows) and mask the rest
+        of the chosen bucket; returns the bucket."""
+        n = int(ids.shape[0])
+        b = self.bucket_for(n)
+        self.host_ids[:n].copy_(ids.view(n, 1))
+        self.host_ids[n:b].zero_()
+        self.host_pos[:n].copy_(pos)
+        self.host_pos[n:b].fill_(-1)
+        self.host_bt[:b].zero_()
+        self.host_bt[:n, : bt.shape[1]].copy_(bt)
+        self.host_ctx[:n].copy_(ctx)
+        self.host_ctx[n:b].zero_()
+        self.active, self.bucket = n, b
+        return b
+
+    def step(self) -> list[int]:
+        """H2D copy of the bucket's staged rows, replay of its graph, D2H of
+        the active rows' next tokens."""
+        b = self.bucket
+        if not self.graphs:
+            self.capture()
+        self.ids[:b].copy_(self.host_ids[:b], non_blocking=True)
+        self.pos[:b].copy_(self.host_pos[:b], non_blocking=True)
+        self.bt[:b].copy_(self.host_bt[:b], non_blocking=True)
+        self.ctx[:b].copy_(self.host_ctx[:b], non_blocking=True)
+        g, _, nxt = self.graphs[b]
+        g.replay()
+        return nxt[: self.active].tolist()
+
+    def logits(self) -> torch.Tensor:
+        """Logits of the last step's active rows [n, 1, vocab]."""
+        return self.graphs[self.bucket][1][: self.active]
+
+    def release(self) -> None:
+        self.graphs = {}

@@ -135,13 +135,21 @@ def qk_norm_rope_paged_write(q, k, v, q_norm_weight, k_norm_weight, eps, cos_tab
     norm="reference" uses torch's rms_norm (the reference module)."""
     nf = rms_norm_kernel_order if norm == "kernel" else rms_norm_reference
     seq, positions = token_positions(pos, q_len, cu_seqlens)
+    # A negative start position marks an idle sequence: no cache write, zero
+    # outputs (the kernel's contract; the reference engine uses a trash block
+    # instead, llm_engine.py:67-69).
+    idle = torch.as_tensor(pos).long().reshape(-1)[seq] < 0
+    positions = torch.where(idle, torch.zeros_like(positions), positions)
     qn = nf(q, q_norm_weight, eps)
     kn = nf(k, k_norm_weight, eps)
     q_out = rope_from_tables(qn, cos_tab, sin_tab, positions)
     k_out = rope_from_tables(kn, cos_tab, sin_tab, positions)
+    q_out = torch.where(idle[:, None, None], torch.zeros_like(q_out), q_out)
+    k_out = torch.where(idle[:, None, None], torch.zeros_like(k_out), k_out)
+    live = ~idle
     bs = k_cache.shape[1]
-    phys = block_table.long()[seq, positions // bs]
-    off = positions % bs
-    k_cache[phys, off] = k_out
-    v_cache[phys, off] = v
+    phys = block_table.long()[seq[live], positions[live] // bs]
+    off = positions[live] % bs
+    k_cache[phys, off] = k_out[live]
+    v_cache[phys, off] = v[live]
     return q_out, k_out

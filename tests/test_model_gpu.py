@@ -103,3 +103,56 @@ def test_prefill_then_graph_decode_matches_reference_model(pkg, cuda_dev):
         pos = pos + 1
     pkg.check_device_errors(cuda_dev.index)
     dg.release()
+
+
+def test_bucketed_decode_graph_masks_idle_rows(pkg, cuda_dev):
+    """5 active rows replayed in the 8-row bucket: the same logits as a plain
+    5-row decode graph, and the 3 masked rows write no cache slot (no trash
+    block: block 0 and every unused block keep their bytes)."""
+    from lean_infer_b200 import qwen3
+    from lean_infer_b200.cache import BlockAllocator, BlockCache
+
+    cfg = qwen3.ModelConfig(num_hidden_layers=2, vocab_size=4096)
+    model = qwen3.random_model(cfg, cuda_dev, seed=9)
+    NB, BS = 40, 256
+    cache_a = BlockCache(cfg.num_hidden_layers, NB, BS, 8, 128, cuda_dev)
+    g = torch.Generator(device=cuda_dev).manual_seed(10)
+    cache_a.k.copy_(torch.randn(cache_a.k.shape, generator=g, device=cuda_dev).to(torch.bfloat16))
+    cache_a.v.copy_(torch.randn(cache_a.v.shape, generator=g, device=cuda_dev).to(torch.bfloat16))
+    cache_b = BlockCache(cfg.num_hidden_layers, NB, BS, 8, 128, cuda_dev)
+    cache_b.k.copy_(cache_a.k)
+    cache_b.v.copy_(cache_a.v)
+    k0, v0 = cache_a.k.clone(), cache_a.v.clone()
+    lens = [100, 300, 1000, 7, 520]
+    alloc = BlockAllocator(NB)
+    tables = [alloc.allocate(-(-(L + 2) // BS)) for L in lens]
+    max_blocks = max(len(t) for t in tables)
+    bt = torch.zeros(len(lens), max_blocks, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, : len(t)] = torch.tensor(t)
+    used = sorted({b for t in tables for b in t})
+    unused = [b for b in range(NB) if b not in used]
+    ids = torch.randint(0, cfg.vocab_size, (len(lens), 1), generator=torch.Generator().manual_seed(11))
+    pos = torch.tensor(lens, dtype=torch.long)
+    ctx = (pos + 1).to(torch.int32)
+
+    ref = qwen3.DecodeGraph(model, cache_b, len(lens), max_blocks)
+    ref.stage(ids, pos, bt, ctx)
+    toks_ref = ref.step()
+    bg = qwen3.BucketedDecodeGraph(model, cache_a, [2, 8, 16], max_blocks)
+    assert bg.stage(ids, pos, bt, ctx) == 8
+    toks = bg.step()
+    torch.cuda.synchronize()
+    pkg.check_device_errors(cuda_dev.index)
+    la, lb = bg.logits()[:, 0].float(), ref.logits[:, 0].float()
+    assert ((la - lb).norm() / lb.norm()).item() <= 1e-2
+    assert sum(int(a == b) for a, b in zip(toks, toks_ref)) >= 4
+    for blk in unused:  # block 0 included: idle rows wrote nothing
+        assert torch.equal(cache_a.k[:, blk], k0[:, blk]) and torch.equal(cache_a.v[:, blk], v0[:, blk])
+    # the active rows did write their slot
+    assert not torch.equal(cache_a.k[:, bt[0, 0]], k0[:, bt[0, 0]])
+    # a 2-row step uses the 2-row bucket
+    assert bg.stage(ids[:2], pos[:2] + 1, bt[:2], ctx[:2] + 1) == 2
+    assert len(bg.step()) == 2
+    ref.release()
+    bg.release()

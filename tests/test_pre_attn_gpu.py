@@ -176,3 +176,27 @@ def test_bad_block_id_skips_write_and_reports(pkg, cuda_dev):
     opre.qk_norm_rope_paged_write(q[keep], k[keep], v[keep], qw, kw, 1e-6, cos, sin, pos[keep], bt[keep], kr, vr,
                                   q_len=1)
     assert torch.equal(kc.cpu(), kr) and torch.equal(vc.cpu(), vr)
+
+
+@pytest.mark.parametrize("q_len", [1, 33])
+def test_idle_rows_write_nothing(pkg, cuda_dev, q_len):
+    """A negative start position marks an idle row: its cache slots stay
+    untouched (no trash block needed), its q / k outputs are zeros, no error."""
+    B = 12
+    q, k, v, qw, kw, pos, bt, cu, pool = _random_case(B, q_len, seed=5 + q_len, bs=256, nb=400, max_pos=4096)
+    pos = pos.clone()
+    pos[1::3] = -1
+    cos, sin = opre.rope_tables(4096, 128, 1e6)
+    kc, vc = pool.clone().to(cuda_dev), pool.clone().to(cuda_dev)
+    d = cuda_dev
+    k_out = torch.empty_like(k).to(d)
+    q_out = pkg.qk_norm_rope_paged_write(q.to(d), k.to(d), v.to(d), qw.to(d), kw.to(d), cos.to(d), sin.to(d),
+                                         pos.to(d), bt.to(d), kc, vc, k_out=k_out)
+    torch.cuda.synchronize()
+    pkg.check_device_errors(d.index)  # idle rows raise nothing
+    kr, vr = pool.clone(), pool.clone()
+    q_ref, k_ref = opre.qk_norm_rope_paged_write(q, k, v, qw, kw, 1e-6, cos, sin, pos, bt, kr, vr, q_len=q_len)
+    assert torch.equal(q_out.cpu(), q_ref) and torch.equal(k_out.cpu(), k_ref)
+    assert torch.equal(kc.cpu(), kr) and torch.equal(vc.cpu(), vr)
+    idle_tok = (pos < 0).repeat_interleave(q_len)
+    assert torch.count_nonzero(q_out.cpu()[idle_tok]) == 0
