@@ -407,7 +407,9 @@ def run_ours(args):
     for _ in range(args.warmup):
         dg.replay()
     torch.cuda.synchronize()
-    launches_per_step = cfg.num_hidden_layers * 3  # fused pre-attention, decode, combine
+    # per layer: fused pre-attention, decode, combine, two add+RMSNorm, SiLU*mul;
+    # plus the first layer's input RMSNorm
+    launches_per_step = cfg.num_hidden_layers * 6 + 1
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()

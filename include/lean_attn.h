@@ -297,6 +297,22 @@ int la_prefill_paged(
     float* softmax_lse,
     int* dev_error, cudaStream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Decode-step glue (one launch each; no counterpart in the attention path).
+ * la_add_rms_norm: h' = bf16(h + a) (a nullable: h' = h), written to h_out
+ * (nullable; may alias h), and x_out = bf16(h' * rsqrt(mean(h'^2) + eps) * w)
+ * computed in fp32 — the residual add closing a sub-layer and the nn.RMSNorm
+ * opening the next (leaninfer/qwen3/model.py:80-83, 75-76, 92). bf16 rows of
+ * n elements (n a multiple of 8, at most 4096), 16-byte aligned rows.
+ * la_silu_mul: out = bf16(SiLU(gate) * up) from gate_up [rows, 2n] = gate |
+ * up (Qwen3MLP with a fused gate/up projection, model.py:32-33).
+ * ------------------------------------------------------------------------ */
+int la_add_rms_norm(const void* h, int64_t h_row_stride, const void* a, int64_t a_row_stride,
+                    void* h_out, int64_t h_out_row_stride, void* x_out, int64_t x_out_row_stride,
+                    const void* weight, int64_t rows, int n, float eps, cudaStream_t stream);
+int la_silu_mul(const void* gate_up, int64_t gate_up_row_stride, void* out, int64_t out_row_stride,
+                int64_t rows, int n, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -11,7 +11,9 @@ confined to how the work is launched:
     of qk_norm_rope_paged_write, with rope from a position-indexed table
     instead of build_rope per forward (model.py:98);
   * decode attention (model.py:60-67) is flash_attn_with_kvcache from this
-    package; prefill attention (model.py:56-57) is flash_attn_varlen_func.
+    package; prefill attention (model.py:56-57) is flash_attn_varlen_func;
+  * each residual add and the RMSNorm after it are one launch
+    (add_rms_norm), and SiLU(gate) * up is one launch (silu_mul).
 Weights are random-init bf16 (no checkpoint is loaded: the benchmark runs on
 synthetic data).
 """
@@ -23,8 +25,40 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+import ctypes
+
+from . import _lib
 from . import flash_attn_interface as fai
 from .cache import BlockCache
+
+
+def add_rms_norm(h: torch.Tensor, a: torch.Tensor | None, weight: torch.Tensor, eps: float,
+                 inplace: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+    """(h + a, RMSNorm(h + a) * weight) for bf16 rows [T, n] in one launch
+    (la_add_rms_norm); with a None: (h, RMSNorm(h) * weight). The sum is
+    written into h when inplace."""
+    T, n = h.shape
+    x = torch.empty_like(h)
+    h_out = (h if inplace else torch.empty_like(h)) if a is not None else None
+    if T:
+        _lib.call("la_add_rms_norm", ctypes.c_void_p(h.data_ptr()), h.stride(0),
+                  ctypes.c_void_p(a.data_ptr() if a is not None else 0), a.stride(0) if a is not None else n,
+                  ctypes.c_void_p(h_out.data_ptr() if h_out is not None else 0),
+                  h_out.stride(0) if h_out is not None else n, ctypes.c_void_p(x.data_ptr()), x.stride(0),
+                  ctypes.c_void_p(weight.data_ptr()), T, n, ctypes.c_float(eps),
+                  ctypes.c_void_p(torch.cuda.current_stream(h.device).cuda_stream))
+    return (h_out if h_out is not None else h), x
+
+
+def silu_mul(gate_up: torch.Tensor, n: int) -> torch.Tensor:
+    """SiLU(gate_up[:, :n]) * gate_up[:, n:] in one launch (la_silu_mul)."""
+    T = gate_up.shape[0]
+    out = torch.empty(T, n, dtype=gate_up.dtype, device=gate_up.device)
+    if T:
+        _lib.call("la_silu_mul", ctypes.c_void_p(gate_up.data_ptr()), gate_up.stride(0),
+                  ctypes.c_void_p(out.data_ptr()), out.stride(0), T, n,
+                  ctypes.c_void_p(torch.cuda.current_stream(gate_up.device).cuda_stream))
+    return out
 
 
 @dataclass(frozen=True)
@@ -90,8 +124,7 @@ class Qwen3MLP(nn.Module):
         self.inter = cfg.intermediate_size
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        gu = self.gate_up_proj(x)
-        return self.down_proj(F.silu(gu[:, : self.inter]) * gu[:, self.inter:])
+        return self.down_proj(silu_mul(self.gate_up_proj(x), self.inter))
 
 
 class Qwen3DecoderLayer(nn.Module):
@@ -103,11 +136,15 @@ class Qwen3DecoderLayer(nn.Module):
         self.post_attention_layernorm = nn.Parameter(torch.ones(cfg.hidden_size))
         self.eps = cfg.rms_norm_eps
 
-    def forward(self, h, cache, layer, block_tables, pos, cache_seqlens, rope, cu_seqlens=None, max_seqlen=0):
-        x = F.rms_norm(h, (h.shape[-1],), self.input_layernorm, self.eps)
-        h = h + self.self_attn(x, cache, layer, block_tables, pos, cache_seqlens, rope, cu_seqlens, max_seqlen)
-        x = F.rms_norm(h, (h.shape[-1],), self.post_attention_layernorm, self.eps)
-        return h + self.mlp(x)
+    def forward(self, h, x, next_norm, cache, layer, block_tables, pos, cache_seqlens, rope, cu_seqlens=None,
+                max_seqlen=0):
+        """h: residual stream [T, hidden]; x = RMSNorm(h) * input_layernorm
+        (produced by the previous layer's last fused add). Returns the new h
+        and RMSNorm(h) * next_norm (the next layer's input norm, or the
+        model's final norm)."""
+        a = self.self_attn(x, cache, layer, block_tables, pos, cache_seqlens, rope, cu_seqlens, max_seqlen)
+        h, x = add_rms_norm(h, a, self.post_attention_layernorm, self.eps)
+        return add_rms_norm(h, self.mlp(x), next_norm, self.eps)
 
 
 class Qwen3ForCausalLM(nn.Module):
@@ -137,10 +174,12 @@ class Qwen3ForCausalLM(nn.Module):
         ids = input_ids.reshape(-1)
         h = self.embed_tokens(ids)
         rope = self._rope if self._rope is not None else self.rope(4096)
+        eps = self.config.rms_norm_eps
+        _, x = add_rms_norm(h, None, self.layers[0].input_layernorm, eps)
         for i, layer in enumerate(self.layers):
-            h = layer(h, cache, i, block_tables, pos, cache_seqlens, rope, cu_seqlens, max_seqlen)
-        h = F.rms_norm(h, (h.shape[-1],), self.norm, self.config.rms_norm_eps)
-        logits = F.linear(h, self.embed_tokens.weight)
+            nxt = self.layers[i + 1].input_layernorm if i + 1 < len(self.layers) else self.norm
+            h, x = layer(h, x, nxt, cache, i, block_tables, pos, cache_seqlens, rope, cu_seqlens, max_seqlen)
+        logits = F.linear(x, self.embed_tokens.weight)  # x = final RMSNorm(h) * norm
         return logits.view(input_ids.shape[0], -1, logits.shape[-1]) if cache_seqlens is not None else logits
 
 

@@ -92,3 +92,19 @@ def test_argument_errors_before_launch(pkg):
     assert paged(bs=48) == 2
     assert paged(T=9) == 1
     assert paged(q_len=0, T=0) == 0  # nothing to do
+
+
+def test_glue_argument_checks(pkg):
+    """The fused glue kernels validate before launching (no GPU needed)."""
+    from lean_infer_b200 import _lib
+
+    lib = _lib.load()
+    null = ctypes.c_void_p(0)
+    fake = ctypes.c_void_p(1 << 20)
+    # a null addend is allowed: only the given pointers' strides are checked
+    assert lib.la_add_rms_norm(fake, 1024, null, 0, null, 0, fake, 1024, fake, 0, 1024, ctypes.c_float(1e-6), null) == 0
+    assert lib.la_add_rms_norm(null, 1024, null, 0, null, 0, fake, 1024, fake, 4, 1024, ctypes.c_float(1e-6), null) == 1
+    assert lib.la_add_rms_norm(fake, 1024, null, 0, null, 0, fake, 1024, fake, 4, 1020, ctypes.c_float(1e-6), null) == 2
+    assert lib.la_add_rms_norm(fake, 1000, null, 0, null, 0, fake, 1024, fake, 4, 1024, ctypes.c_float(1e-6), null) == 3
+    assert lib.la_silu_mul(fake, 6144, fake, 3072, 0, 3072, null) == 0
+    assert lib.la_silu_mul(fake, 6000, fake, 3072, 4, 3072, null) == 3
