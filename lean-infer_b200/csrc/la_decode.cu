@@ -282,11 +282,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         d.flags = flags;
         d.slot = 2 * static_cast<int>(blockIdx.x) + (pb <= u0 ? 0 : 1);
         descs[s] = d;
-        const uint32_t bytes = static_cast<uint32_t>(__popc(act)) * (2 * kWarpBytes) + p.q_bytes;
+        // Q is read only on a sequence's first unit (kFlagFirst): load it there.
+        const bool first = (flags & kFlagFirst) != 0;
+        const uint32_t bytes = static_cast<uint32_t>(__popc(act)) * (2 * kWarpBytes) + (first ? p.q_bytes : 0u);
         mbar_arrive_expect_tx(&full[s], bytes);
-        uint8_t* qs = st + 2 * kKVBytes;
-        tma_load_3d(qs, &tm_q, &full[s], 0, 0, b);
-        tma_load_3d(qs + p.q_half_bytes, &tm_q, &full[s], 64, 0, b);
+        if (first) {
+          uint8_t* qs = st + 2 * kKVBytes;
+          tma_load_3d(qs, &tm_q, &full[s], 0, 0, b);
+          tma_load_3d(qs + p.q_half_bytes, &tm_q, &full[s], 64, 0, b);
+        }
       }
       __syncwarp();
       if (phys < 0) phys = -1;  // outside the pool: TMA fills zeros
