@@ -568,8 +568,10 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
   const int lane = threadIdx.x;
   const float NEG_INF = -__int_as_float(0x7f800000);
 
-  grid_dependency_wait();
-  // T (all units) and P_b (units before sequence b).
+  // T (all units) and P_b (units before sequence b). They depend only on
+  // cache_seqlens, which were final before the decode grid started (it does
+  // not write them), so they are computed while that grid still runs; every
+  // CTA waits for it before touching outputs or partials.
   long long T = 0, Pb = 0;
   for (int base = 0; base < p.batch; base += 32) {
     const int bb = base + lane;
@@ -588,6 +590,7 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
   const long long oofs = static_cast<long long>(b) * p.out_b_stride + static_cast<long long>(hh) * p.out_h_stride +
                          lane * 4;
   float* lse = p.lse_out ? p.lse_out + static_cast<long long>(b) * p.hq + hh : nullptr;
+  grid_dependency_wait();
 
   if (nb == 0) {
     for (int r = 0; r < p.nouts; ++r) *reinterpret_cast<uint2*>(p.outs[r] + oofs) = make_uint2(0u, 0u);
