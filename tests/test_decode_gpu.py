@@ -82,9 +82,12 @@ def test_empty_rows_are_zero(pkg, cuda_dev):
     assert (out.float() - ref).abs().max().item() <= TOL
 
 
-def test_many_short_sequences(pkg, cuda_dev):
-    """More sequences than CTAs: most are finished inside one CTA."""
-    run_case(pkg, cuda_dev, 300, 1, 300, nb=None, seed=5)
+@pytest.mark.parametrize("B", [256, 257, 300])
+def test_many_short_sequences(pkg, cuda_dev, B):
+    """More sequences than CTAs: most are finished inside one CTA. Up to 256
+    sequences the split is computed from lengths held in registers, above
+    that by the scan over the lengths in memory: both sides of the edge."""
+    run_case(pkg, cuda_dev, B, 1, 300, nb=None, seed=5)
 
 
 @pytest.mark.parametrize("bs", [16, 32, 64, 128])
