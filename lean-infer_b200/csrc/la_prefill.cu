@@ -77,7 +77,8 @@ struct Params {
   const int* cu;  // query starts [num_seqs + 1], or null: sequence s has q_len queries from token s * q_len
   int q_len;
   int num_seqs;
-  int n_qp;  // query-tile pairs of the longest sequence
+  int n_qp;  // items (query-tile pairs, or single tiles) of the longest sequence
+  int pair;  // query tiles per item: 2, or 1 when pairs would leave SMs idle
   int tq;    // tokens per query tile (128 / group)
   int tq_shift;  // log2(tq)
   int hq, hkv, group;
@@ -157,7 +158,7 @@ __device__ __forceinline__ bool seq_has_pair(const Params& p, int s, int q0) {
 // Items at one level (warp-collective).
 __device__ __forceinline__ int level_count(const Params& p, int level) {
   const int lane = threadIdx.x & 31;
-  const int q0 = level * 2 * p.tq;
+  const int q0 = level * p.pair * p.tq;
   int n = 0;
   for (int b = 0; b < p.num_seqs; b += 32) n += __popc(__ballot_sync(0xffffffffu, seq_has_pair(p, b + lane, q0)));
   return n * p.hkv;
@@ -191,7 +192,7 @@ __device__ __forceinline__ bool walker_next(const Params& p, Walker& w, Item& it
   }
   const int idx = static_cast<int>(r - w.base);
   const int ord = idx / p.hkv;  // the ord-th sequence (index order) that has this level's pair
-  const int q0 = w.level * 2 * p.tq;
+  const int q0 = w.level * p.pair * p.tq;
   int seen = 0, s = 0;
   for (int b = 0; b < p.num_seqs; b += 32) {
     const unsigned m = __ballot_sync(0xffffffffu, seq_has_pair(p, b + lane, q0));
@@ -211,7 +212,7 @@ __device__ __forceinline__ bool walker_next(const Params& p, Walker& w, Item& it
   it.K = p.paged ? max(p.k_lens[s], 0) : it.L;
   it.off = it.K - it.L;
   it.q0 = q0;
-  it.has1 = it.L > q0 + p.tq;
+  it.has1 = p.pair == 2 && it.L > q0 + p.tq;
   it.n0 = kv_tiles(p, it, q0);
   it.n1 = it.has1 ? kv_tiles(p, it, q0 + p.tq) : 0;
   it.n = max(it.n0, it.n1);
@@ -331,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       long long nld = 0;  // K/V tiles loaded
       bool ok = true;
       while (ok && walker_next(p, w, it)) {
-        if (lane == 0 && it.q0 + 2 * p.tq >= p.n_qp * 2 * p.tq && it.L > p.n_qp * 2 * p.tq && p.err)
+        if (lane == 0 && it.q0 + p.pair * p.tq >= p.n_qp * p.pair * p.tq && it.L > p.n_qp * p.pair * p.tq && p.err)
           atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);  // longer than max_seqlen: the tail is not computed
         if (!(ok = wait_all(q_empty, (kq & 1) ^ 1u))) break;
         if (lane == 0) {
@@ -685,13 +686,23 @@ namespace la {
 namespace prefill {
 
 // Common tail of the two entry points: the persistent grid over the items.
-static int launch(const CUtensorMap& tq_map, const CUtensorMap& tk_map, const CUtensorMap& tv_map, const Params& p,
-                  cudaStream_t stream) {
-  const long long items = static_cast<long long>(p.n_qp) * p.num_seqs * p.hkv;
-  if (items > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
+// n_qt: query tiles of the longest sequence. Items are pairs of query tiles
+// (the two tiles share every K/V tile); when even the upper bound on the
+// pair count cannot fill the SMs (one short prompt), items are single tiles:
+// twice as many items, each half as long.
+static int launch(const CUtensorMap& tq_map, const CUtensorMap& tk_map, const CUtensorMap& tv_map, Params p,
+                  int n_qt, cudaStream_t stream) {
   const int device = current_device();
   const int sms = device >= 0 ? num_sms(device) : 0;
   if (sms <= 0) return LA_ERR_CUDA;
+  p.pair = 2;
+  p.n_qp = (n_qt + 1) / 2;
+  if (static_cast<long long>(p.n_qp) * p.num_seqs * p.hkv < sms) {
+    p.pair = 1;
+    p.n_qp = n_qt;
+  }
+  const long long items = static_cast<long long>(p.n_qp) * p.num_seqs * p.hkv;
+  if (items > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
   const long long ctas = sms;  // one persistent CTA per SM (all of its TMEM and most of its shared memory)
   const dim3 grid(static_cast<unsigned>(items < ctas ? items : ctas));
   return cuda_status(launch_pdl(prefill_kernel, grid, dim3(kThreads), kSmemBytes, stream, tq_map, tk_map, tv_map, p));
@@ -765,11 +776,11 @@ extern "C" int la_prefill_varlen(const void* q, int64_t q_token_stride, int64_t 
   }
   p.cu = cu_seqlens;
   p.num_seqs = num_seqs;
-  p.n_qp = ((max_seqlen + p.tq - 1) / p.tq + 1) / 2;
+  const int n_qt = (max_seqlen + p.tq - 1) / p.tq;
   p.causal = causal ? 1 : 0;
   p.lse = softmax_lse;
   p.err = dev_error;
-  return launch(tq_map, tk_map, tv_map, p, stream);
+  return launch(tq_map, tk_map, tv_map, p, n_qt, stream);
 }
 
 extern "C" int la_prefill_paged(const void* q, int64_t q_token_stride, int64_t q_head_stride, const void* k_cache,
@@ -819,7 +830,7 @@ extern "C" int la_prefill_paged(const void* q, int64_t q_token_stride, int64_t q
   p.cu = cu_seqlens_q;
   p.q_len = q_len;
   p.num_seqs = num_seqs;
-  p.n_qp = ((max_seqlen_q + p.tq - 1) / p.tq + 1) / 2;
+  const int n_qt = (max_seqlen_q + p.tq - 1) / p.tq;
   p.causal = causal ? 1 : 0;
   p.lse = softmax_lse;
   p.err = dev_error;
@@ -831,5 +842,5 @@ extern "C" int la_prefill_paged(const void* q, int64_t q_token_stride, int64_t q
   p.bs = block_size;
   p.box_keys = box_keys;
   p.num_blocks = static_cast<int>(num_blocks);
-  return launch(tq_map, tk_map, tv_map, p, stream);
+  return launch(tq_map, tk_map, tv_map, p, n_qt, stream);
 }
