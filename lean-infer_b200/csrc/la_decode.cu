@@ -136,16 +136,17 @@ __device__ long long total_units(const Params& p, int lane) {
   return tot;
 }
 
-// The split for up to 256 sequences from their lengths held in registers
+// The split for up to 32 x kChunks sequences from their lengths held in registers
 // (lane l holds sequences 32 i + l): total units T, this CTA's range [u0, u1),
 // the sequence b0 it starts in and that sequence's first unit pb0.
 __device__ __forceinline__ long long cta_start(long long c, long long T, long long G);
-__device__ __forceinline__ void split_from_regs(const Params& p, int lane, const int (&un)[8], long long& T,
+template <int kChunks>
+__device__ __forceinline__ void split_from_regs(const Params& p, int lane, const int (&un)[kChunks], long long& T,
                                                 long long& u0, long long& u1, int& b0, long long& pb0) {
   const int chunks = (p.batch + 31) >> 5;
   T = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < kChunks; ++i) {
     if (i < chunks) {
       int n = un[i];
 #pragma unroll
@@ -161,7 +162,7 @@ __device__ __forceinline__ void split_from_regs(const Params& p, int lane, const
   if (u1 <= u0) return;
   long long acc = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < kChunks; ++i) {
     if (i < chunks) {
       const int b = i * 32 + lane;
       const int n = un[i];
@@ -189,7 +190,10 @@ __device__ __forceinline__ long long cta_start(long long c, long long T, long lo
 // CTA whose range contains unit x: floor(((x + 1) * G - 1) / T).
 __device__ __forceinline__ long long cta_of(long long x, long long T, long long G) { return ((x + 1) * G - 1) / T; }
 
-template <int kStages>
+// kChunks: the split is held in registers for up to 32 x kChunks sequences
+// (8 for the engine's batches, 32 for the many short rows of the KV-head-
+// sharded partition).
+template <int kStages, int kChunks>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -227,15 +231,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   // lengths as they are now (read through L2 only, so no stale line stays in
   // L1), then the lengths are read again after the wait: if any changed (the
   // previous kernel wrote them) the split is recomputed from the final ones.
-  const bool spec = p.batch <= 256;
-  int raw[8];
+  const bool spec = p.batch <= 32 * kChunks;
+  int raw[kChunks];
   long long sT = 0, su0 = 0, su1 = 0, spb0 = 0;
   int sb0 = 0;
   if (warp == kCWarps && spec) {
-    int un[8];
+    int un[kChunks];
     const long long cap = static_cast<long long>(p.max_blocks) * p.block_size;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < kChunks; ++i) {
       const int b = i * 32 + lane;
       raw[i] = (b < p.batch) ? __ldcg(p.seqlens + b) : 0;
       const long long c = raw[i] < 0 ? 0 : (raw[i] > cap ? cap : raw[i]);
@@ -250,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool same = spec;
     if (spec) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < kChunks; ++i) {
         const int b = i * 32 + lane;
         if (b < p.batch && __ldcg(p.seqlens + b) != raw[i]) same = false;
       }
@@ -755,9 +759,13 @@ static int grid_for(int device) { return num_sms(device); }
 int decode_init(int device) {
   (void)device;
   const int lim = 227 * 1024;
-  cudaError_t e = cudaFuncSetAttribute(decode::paged_decode_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  cudaError_t e = cudaFuncSetAttribute(decode::paged_decode_kernel<3, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(decode::paged_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    e = cudaFuncSetAttribute(decode::paged_decode_kernel<2, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode::paged_decode_kernel<3, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode::paged_decode_kernel<2, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   if (e == cudaSuccess) {
     cudaFuncAttributes a;
     e = cudaFuncGetAttributes(&a, decode::paged_decode_combine_kernel);
@@ -904,9 +912,11 @@ static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_he
 
   cudaError_t e;
   if (stages == 3)
-    e = launch_pdl(paged_decode_kernel<3>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p);
+    e = batch <= 256 ? launch_pdl(paged_decode_kernel<3, 8>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p)
+                     : launch_pdl(paged_decode_kernel<3, 32>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p);
   else
-    e = launch_pdl(paged_decode_kernel<2>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p);
+    e = batch <= 256 ? launch_pdl(paged_decode_kernel<2, 8>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p)
+                     : launch_pdl(paged_decode_kernel<2, 32>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p);
   if (e != cudaSuccess) return cuda_status(e);
   e = launch_pdl(paged_decode_combine_kernel, dim3(batch, num_q_heads), dim3(32), 0, stream, p, grid);
   return cuda_status(e);
