@@ -11,7 +11,7 @@ KV-head sharding   rank r of P holds kv heads [r*Hkv/P, (r+1)*Hkv/P) of every
                    its heads; the [B, Hq/P, D] outputs are all-gathered over
                    NCCL (NVLink/NVSwitch) into [B, Hq, D] before o_proj.
 
-The reference is single-GPU (SURVEY: no torch.distributed anywhere); these
+The reference is single-GPU (it uses no torch.distributed at all); these
 are the two partitionings its decode step admits.
 """
 from __future__ import annotations

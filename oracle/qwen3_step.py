@@ -1,5 +1,5 @@
 """CPU fp32 restatement of the reference model's decode step — the CPU
-baseline of the benchmark. TEST / BASELINE INFRASTRUCTURE ONLY.
+baseline of the benchmark. Test and CPU-baseline infrastructure only.
 
 Follows leaninfer/qwen3/model.py:25-112 op for op in fp32 on the host cores:
 embedding, per layer input RMSNorm, q/k/v projections, q_norm/k_norm,
