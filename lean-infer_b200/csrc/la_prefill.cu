@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* kv_full = bars + 2;       // [kStages]
   uint64_t* kv_empty = bars + 6;      // [kStages]
   uint64_t* s_full = bars + 10;       // [2] S_i written
-  uint64_t* s_free = bars + 12;       // [2] PV_i done: S_i/P_i columns free, O_i complete
+  uint64_t* s_free = bars + 12;       // [2] PV_i done: O_i complete
   uint64_t* p_full = bars + 14;       // [2] P_i written (128 arrivals)
   uint64_t* o_empty = bars + 16;      // [2] the epilogue has read O_i (128 arrivals)
   uint64_t* st_full = bars + 18;      // [2] row statistics of tile i written (128)
@@ -369,13 +369,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       Item it;
       int kq = 0;
       long long nld = 0;               // K/V ring position of the item's K(0)
-      uint32_t cs[2] = {0, 0};         // S_i issued
       uint32_t cp[2] = {0, 0};         // PV_i issued
       uint32_t items_i[2] = {0, 0};    // items in which tile i ran
       bool ok = true;
+      // S_i(j+1) is written over P_i(j), which PV_i(j) reads: both are issued
+      // by this thread, PV_i(j) first, and the tensor core executes one
+      // thread's MMAs in issue order, so S_i(j+1) is issued right behind
+      // PV_i(j) without waiting for it to complete (waiting left the tensor
+      // core idle for the commit -> mbarrier -> issue round trip).
       auto issue_s = [&](int i, const uint8_t* kt) -> bool {
-        if (!wait_all(&s_free[i], (cs[i] & 1) ^ 1u)) return false;  // PV_i of the previous tile done
-        tc_fence_after();
         if (lane == 0) {
           // k-step ks: descriptor start address + (64-dim half, 32-byte step) / 16
           const uint64_t ad = desc_kmajor(sQ + i * kQTile, kQHalf, 0), bd = desc_kmajor(kt, kKVHalf, 0);
@@ -386,7 +388,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&s_full[i]);
         }
         __syncwarp();
-        ++cs[i];
         return true;
       };
       auto issue_pv = [&](int i, int j, const uint8_t* vt) -> bool {
@@ -635,9 +636,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int a = 0; a < 4; ++a) f2_unpack(acc2[a], ps[2 * a], ps[2 * a + 1]);
         const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         l = l * alpha + rs;
-        // O_i holds PV of tiles < j (S_i(j) was issued after PV_i(j-1)
-        // completed) and PV_i(j) waits for P_i(j): rescale it in place when a
-        // row of this warp raised its max. (A first tile's PV overwrites O.)
+        // O_i holds PV of tiles < j (S_i(j) was issued after PV_i(j-1), and
+        // the commit that signalled S_i(j) covers every earlier MMA of the
+        // issuing thread) and PV_i(j) waits for P_i(j): rescale it in place
+        // when a row of this warp raised its max. (A first tile's PV
+        // overwrites O.)
         if (j >= 1 && __any_sync(0xffffffffu, m_new != m)) {
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
