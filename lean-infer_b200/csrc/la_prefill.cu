@@ -24,9 +24,9 @@
 //                       read MN-major from its TMA tile
 // The MMA warp interleaves the two tiles (PV_0(j), S_0(j+1), PV_1(j),
 // S_1(j+1)) so the tensor core computes one tile's products while the other
-// tile's softmax runs. S_i(j+1) overwrites P_i(j), so it waits for PV_i(j);
-// in exchange, when softmax i sees S_i(j+1), O_i is complete and can be
-// rescaled in place. The row max is raised (and O, l rescaled) only when a
+// tile's softmax runs. S_i(j+1) overwrites P_i(j); it is issued right behind
+// PV_i(j), which the tensor core executes first, and when softmax i sees
+// S_i(j+1), O_i is complete and can be rescaled in place. The row max is raised (and O, l rescaled) only when a
 // tile's max exceeds the running one by more than 8 (log2 units), so most
 // tiles skip the rescale.
 //
