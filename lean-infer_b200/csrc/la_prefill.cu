@@ -71,7 +71,8 @@ constexpr int kOffStage = kOffKV + kStages * kKVTile;      // 192 KB
 constexpr int kStageBytes = 32 * 128;                      // 32 rows x 64 dims bf16
 constexpr int kOffStats = kOffStage + 4 * kStageBytes;     // 208 KB
 constexpr int kOffBar = kOffStats + 2 * 2 * kRows * 4;     // + 2 KB
-constexpr size_t kSmemBytes = kOffBar + 256 + 1024;
+constexpr int kOffState = kOffBar + 256;                   // per softmax warp: Walker + Item, 128 B
+constexpr size_t kSmemBytes = kOffState + 8 * 128 + 1024;
 
 struct Params {
   const int* cu;  // query starts [num_seqs + 1], or null: sequence s has q_len queries from token s * q_len
@@ -554,9 +555,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t colS = i * 128, colO = kColO + i * 128;
     const float sl2 = p.scale_log2;
-    Walker w;
+    // The walk state lives in shared memory: it is only needed between
+    // tiles, and keeping it out of registers leaves them to the
+    // exponential loop.
+    Walker& w = *reinterpret_cast<Walker*>(smem + kOffState + warp * 128);
+    Item& it = *reinterpret_cast<Item*>(smem + kOffState + warp * 128 + 32);
     walker_init(p, w);
-    Item it;
     uint32_t t = 0;      // S_i tiles seen
     uint32_t nst = 0;    // items whose statistics were written
     bool ok = true;
