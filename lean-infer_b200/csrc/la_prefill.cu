@@ -63,6 +63,13 @@ constexpr uint32_t kIdescPV = idesc_bf16_f32(128, 128, false, true);
 constexpr int kRegSoftmax = 160, kRegEpilogue = 88, kRegOther = 104;
 static_assert(256 * kRegSoftmax + 128 * kRegEpilogue + 128 * kRegOther <= kThreads * 128,
               "the register split must fit in the registers the CTA is launched with");
+// setmaxnreg.inc may only raise and .dec only lower a warp's count (128 at
+// launch); the other direction is an illegal instruction.
+static_assert(kRegSoftmax >= 128 && kRegEpilogue <= 128 && kRegOther <= 128,
+              "softmax warpgroups use setmaxnreg.inc, the others setmaxnreg.dec");
+static_assert(kRegSoftmax % 8 == 0 && kRegEpilogue % 8 == 0 && kRegOther % 8 == 0 && kRegEpilogue >= 24 &&
+                  kRegSoftmax <= 256,
+              "setmaxnreg counts are multiples of 8 in [24, 256]");
 // Shared memory: Q0 Q1 | K/V ring | O staging (4 KB per epilogue warp) |
 // row statistics (l, m of both tiles) | barriers; base aligned to 1024 B (the
 // 128-byte swizzle atom) at run time.
