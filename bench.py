@@ -33,7 +33,6 @@ import statistics
 import subprocess
 import sys
 import threading
-import time
 from pathlib import Path
 
 import torch
