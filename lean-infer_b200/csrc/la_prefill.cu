@@ -26,9 +26,9 @@
 // S_1(j+1)) so the tensor core computes one tile's products while the other
 // tile's softmax runs. S_i(j+1) overwrites P_i(j); it is issued right behind
 // PV_i(j), which the tensor core executes first, and when softmax i sees
-// S_i(j+1), O_i is complete and can be rescaled in place. The row max is raised (and O, l rescaled) only when a
-// tile's max exceeds the running one by more than 8 (log2 units), so most
-// tiles skip the rescale.
+// S_i(j+1), O_i is complete and can be rescaled in place. The row max is
+// raised (and O, l rescaled) only when a tile's max exceeds the running one
+// by more than 8 (log2 units), so most tiles skip the rescale.
 //
 // Warps (16): 0-3 softmax of tile 0, 4-7 softmax of tile 1, 8-11 epilogue
 // (normalise O_i, store it through shared memory with coalesced rows, lse),
