@@ -520,6 +520,16 @@ def _varlen_paged(q, k_cache, v_cache, cu_q, cu_k, max_seqlen_q, softmax_scale, 
 _uniform_cu: dict[tuple, torch.Tensor] = {}
 
 
+def _uniform_cu_for(B: int, L: int, device) -> torch.Tensor:
+    """cu_seqlens [0, L, 2L, ..., BL] int32 on `device`, cached per shape."""
+    key = (B, L, device)
+    cu = _uniform_cu.get(key)
+    if cu is None:
+        cu = torch.arange(0, (B + 1) * L, L, dtype=torch.int32, device=device)
+        _uniform_cu[key] = cu
+    return cu
+
+
 def scaled_dot_product_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, attn_mask=None,
                                  dropout_p: float = 0.0, is_causal: bool = False, scale: Optional[float] = None,
                                  enable_gqa: bool = False) -> torch.Tensor:
@@ -535,12 +545,14 @@ def scaled_dot_product_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
     if Hq != Hkv and not enable_gqa:
         raise RuntimeError("Hq != Hkv requires enable_gqa=True")
     qt, kt, vt = (x.transpose(1, 2) for x in (q, k, v))  # [B, L, H, D]
+    if B == 1:
+        # One sequence (the reference's prefill): the kernel takes the token
+        # and head strides as they are, so the [1, H, L, D] tensors need no copy.
+        cu = _uniform_cu_for(1, L, q.device)
+        out = flash_attn_varlen_func(qt[0], kt[0], vt[0], cu, cu, L, L, softmax_scale=scale, causal=is_causal)
+        return out.view(1, L, Hq, D).transpose(1, 2)
     qt, kt, vt = (x if x.is_contiguous() else x.contiguous() for x in (qt, kt, vt))
-    key = (B, L, q.device)
-    cu = _uniform_cu.get(key)
-    if cu is None:
-        cu = torch.arange(0, (B + 1) * L, L, dtype=torch.int32, device=q.device)
-        _uniform_cu[key] = cu
+    cu = _uniform_cu_for(B, L, q.device)
     out = flash_attn_varlen_func(qt.view(B * L, Hq, D), kt.view(B * L, Hkv, D), vt.view(B * L, Hkv, D), cu, cu, L, L,
                                  softmax_scale=scale, causal=is_causal)
     return out.view(B, L, Hq, D).transpose(1, 2)

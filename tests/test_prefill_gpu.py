@@ -141,3 +141,23 @@ def test_matches_flash_attn_varlen(pkg, cuda_dev):
     out = pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx, causal=True)
     torch.cuda.synchronize()
     assert (out.float() - ref.float()).abs().max().item() <= TOL
+
+
+# One prompt (the reference's own prefill shape, B=1): single-tile items.
+@pytest.mark.parametrize("L", [300, 525, 700, 1024, 1500, 2000])
+def test_single_prompt(pkg, cuda_dev, L):
+    run(pkg, cuda_dev, [L], seed=L, lse=True)
+
+
+def test_sdpa_single_prompt_strided_views(pkg, cuda_dev):
+    """The SDPA drop-in at B=1 passes the [1, H, L, D] tensors' strides to the
+    kernel (no copies); results match the oracle."""
+    L = 640
+    q, k, v, cu, _ = _case([L], seed=21)
+    qd = q.to(cuda_dev).transpose(0, 1)[None]  # [1, Hq, L, D] views of [L, Hq, D]
+    kd = k.to(cuda_dev).transpose(0, 1)[None]
+    vd = v.to(cuda_dev).transpose(0, 1)[None]
+    out = pkg.scaled_dot_product_attention(qd, kd, vd, is_causal=True, enable_gqa=True)
+    torch.cuda.synchronize()
+    ref = opa.varlen_causal_prefill(q, k, v, cu)
+    assert (out[0].transpose(0, 1).cpu().float() - ref).abs().max().item() <= TOL
