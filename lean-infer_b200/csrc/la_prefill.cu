@@ -291,7 +291,206 @@ __global__ void __launch_bounds__(kThreads, 1)
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
   };
 
-  if (wg == 3) {
+  if (wg < 2) {
+    regs_inc<kRegSoftmax>();
+    // ------------------------------------------------------------ softmax of tile i = wg
+    const int i = wg;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t colS = i * 128, colO = kColO + i * 128;
+    const float sl2 = p.scale_log2;
+    // The walk state lives in shared memory: it is only needed between
+    // tiles, and keeping it out of registers leaves them to the
+    // exponential loop.
+    Walker& w = *reinterpret_cast<Walker*>(smem + kOffState + warp * 128);
+    Item& it = *reinterpret_cast<Item*>(smem + kOffState + warp * 128 + 32);
+    walker_init(p, w);
+    uint32_t t = 0;      // S_i tiles seen
+    uint32_t nst = 0;    // items whose statistics were written
+    bool ok = true;
+    while (ok && walker_next(p, w, it)) {
+      const int ni = i ? it.n1 : it.n0;
+      if (ni == 0) continue;
+      const int tok = it.q0 + i * p.tq + (row & (p.tq - 1));        // token index within the sequence
+      const int lim = p.causal ? min(max(tok + 1 + it.off, 0), it.K) : it.K;  // keys [0, lim) are visible
+      float m = NEG_INF, l = 0.f;
+      for (int j = 0; j < ni; ++j, ++t) {
+        // tcgen05.ld is warp-collective: keep the decision to continue warp-uniform
+        if (!(ok = wait_all(&s_full[i], t & 1))) break;
+        tc_fence_after();
+        float sv[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) tmem_ld32(taddr + colS + c * 32, sv[c]);
+        tc_wait_ld();
+
+        // Row max of the raw scores with 8 independent partial maxima.
+        const int nvis = lim - j * kKeys;  // visible columns of this tile
+        float mx[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mx[a] = NEG_INF;
+        const bool whole = __all_sync(0xffffffffu, nvis >= kKeys);  // whole tile visible: no mask
+        if (whole) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) mx[(e >> 1) & 7] = fmax3(mx[(e >> 1) & 7], sv[c][e], sv[c][e + 1]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float x0 = (c * 32 + e < nvis) ? sv[c][e] : NEG_INF;
+              const float x1 = (c * 32 + e + 1 < nvis) ? sv[c][e + 1] : NEG_INF;
+              sv[c][e] = x0;
+              sv[c][e + 1] = x1;
+              mx[(e >> 1) & 7] = fmax3(mx[(e >> 1) & 7], x0, x1);
+            }
+        }
+        const float mt = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7])) * sl2;
+        const float m_new = (mt > m + 8.f) ? mt : m;
+        // A row that has seen no key yet keeps m = -inf: use 0 as its
+        // reference so P and alpha come out 0 instead of NaN.
+        const float m_ref = (m_new == NEG_INF) ? 0.f : m_new;
+        const float alpha = ex2(m - m_ref);  // 0 on the first tile, 1 when m is kept
+        const float neg_m = -m_ref;
+        // P = exp2(S*scale*log2e - m) -> bf16 pairs over the first 64 columns
+        // of S_i, one 64-key half at a time (S values become packed P as
+        // they are used, which keeps the live registers near one S row).
+        // Scale and shift (and later sum) in packed pairs; 2^x on the MUFU
+        // unit. (Moving part of the exponentials to an FMA-pipe polynomial
+        // was measured slower: the softmax is issue-bound, not MUFU-bound.)
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(neg_m, neg_m);
+        uint64_t acc2[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) acc2[a] = 0ull;
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          float pk[32];
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            const uint64_t y2 =
+                f2_fma(f2_pack(sv[2 * c2 + (x >> 4)][(x & 15) * 2], sv[2 * c2 + (x >> 4)][(x & 15) * 2 + 1]), sl2x2, negm2);
+            float e0, e1;
+            f2_unpack(y2, e0, e1);
+            e0 = ex2(e0);  // masked: -inf -> 0
+            e1 = ex2(e1);
+            acc2[x & 3] = f2_add(acc2[x & 3], f2_pack(e0, e1));
+            pk[x] = __uint_as_float(pack_bf16x2(e0, e1));
+          }
+          tmem_st32(taddr + colS + c2 * 32, pk);
+        }
+        float ps[8];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) f2_unpack(acc2[a], ps[2 * a], ps[2 * a + 1]);
+        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        l = l * alpha + rs;
+        // O_i holds PV of tiles < j (S_i(j) was issued after PV_i(j-1), and
+        // the commit that signalled S_i(j) covers every earlier MMA of the
+        // issuing thread) and PV_i(j) waits for P_i(j): rescale it in place
+        // when a row of this warp raised its max. (A first tile's PV
+        // overwrites O.)
+        if (j >= 1 && __any_sync(0xffffffffu, m_new != m)) {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tmem_ld32(taddr + colO + c * 32, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(taddr + colO + c * 32, o);
+          }
+        }
+        m = m_new;
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[i]);
+      }
+      if (!ok) break;
+      // Row statistics for the epilogue.
+      if (!(ok = wait_all(&st_empty[i], (nst & 1) ^ 1u))) break;
+      stats[(i * 2 + 0) * kRows + row] = l;
+      stats[(i * 2 + 1) * kRows + row] = m;
+      mbar_arrive(&st_full[i]);
+      ++nst;
+    }
+  } else if (wg == 2) {
+    regs_dec<kRegEpilogue>();
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    uint8_t* stage = smem + kOffStage + quarter * kStageBytes;
+    Walker w;
+    walker_init(p, w);
+    Item it;
+    uint32_t cp[2] = {0, 0};       // PV_i so far (through this item)
+    uint32_t items_i[2] = {0, 0};  // items in which tile i ran
+    bool ok = true;
+    while (ok && walker_next(p, w, it)) {
+      for (int i = 0; i < 2 && ok; ++i) {
+        const int ni = i ? it.n1 : it.n0;
+        if (ni == 0) continue;
+        cp[i] += ni;
+        if (!(ok = wait_all(&st_full[i], items_i[i] & 1))) break;
+        const float l = stats[(i * 2 + 0) * kRows + row];
+        const float m = stats[(i * 2 + 1) * kRows + row];
+        mbar_arrive(&st_empty[i]);
+        if (!(ok = wait_all(&s_free[i], (cp[i] - 1) & 1))) break;  // the item's last PV_i
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const int qt0 = it.q0 + i * p.tq;
+        {
+          const int g = row >> p.tq_shift;
+          const int tok = qt0 + (row & (p.tq - 1));
+          if (p.lse && tok < it.L)
+            p.lse[static_cast<long long>(it.h * p.group + g) * p.total + it.seq0 + tok] =
+                l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
+        }
+        // O_i rows -> global through this warp's staging buffer, one 64-dim
+        // half at a time: each thread writes its row (8 chunks of 16 B,
+        // XOR-swizzled by row), then each store instruction writes 4 rows x
+        // 128 contiguous bytes. Rows past the sequence's end are not stored.
+#pragma unroll 1
+        for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            float o[32];
+            tmem_ld32(taddr + kColO + i * 128 + h2 * 64 + c * 32, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int q4 = 0; q4 < 4; ++q4) {
+              uint4 u;
+              u.x = pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv);
+              u.y = pack_bf16x2(o[q4 * 8 + 2] * inv, o[q4 * 8 + 3] * inv);
+              u.z = pack_bf16x2(o[q4 * 8 + 4] * inv, o[q4 * 8 + 5] * inv);
+              u.w = pack_bf16x2(o[q4 * 8 + 6] * inv, o[q4 * 8 + 7] * inv);
+              const int ch = c * 4 + q4;
+              *reinterpret_cast<uint4*>(stage + lane * 128 + ((ch ^ (lane & 7)) << 4)) = u;
+            }
+          }
+          if (h2 == 1) {  // all of O_i is in registers or staged: the next item may overwrite it
+            tc_fence_before();
+            mbar_arrive(&o_empty[i]);
+          }
+          __syncwarp();
+#pragma unroll 1
+          for (int x = 0; x < 8; ++x) {
+            const int r = x * 4 + (lane >> 3), ch = lane & 7;
+            const int rrow = quarter * 32 + r;
+            const int rg = rrow >> p.tq_shift;
+            const int rtok = qt0 + (rrow & (p.tq - 1));
+            const uint4 u = *reinterpret_cast<const uint4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4));
+            if (rtok < it.L)
+              *reinterpret_cast<uint4*>(p.out + static_cast<long long>(it.seq0 + rtok) * p.out_ts +
+                                        static_cast<long long>(it.h * p.group + rg) * p.out_hs + h2 * 64 + ch * 8) = u;
+          }
+          __syncwarp();
+        }
+        ++items_i[i];
+      }
+    }
+  } else {
     regs_dec<kRegOther>();
     if (warp == 13) {
       // ---------------------------------------------------------- TMA producer (lane 0 issues)
@@ -477,205 +676,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
     }
     // warps 14, 15: no role
-  } else if (wg == 2) {
-    regs_dec<kRegEpilogue>();
-    // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    uint8_t* stage = smem + kOffStage + quarter * kStageBytes;
-    Walker w;
-    walker_init(p, w);
-    Item it;
-    uint32_t cp[2] = {0, 0};       // PV_i so far (through this item)
-    uint32_t items_i[2] = {0, 0};  // items in which tile i ran
-    bool ok = true;
-    while (ok && walker_next(p, w, it)) {
-      for (int i = 0; i < 2 && ok; ++i) {
-        const int ni = i ? it.n1 : it.n0;
-        if (ni == 0) continue;
-        cp[i] += ni;
-        if (!(ok = wait_all(&st_full[i], items_i[i] & 1))) break;
-        const float l = stats[(i * 2 + 0) * kRows + row];
-        const float m = stats[(i * 2 + 1) * kRows + row];
-        mbar_arrive(&st_empty[i]);
-        if (!(ok = wait_all(&s_free[i], (cp[i] - 1) & 1))) break;  // the item's last PV_i
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        const int qt0 = it.q0 + i * p.tq;
-        {
-          const int g = row >> p.tq_shift;
-          const int tok = qt0 + (row & (p.tq - 1));
-          if (p.lse && tok < it.L)
-            p.lse[static_cast<long long>(it.h * p.group + g) * p.total + it.seq0 + tok] =
-                l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
-        }
-        // O_i rows -> global through this warp's staging buffer, one 64-dim
-        // half at a time: each thread writes its row (8 chunks of 16 B,
-        // XOR-swizzled by row), then each store instruction writes 4 rows x
-        // 128 contiguous bytes. Rows past the sequence's end are not stored.
-#pragma unroll 1
-        for (int h2 = 0; h2 < 2; ++h2) {
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            float o[32];
-            tmem_ld32(taddr + kColO + i * 128 + h2 * 64 + c * 32, o);
-            tc_wait_ld();
-#pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {
-              uint4 u;
-              u.x = pack_bf16x2(o[q4 * 8 + 0] * inv, o[q4 * 8 + 1] * inv);
-              u.y = pack_bf16x2(o[q4 * 8 + 2] * inv, o[q4 * 8 + 3] * inv);
-              u.z = pack_bf16x2(o[q4 * 8 + 4] * inv, o[q4 * 8 + 5] * inv);
-              u.w = pack_bf16x2(o[q4 * 8 + 6] * inv, o[q4 * 8 + 7] * inv);
-              const int ch = c * 4 + q4;
-              *reinterpret_cast<uint4*>(stage + lane * 128 + ((ch ^ (lane & 7)) << 4)) = u;
-            }
-          }
-          if (h2 == 1) {  // all of O_i is in registers or staged: the next item may overwrite it
-            tc_fence_before();
-            mbar_arrive(&o_empty[i]);
-          }
-          __syncwarp();
-#pragma unroll 1
-          for (int x = 0; x < 8; ++x) {
-            const int r = x * 4 + (lane >> 3), ch = lane & 7;
-            const int rrow = quarter * 32 + r;
-            const int rg = rrow >> p.tq_shift;
-            const int rtok = qt0 + (rrow & (p.tq - 1));
-            const uint4 u = *reinterpret_cast<const uint4*>(stage + r * 128 + ((ch ^ (r & 7)) << 4));
-            if (rtok < it.L)
-              *reinterpret_cast<uint4*>(p.out + static_cast<long long>(it.seq0 + rtok) * p.out_ts +
-                                        static_cast<long long>(it.h * p.group + rg) * p.out_hs + h2 * 64 + ch * 8) = u;
-          }
-          __syncwarp();
-        }
-        ++items_i[i];
-      }
-    }
-  } else {
-    regs_inc<kRegSoftmax>();
-    // ------------------------------------------------------------ softmax of tile i = wg
-    const int i = wg;
-    const int quarter = warp & 3;
-    const int row = quarter * 32 + lane;
-    const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint32_t colS = i * 128, colO = kColO + i * 128;
-    const float sl2 = p.scale_log2;
-    // The walk state lives in shared memory: it is only needed between
-    // tiles, and keeping it out of registers leaves them to the
-    // exponential loop.
-    Walker& w = *reinterpret_cast<Walker*>(smem + kOffState + warp * 128);
-    Item& it = *reinterpret_cast<Item*>(smem + kOffState + warp * 128 + 32);
-    walker_init(p, w);
-    uint32_t t = 0;      // S_i tiles seen
-    uint32_t nst = 0;    // items whose statistics were written
-    bool ok = true;
-    while (ok && walker_next(p, w, it)) {
-      const int ni = i ? it.n1 : it.n0;
-      if (ni == 0) continue;
-      const int tok = it.q0 + i * p.tq + (row & (p.tq - 1));        // token index within the sequence
-      const int lim = p.causal ? min(max(tok + 1 + it.off, 0), it.K) : it.K;  // keys [0, lim) are visible
-      float m = NEG_INF, l = 0.f;
-      for (int j = 0; j < ni; ++j, ++t) {
-        // tcgen05.ld is warp-collective: keep the decision to continue warp-uniform
-        if (!(ok = wait_all(&s_full[i], t & 1))) break;
-        tc_fence_after();
-        float sv[4][32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(taddr + colS + c * 32, sv[c]);
-        tc_wait_ld();
-
-        // Row max of the raw scores with 8 independent partial maxima.
-        const int nvis = lim - j * kKeys;  // visible columns of this tile
-        float mx[8];
-#pragma unroll
-        for (int a = 0; a < 8; ++a) mx[a] = NEG_INF;
-        const bool whole = __all_sync(0xffffffffu, nvis >= kKeys);  // whole tile visible: no mask
-        if (whole) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) mx[(e >> 1) & 7] = fmax3(mx[(e >> 1) & 7], sv[c][e], sv[c][e + 1]);
-        } else {
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              const float x0 = (c * 32 + e < nvis) ? sv[c][e] : NEG_INF;
-              const float x1 = (c * 32 + e + 1 < nvis) ? sv[c][e + 1] : NEG_INF;
-              sv[c][e] = x0;
-              sv[c][e + 1] = x1;
-              mx[(e >> 1) & 7] = fmax3(mx[(e >> 1) & 7], x0, x1);
-            }
-        }
-        const float mt = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7])) * sl2;
-        const float m_new = (mt > m + 8.f) ? mt : m;
-        // A row that has seen no key yet keeps m = -inf: use 0 as its
-        // reference so P and alpha come out 0 instead of NaN.
-        const float m_ref = (m_new == NEG_INF) ? 0.f : m_new;
-        const float alpha = ex2(m - m_ref);  // 0 on the first tile, 1 when m is kept
-        const float neg_m = -m_ref;
-        // P = exp2(S*scale*log2e - m) -> bf16 pairs over the first 64 columns
-        // of S_i, one 64-key half at a time (S values become packed P as
-        // they are used, which keeps the live registers near one S row).
-        // Scale and shift (and later sum) in packed pairs; 2^x on the MUFU
-        // unit. (Moving part of the exponentials to an FMA-pipe polynomial
-        // was measured slower: the softmax is issue-bound, not MUFU-bound.)
-        const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(neg_m, neg_m);
-        uint64_t acc2[4];
-#pragma unroll
-        for (int a = 0; a < 4; ++a) acc2[a] = 0ull;
-#pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          float pk[32];
-#pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            const uint64_t y2 =
-                f2_fma(f2_pack(sv[2 * c2 + (x >> 4)][(x & 15) * 2], sv[2 * c2 + (x >> 4)][(x & 15) * 2 + 1]), sl2x2, negm2);
-            float e0, e1;
-            f2_unpack(y2, e0, e1);
-            e0 = ex2(e0);  // masked: -inf -> 0
-            e1 = ex2(e1);
-            acc2[x & 3] = f2_add(acc2[x & 3], f2_pack(e0, e1));
-            pk[x] = __uint_as_float(pack_bf16x2(e0, e1));
-          }
-          tmem_st32(taddr + colS + c2 * 32, pk);
-        }
-        float ps[8];
-#pragma unroll
-        for (int a = 0; a < 4; ++a) f2_unpack(acc2[a], ps[2 * a], ps[2 * a + 1]);
-        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-        l = l * alpha + rs;
-        // O_i holds PV of tiles < j (S_i(j) was issued after PV_i(j-1), and
-        // the commit that signalled S_i(j) covers every earlier MMA of the
-        // issuing thread) and PV_i(j) waits for P_i(j): rescale it in place
-        // when a row of this warp raised its max. (A first tile's PV
-        // overwrites O.)
-        if (j >= 1 && __any_sync(0xffffffffu, m_new != m)) {
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            float o[32];
-            tmem_ld32(taddr + colO + c * 32, o);
-            tc_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] *= alpha;
-            tmem_st32(taddr + colO + c * 32, o);
-          }
-        }
-        m = m_new;
-        tc_wait_st();
-        tc_fence_before();
-        mbar_arrive(&p_full[i]);
-      }
-      if (!ok) break;
-      // Row statistics for the epilogue.
-      if (!(ok = wait_all(&st_empty[i], (nst & 1) ^ 1u))) break;
-      stats[(i * 2 + 0) * kRows + row] = l;
-      stats[(i * 2 + 1) * kRows + row] = m;
-      mbar_arrive(&st_full[i]);
-      ++nst;
-    }
   }
   tc_fence_before();
   __syncthreads();
