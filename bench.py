@@ -407,8 +407,8 @@ def run_ours(args):
         dg.replay()
     torch.cuda.synchronize()
     # per layer: fused pre-attention, decode, combine, two add+RMSNorm, SiLU*mul;
-    # plus the first layer's input RMSNorm
-    launches_per_step = cfg.num_hidden_layers * 6 + 1
+    # plus the first layer's input RMSNorm and the greedy-token argmax
+    launches_per_step = cfg.num_hidden_layers * 6 + 2
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         barrier()

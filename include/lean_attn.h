@@ -313,6 +313,15 @@ int la_add_rms_norm(const void* h, int64_t h_row_stride, const void* a, int64_t 
 int la_silu_mul(const void* gate_up, int64_t gate_up_row_stride, void* out, int64_t out_row_stride,
                 int64_t rows, int n, cudaStream_t stream);
 
+/* la_argmax_rows: out[r] = index of the maximum of row r of a bf16 matrix
+ * [rows, cols] (row stride in elements), int64 — the greedy next token,
+ * logits[:, -1].argmax(-1) (leaninfer/engine/llm_engine.py:86, 111, 135),
+ * with torch.argmax's rules: the first index holding the maximum (+0 and -0
+ * equal), and a NaN counts as larger than every number. cols >= 1; rows whose
+ * starts are 16-byte aligned are read with 16-byte loads. */
+int la_argmax_rows(const void* x, int64_t row_stride, int64_t rows, int64_t cols, int64_t* out,
+                   cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -124,6 +124,7 @@ _SIGNATURES = {
     "la_add_rms_norm": [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
                         c_int64, c_int, c_float, c_void_p],
     "la_silu_mul": [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int, c_void_p],
+    "la_argmax_rows": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "la_prefill_paged": [
         c_void_p, c_int64, c_int64,
         c_void_p, c_void_p,

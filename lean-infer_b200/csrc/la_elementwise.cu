@@ -6,6 +6,9 @@
 //   la_silu_mul: SiLU(gate) * up on the fused gate_up projection
 //     (Qwen3MLP, model.py:32-33).
 // Both read their inputs once and round their outputs to bf16 once, from fp32.
+//   la_argmax_rows: the greedy next token, logits[:, -1].argmax(-1)
+//     (leaninfer/engine/llm_engine.py:86, 111, 135), with torch.argmax's
+//     rules: the first index of the maximum, and NaN above every number.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -129,6 +132,102 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const SiluParams p) {
   *reinterpret_cast<uint4*>(p.out + row * p.out_rs + c) = o;
 }
 
+// ---------------------------------------------------------------- argmax
+// Order key of a bf16 value: larger key = larger value, equal values (+0 and
+// -0 included) get equal keys, every NaN gets the largest key.
+__device__ __forceinline__ uint32_t argmax_key(uint32_t b) {
+  b &= 0xffffu;
+  if ((b & 0x7fffu) > 0x7f80u) return 0x10000u;
+  if (b == 0x8000u) b = 0u;
+  return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);
+}
+
+constexpr int kArgmaxThreads = 512;
+constexpr int kArgmaxUnroll = 8;  // 16-byte loads in flight per thread
+
+struct ArgmaxParams {
+  const __nv_bfloat16* x;
+  long long rs;  // row stride (elements)
+  int cols;
+  int vec;       // every row starts 16-byte aligned: 8-element chunks
+  long long* out;
+};
+
+// One CTA per row. Thread t reads chunks t, t + 512, ... of 8 values with
+// 16-byte loads and keeps the first chunk holding its largest key (a chunk's
+// max from three packed bf16x2 max operations, NaN-propagating); afterwards it
+// finds the first index of that key inside the chunk, and the block keeps the
+// largest key with the smallest index.
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_rows_kernel(const ArgmaxParams p) {
+  grid_dependency_wait();
+  grid_launch_dependents();
+  const __nv_bfloat16* row = p.x + static_cast<long long>(blockIdx.x) * p.rs;
+  const int t = threadIdx.x;
+  uint32_t best = 0;  // below every key
+  int best_idx = 0x7fffffff;
+  const int nchunk = p.vec ? p.cols / 8 : 0;
+  int best_chunk = -1;
+  const uint4* rv = reinterpret_cast<const uint4*>(row);
+  for (int c0 = t; c0 < nchunk; c0 += kArgmaxThreads * kArgmaxUnroll) {
+    uint4 u[kArgmaxUnroll];
+#pragma unroll
+    for (int k = 0; k < kArgmaxUnroll; ++k) {
+      const int c = c0 + k * kArgmaxThreads;
+      if (c < nchunk) u[k] = __ldcs(rv + c);  // read once: do not keep in L1/L2
+    }
+#pragma unroll
+    for (int k = 0; k < kArgmaxUnroll; ++k) {
+      const int c = c0 + k * kArgmaxThreads;
+      if (c < nchunk) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u[k]);
+        const __nv_bfloat162 m2 = __hmax2_nan(__hmax2_nan(h[0], h[1]), __hmax2_nan(h[2], h[3]));
+        const uint32_t mb = *reinterpret_cast<const uint32_t*>(&m2);
+        const uint32_t key = max(argmax_key(mb), argmax_key(mb >> 16));
+        if (key > best) {
+          best = key;
+          best_chunk = c;
+        }
+      }
+    }
+  }
+  if (best_chunk >= 0) {  // first element of the chunk with the chunk's best key
+    const uint4 u = rv[best_chunk];
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(&u);
+#pragma unroll
+    for (int k = 7; k >= 0; --k)
+      if (argmax_key(e[k]) == best) best_idx = best_chunk * 8 + k;
+  }
+  // Elements outside the chunks (the tail, or every element when rows are not
+  // 16-byte aligned): indices above every chunk, visited in increasing order.
+  const uint16_t* rb = reinterpret_cast<const uint16_t*>(row);
+  for (int i = nchunk * 8 + t; i < p.cols; i += kArgmaxThreads) {
+    const uint32_t key = argmax_key(rb[i]);
+    if (key > best) {
+      best = key;
+      best_idx = i;
+    }
+  }
+  // Largest key, then smallest index.
+  unsigned long long v = (static_cast<unsigned long long>(best) << 32) | static_cast<uint32_t>(~best_idx);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
+  }
+  __shared__ unsigned long long part[kArgmaxThreads / 32];
+  if ((t & 31) == 0) part[t >> 5] = v;
+  __syncthreads();
+  if (t < 32) {
+    v = t < kArgmaxThreads / 32 ? part[t] : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+      v = w > v ? w : v;
+    }
+    if (t == 0) p.out[blockIdx.x] = static_cast<long long>(~static_cast<uint32_t>(v));
+  }
+}
+
 }  // namespace elementwise
 }  // namespace la
 
@@ -183,4 +282,23 @@ extern "C" int la_silu_mul(const void* gate_up, int64_t gate_up_row_stride, void
   const long long blocks = (p.total8 + 255) / 256;
   if (blocks > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
   return cuda_status(launch_pdl(silu_mul_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, p));
+}
+
+extern "C" int la_argmax_rows(const void* x, int64_t row_stride, int64_t rows, int64_t cols, int64_t* out,
+                              cudaStream_t stream) {
+  using namespace la;
+  using namespace la::elementwise;
+  if (!x || !out || rows < 0 || cols <= 0 || cols > 0x7fffffffLL - 8 || row_stride < cols)
+    return LA_ERR_INVALID_ARGUMENT;
+  if (rows > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
+  if (rows == 0) return LA_OK;
+  if (!aligned(x, 2) || !aligned(out, 8)) return LA_ERR_ALIGNMENT;
+  ArgmaxParams p;
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.rs = row_stride;
+  p.cols = static_cast<int>(cols);
+  p.vec = aligned(x, 16) && row_stride % 8 == 0;
+  p.out = reinterpret_cast<long long*>(out);
+  return cuda_status(
+      launch_pdl(argmax_rows_kernel, dim3(static_cast<unsigned>(rows)), dim3(kArgmaxThreads), 0, stream, p));
 }

@@ -13,7 +13,9 @@ confined to how the work is launched:
   * decode attention (model.py:60-67) is flash_attn_with_kvcache from this
     package; prefill attention (model.py:56-57) is flash_attn_varlen_func;
   * each residual add and the RMSNorm after it are one launch
-    (add_rms_norm), and SiLU(gate) * up is one launch (silu_mul).
+    (add_rms_norm), and SiLU(gate) * up is one launch (silu_mul);
+  * the greedy next token, logits[:, -1].argmax(-1)
+    (leaninfer/engine/llm_engine.py:86), is one launch (argmax_rows).
 Weights are random-init bf16 (no checkpoint is loaded: the benchmark runs on
 synthetic data).
 """
@@ -58,6 +60,18 @@ def silu_mul(gate_up: torch.Tensor, n: int) -> torch.Tensor:
         _lib.call("la_silu_mul", ctypes.c_void_p(gate_up.data_ptr()), gate_up.stride(0),
                   ctypes.c_void_p(out.data_ptr()), out.stride(0), T, n,
                   ctypes.c_void_p(torch.cuda.current_stream(gate_up.device).cuda_stream))
+    return out
+
+
+def argmax_rows(x: torch.Tensor) -> torch.Tensor:
+    """x.argmax(-1) for a bf16 matrix [rows, cols] with unit column stride, in
+    one launch (la_argmax_rows): int64 [rows], the first index of each row's
+    maximum, NaN above every number — torch.argmax's rules."""
+    assert x.dim() == 2 and x.dtype == torch.bfloat16 and x.stride(1) == 1
+    out = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
+    if x.shape[0]:
+        _lib.call("la_argmax_rows", ctypes.c_void_p(x.data_ptr()), x.stride(0), x.shape[0], x.shape[1],
+                  ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
     return out
 
 
@@ -225,7 +239,7 @@ class DecodeGraph:
 
     def _forward(self):
         logits = self.model(self.ids, self.cache, self.bt, self.pos, self.ctx)
-        return logits, logits[:, -1].argmax(-1)
+        return logits, argmax_rows(logits[:, -1])
 
     def capture(self) -> None:
         side = torch.cuda.Stream()
@@ -310,7 +324,7 @@ class BucketedDecodeGraph:
 
     def _forward(self, b: int):
         logits = self.model(self.ids[:b], self.cache, self.bt[:b], self.pos[:b], self.ctx[:b])
-        return logits, logits[:, -1].argmax(-1)
+        return logits, argmax_rows(logits[:, -1])
 
     def capture(self) -> None:
         """Three warm-up forwards per bucket on a side stream, then one graph

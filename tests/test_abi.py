@@ -108,3 +108,11 @@ def test_glue_argument_checks(pkg):
     assert lib.la_add_rms_norm(fake, 1000, null, 0, null, 0, fake, 1024, fake, 4, 1024, ctypes.c_float(1e-6), null) == 3
     assert lib.la_silu_mul(fake, 6144, fake, 3072, 0, 3072, null) == 0
     assert lib.la_silu_mul(fake, 6000, fake, 3072, 4, 3072, null) == 3
+    # argmax rows: no rows is a no-op; empty rows, short strides, null or
+    # misaligned pointers are rejected before any launch
+    assert lib.la_argmax_rows(fake, 151936, 0, 151936, fake, null) == 0
+    assert lib.la_argmax_rows(null, 151936, 4, 151936, fake, null) == 1
+    assert lib.la_argmax_rows(fake, 151936, 4, 0, fake, null) == 1
+    assert lib.la_argmax_rows(fake, 100, 4, 151936, fake, null) == 1
+    assert lib.la_argmax_rows(ctypes.c_void_p((1 << 20) + 1), 151936, 4, 151936, fake, null) == 3
+    assert lib.la_argmax_rows(fake, 151936, 4, 151936, ctypes.c_void_p((1 << 20) + 4), null) == 3

@@ -2,7 +2,8 @@
 against plain PyTorch fp32 references of the same ops. Tolerance: the
 residual sum is bit-exact (one bf16 rounding of an fp32 sum); normalised and
 activated outputs within one bf16 rounding (relative 2^-7) of the fp32
-reference."""
+reference. The greedy-token argmax (la_argmax_rows) is index work: it must
+equal torch.argmax exactly, ties, NaN and signed zeros included."""
 import pytest
 import torch
 
@@ -50,3 +51,49 @@ def test_silu_mul(pkg, cuda_dev, T, n):
     ref = torch.nn.functional.silu(gu[:, :n].float()) * gu[:, n:].float()
     torch.cuda.synchronize()
     assert out.shape == (T, n) and _close(out, ref)
+
+
+@pytest.mark.parametrize("rows,cols,stride_pad,offset", [
+    (128, 151936, 0, 0),    # the decode step's logits
+    (3, 151936, 8, 0),      # padded rows
+    (5, 1000, 0, 0),        # 1000 = 125 x 8: chunks only
+    (4, 1003, 0, 0),        # 1003 = 125 x 8 + 3: tail elements
+    (6, 777, 1, 0),         # rows not 16-byte aligned: element path
+    (2, 4096, 0, 3),        # base not 16-byte aligned
+    (1, 1, 0, 0),
+])
+def test_argmax_rows(pkg, cuda_dev, rows, cols, stride_pad, offset):
+    from lean_infer_b200 import qwen3
+
+    g = torch.Generator(device=cuda_dev).manual_seed(rows * 7 + cols)
+    stride = cols + stride_pad
+    buf = torch.randn(offset + rows * stride, generator=g, device=cuda_dev).to(torch.bfloat16)
+    x = buf[offset:].view(rows, stride)[:, :cols]
+    got = qwen3.argmax_rows(x)
+    torch.cuda.synchronize()
+    assert got.dtype == torch.int64 and torch.equal(got, x.argmax(-1))
+
+
+def test_argmax_rows_ties_nan_zeros(pkg, cuda_dev):
+    """Rows built so the answer depends on the tie and NaN rules."""
+    from lean_infer_b200 import qwen3
+
+    cols = 151936
+    x = torch.full((10, cols), -3.0, device=cuda_dev, dtype=torch.bfloat16)
+    x[0, [5000, 17, 90000]] = 2.0                  # tie: the first index
+    x[1, [cols - 1, cols - 2]] = 1.0               # tie in the last chunk
+    x[2] = float("-inf")                           # all -inf: index 0
+    x[2, 123] = float("-inf")
+    x[3, [70000, 4000]] = float("nan")             # NaN beats every number, first NaN
+    x[3, 10] = float("inf")
+    x[4] = 0.0                                     # signed zeros are equal
+    x[4, :100] = -0.0
+    x[5, [8, 9, 10, 11, 12, 13, 14, 15]] = 5.0     # a whole chunk of equal maxima
+    x[6, 1] = float("inf")
+    x[6, 1 + 8 * 512] = float("inf")               # same thread, later chunk
+    x[7] = torch.arange(cols, device=cuda_dev).remainder(251).to(torch.bfloat16)  # many equal maxima
+    x[8, cols - 3] = 7.0                           # max in the tail position of the row
+    x[9, 0] = float("nan")
+    got = qwen3.argmax_rows(x)
+    torch.cuda.synchronize()
+    assert torch.equal(got, x.argmax(-1)), (got.tolist(), x.argmax(-1).tolist())
