@@ -215,19 +215,29 @@ class DecodeGraph:
     (leaninfer/engine/llm_engine.py:23-86): pinned host staging buffers,
     static device buffers ids [B,1] i64, pos [B] i64, bt [B, max_blocks] i32,
     ctx [B] i32; three warm-up forwards on a side stream, then capture. Idle
-    rows get pos 0, ctx 1 and block 0 (the trash block)."""
+    rows get pos 0, ctx 1 and block 0 (the trash block). The four host
+    buffers are views of one pinned allocation and the four device buffers
+    views of one device allocation with the same layout, so a step's inputs
+    go up in a single copy."""
 
     def __init__(self, model: Qwen3ForCausalLM, cache: BlockCache, n_slots: int, max_blocks: int) -> None:
         self.model, self.cache = model, cache
         dev = cache.device
-        self.host_ids = torch.zeros(n_slots, 1, dtype=torch.long, pin_memory=True)
-        self.host_pos = torch.zeros(n_slots, dtype=torch.long, pin_memory=True)
-        self.host_bt = torch.zeros(n_slots, max_blocks, dtype=torch.int32, pin_memory=True)
-        self.host_ctx = torch.ones(n_slots, dtype=torch.int32, pin_memory=True)
-        self.ids = torch.zeros(n_slots, 1, dtype=torch.long, device=dev)
-        self.pos = torch.zeros(n_slots, dtype=torch.long, device=dev)
-        self.bt = torch.zeros(n_slots, max_blocks, dtype=torch.int32, device=dev)
-        self.ctx = torch.ones(n_slots, dtype=torch.int32, device=dev)
+        B = n_slots
+        # byte layout: ids [B] i64 | pos [B] i64 | ctx [B] i32 | bt [B, max_blocks] i32
+        o_pos, o_ctx, o_bt = 8 * B, 16 * B, 20 * B
+        nbytes = o_bt + 4 * B * max_blocks
+
+        def views(buf: torch.Tensor):
+            return (buf[:o_pos].view(torch.long).view(B, 1), buf[o_pos:o_ctx].view(torch.long),
+                    buf[o_ctx:o_bt].view(torch.int32), buf[o_bt:].view(torch.int32).view(B, max_blocks))
+
+        self._host_buf = torch.zeros(nbytes, dtype=torch.uint8, pin_memory=True)
+        self._dev_buf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        self.host_ids, self.host_pos, self.host_ctx, self.host_bt = views(self._host_buf)
+        self.ids, self.pos, self.ctx, self.bt = views(self._dev_buf)
+        self.host_ctx.fill_(1)
+        self.ctx.fill_(1)
         self.graph: torch.cuda.CUDAGraph | None = None
         self.logits: torch.Tensor | None = None
         self.next_tokens: torch.Tensor | None = None
@@ -261,10 +271,7 @@ class DecodeGraph:
         self.host_ctx.copy_(ctx)
 
     def upload(self) -> None:
-        self.ids.copy_(self.host_ids, non_blocking=True)
-        self.pos.copy_(self.host_pos, non_blocking=True)
-        self.bt.copy_(self.host_bt, non_blocking=True)
-        self.ctx.copy_(self.host_ctx, non_blocking=True)
+        self._dev_buf.copy_(self._host_buf, non_blocking=True)  # ids, pos, ctx, bt in one copy
 
     def replay(self) -> None:
         if self.graph is None:
