@@ -71,15 +71,17 @@ static_assert(kRegSoftmax % 8 == 0 && kRegEpilogue % 8 == 0 && kRegOther % 8 == 
                   kRegSoftmax <= 256,
               "setmaxnreg counts are multiples of 8 in [24, 256]");
 // Shared memory: Q0 Q1 | K/V ring | O staging (4 KB per epilogue warp) |
-// row statistics (l, m of both tiles) | barriers; base aligned to 1024 B (the
-// 128-byte swizzle atom) at run time.
+// row statistics (l, m of both tiles) | barriers | softmax walk state | the
+// split softmax's row maxima; base aligned to 1024 B (the 128-byte swizzle
+// atom) at run time.
 constexpr int kOffKV = 2 * kQTile;                         // 64 KB
 constexpr int kOffStage = kOffKV + kStages * kKVTile;      // 192 KB
 constexpr int kStageBytes = 32 * 128;                      // 32 rows x 64 dims bf16
 constexpr int kOffStats = kOffStage + 4 * kStageBytes;     // 208 KB
 constexpr int kOffBar = kOffStats + 2 * 2 * kRows * 4;     // + 2 KB
 constexpr int kOffState = kOffBar + 256;                   // per softmax warp: Walker + Item, 128 B
-constexpr size_t kSmemBytes = kOffState + 8 * 128 + 1024;
+constexpr int kOffXmax = kOffState + 8 * 128;              // split softmax: row maxima of the two halves
+constexpr size_t kSmemBytes = kOffXmax + 2 * kRows * 4 + 1024;
 
 struct Params {
   const int* cu;  // query starts [num_seqs + 1], or null: sequence s has q_len queries from token s * q_len
@@ -228,6 +230,10 @@ __device__ __forceinline__ bool walker_next(const Params& p, Walker& w, Item& it
   return true;
 }
 
+// kSplit (items of single query tiles): both softmax warpgroups work on tile
+// 0, warpgroup h on keys 64h..64h+63 of each 128-key tile, exchanging their
+// row maxima through shared memory, so one tile's softmax takes half as long.
+template <bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -248,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* st_full = bars + 18;      // [2] row statistics of tile i written (128)
   uint64_t* st_empty = bars + 20;     // [2] ... read by the epilogue (128)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  uint64_t* x_full = bars + 26;       // [2] kSplit: warpgroup h's row maxima written (128)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -271,9 +278,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], kSplit && i == 0 ? 256 : 128);
       mbar_init(&o_empty[i], 128);
-      mbar_init(&st_full[i], 128);
+      mbar_init(&st_full[i], kSplit && i == 0 ? 256 : 128);
+      mbar_init(&x_full[i], 128);
       mbar_init(&st_empty[i], 128);
     }
     fence_barrier_init();
@@ -291,7 +299,113 @@ __global__ void __launch_bounds__(kThreads, 1)
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, p.err, LA_DEVERR_WAIT_TIMEOUT));
   };
 
-  if (wg < 2) {
+  if (wg < 2 && kSplit) {
+    regs_inc<kRegSoftmax>();
+    // ------------------------------------------------- softmax of tile 0, keys 64h..64h+63
+    const int h = wg;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const float sl2 = p.scale_log2;
+    float* xmax = reinterpret_cast<float*>(smem + kOffXmax);  // [half][row]
+    Walker& w = *reinterpret_cast<Walker*>(smem + kOffState + warp * 128);
+    Item& it = *reinterpret_cast<Item*>(smem + kOffState + warp * 128 + 32);
+    walker_init(p, w);
+    uint32_t t = 0;    // S_0 tiles seen
+    uint32_t nst = 0;  // items whose statistics were written
+    bool ok = true;
+    while (ok && walker_next(p, w, it)) {
+      const int ni = it.n0;
+      const int tok = it.q0 + (row & (p.tq - 1));
+      const int lim = p.causal ? min(max(tok + 1 + it.off, 0), it.K) : it.K;
+      float m = NEG_INF, l = 0.f;
+      for (int j = 0; j < ni; ++j, ++t) {
+        if (!(ok = wait_all(&s_full[0], t & 1))) break;
+        tc_fence_after();
+        float sv[2][32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) tmem_ld32(taddr + h * 64 + c * 32, sv[c]);
+        tc_wait_ld();
+        const int nvis = lim - j * kKeys - h * 64;  // visible columns of this half
+        float mx[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mx[a] = NEG_INF;
+        const bool whole = __all_sync(0xffffffffu, nvis >= 64);
+        if (whole) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) mx[(e >> 1) & 7] = fmax3(mx[(e >> 1) & 7], sv[c][e], sv[c][e + 1]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float x0 = (c * 32 + e < nvis) ? sv[c][e] : NEG_INF;
+              const float x1 = (c * 32 + e + 1 < nvis) ? sv[c][e + 1] : NEG_INF;
+              sv[c][e] = x0;
+              sv[c][e + 1] = x1;
+              mx[(e >> 1) & 7] = fmax3(mx[(e >> 1) & 7], x0, x1);
+            }
+        }
+        const float mh = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
+        // Exchange the halves' maxima. Both halves' S loads have completed
+        // once the other warpgroup's arrival is seen, so warpgroup 1 may then
+        // write its P over S columns 32-63 (keys 32-63 of warpgroup 0).
+        xmax[h * kRows + row] = mh;
+        mbar_arrive(&x_full[h]);
+        if (!(ok = wait_all(&x_full[h ^ 1], t & 1))) break;
+        const float mt = fmaxf(mh, xmax[(h ^ 1) * kRows + row]) * sl2;
+        const float m_new = (mt > m + 8.f) ? mt : m;
+        const float m_ref = (m_new == NEG_INF) ? 0.f : m_new;
+        const float alpha = ex2(m - m_ref);
+        const float neg_m = -m_ref;
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(neg_m, neg_m);
+        uint64_t acc2[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) acc2[a] = 0ull;
+        float pk[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {
+          const uint64_t y2 = f2_fma(f2_pack(sv[x >> 4][(x & 15) * 2], sv[x >> 4][(x & 15) * 2 + 1]), sl2x2, negm2);
+          float e0, e1;
+          f2_unpack(y2, e0, e1);
+          e0 = ex2(e0);
+          e1 = ex2(e1);
+          acc2[x & 3] = f2_add(acc2[x & 3], f2_pack(e0, e1));
+          pk[x] = __uint_as_float(pack_bf16x2(e0, e1));
+        }
+        tmem_st32(taddr + h * 32, pk);  // P of keys 64h..64h+63: columns 32h..32h+31
+        float ps[8];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) f2_unpack(acc2[a], ps[2 * a], ps[2 * a + 1]);
+        l = l * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
+        if (j >= 1 && __any_sync(0xffffffffu, m_new != m)) {  // this half's 64 columns of O
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            float o[32];
+            tmem_ld32(taddr + kColO + h * 64 + c * 32, o);
+            tc_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(taddr + kColO + h * 64 + c * 32, o);
+          }
+        }
+        m = m_new;
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[0]);
+      }
+      if (!ok) break;
+      // Row statistics: the two halves' partial sums (same max) in the l
+      // rows of tiles 0 and 1, the max in tile 0's; the epilogue adds them.
+      if (!(ok = wait_all(&st_empty[0], (nst & 1) ^ 1u))) break;
+      stats[(h * 2 + 0) * kRows + row] = l;
+      if (h == 0) stats[kRows + row] = m;
+      mbar_arrive(&st_full[0]);
+      ++nst;
+    }
+  } else if (wg < 2) {
     regs_inc<kRegSoftmax>();
     // ------------------------------------------------------------ softmax of tile i = wg
     const int i = wg;
@@ -433,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ni == 0) continue;
         cp[i] += ni;
         if (!(ok = wait_all(&st_full[i], items_i[i] & 1))) break;
-        const float l = stats[(i * 2 + 0) * kRows + row];
+        const float l = kSplit ? stats[row] + stats[2 * kRows + row] : stats[(i * 2 + 0) * kRows + row];
         const float m = stats[(i * 2 + 1) * kRows + row];
         mbar_arrive(&st_empty[i]);
         if (!(ok = wait_all(&s_free[i], (cp[i] - 1) & 1))) break;  // the item's last PV_i
@@ -689,8 +803,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 int prefill_init(int device) {
   (void)device;
-  cudaError_t e = cudaFuncSetAttribute(prefill::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(prefill::prefill_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(prefill::kSmemBytes));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(prefill::prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(prefill::kSmemBytes));
   return cuda_status(e);
 }
 
@@ -719,7 +836,10 @@ static int launch(const CUtensorMap& tq_map, const CUtensorMap& tk_map, const CU
   if (items > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
   const long long ctas = sms;  // one persistent CTA per SM (all of its TMEM and most of its shared memory)
   const dim3 grid(static_cast<unsigned>(items < ctas ? items : ctas));
-  return cuda_status(launch_pdl(prefill_kernel, grid, dim3(kThreads), kSmemBytes, stream, tq_map, tk_map, tv_map, p));
+  return cuda_status(p.pair == 1 ? launch_pdl(prefill_kernel<true>, grid, dim3(kThreads), kSmemBytes, stream, tq_map,
+                                               tk_map, tv_map, p)
+                                 : launch_pdl(prefill_kernel<false>, grid, dim3(kThreads), kSmemBytes, stream, tq_map,
+                                              tk_map, tv_map, p));
 }
 
 // Q map [total, Hq, D] with a (64 dims, 1 head, tq tokens) box, and the
