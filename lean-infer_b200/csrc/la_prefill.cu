@@ -79,9 +79,14 @@ constexpr int kOffStage = kOffKV + kStages * kKVTile;      // 192 KB
 constexpr int kStageBytes = 32 * 128;                      // 32 rows x 64 dims bf16
 constexpr int kOffStats = kOffStage + 4 * kStageBytes;     // 208 KB
 constexpr int kOffBar = kOffStats + 2 * 2 * kRows * 4;     // + 2 KB
-constexpr int kOffState = kOffBar + 256;                   // per softmax warp: Walker + Item, 128 B
-constexpr int kOffXmax = kOffState + 8 * 128;              // split softmax: row maxima of the two halves
-constexpr size_t kSmemBytes = kOffXmax + 2 * kRows * 4 + 1024;
+// After the barriers: per softmax warp its Walker + Item (128 B); the split
+// instance has 256 B more of barriers and, after the walk state, its row
+// maxima [step % 2][half][row].
+template <bool kSplit>
+__host__ __device__ constexpr int off_state() { return kOffBar + (kSplit ? 512 : 256); }
+template <bool kSplit>
+__host__ __device__ constexpr int off_xmax() { return off_state<kSplit>() + 8 * 128; }
+constexpr size_t kSmemBytes = off_xmax<true>() + 2 * 2 * kRows * 4 + 1024;  // both instances
 
 struct Params {
   const int* cu;  // query starts [num_seqs + 1], or null: sequence s has q_len queries from token s * q_len
@@ -232,7 +237,10 @@ __device__ __forceinline__ bool walker_next(const Params& p, Walker& w, Item& it
 
 // kSplit (items of single query tiles): both softmax warpgroups work on tile
 // 0, warpgroup h on keys 64h..64h+63 of each 128-key tile, exchanging their
-// row maxima through shared memory, so one tile's softmax takes half as long.
+// row maxima through shared memory, so one tile's softmax takes half as long;
+// and S is double buffered in the TMEM columns a second tile would use, so
+// S(j+1) is computed while the softmax works on S(j) and the softmax runs
+// from one KV tile to the next without waiting for the tensor core.
 template <bool kSplit>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -254,7 +262,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* st_full = bars + 18;      // [2] row statistics of tile i written (128)
   uint64_t* st_empty = bars + 20;     // [2] ... read by the epilogue (128)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
-  uint64_t* x_full = bars + 26;       // [2] kSplit: warpgroup h's row maxima written (128)
+  // kSplit: the two softmax warpgroups may be one step apart (S is double
+  // buffered), so their exchange and their P-ready arrivals alternate
+  // between two barriers by step parity, [2 * (step % 2) + h] and
+  // [2 * h + step % 2] (128 arrivals each).
+  uint64_t* x_full = bars + 32;       // [4] warpgroup h's row maxima of a step written
+  uint64_t* ph_full = bars + 36;      // [4] warpgroup h's half of P(step) written
+  // kSplit: an item's last PV done. The softmax no longer waits for each PV
+  // before the next S, so s_free may lag the epilogue by more than one phase
+  // and its parity cannot name the item's last PV.
+  uint64_t* o_full = bars + 40;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -278,10 +295,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 1);
-      mbar_init(&p_full[i], kSplit && i == 0 ? 256 : 128);
+      mbar_init(&p_full[i], 128);
       mbar_init(&o_empty[i], 128);
       mbar_init(&st_full[i], kSplit && i == 0 ? 256 : 128);
-      mbar_init(&x_full[i], 128);
+      if (kSplit) {
+        if (i == 0) mbar_init(o_full, 1);
+        mbar_init(&x_full[i], 128);
+        mbar_init(&x_full[i + 2], 128);
+        mbar_init(&ph_full[i], 128);
+        mbar_init(&ph_full[i + 2], 128);
+      }
       mbar_init(&st_empty[i], 128);
     }
     fence_barrier_init();
@@ -307,9 +330,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quarter * 32 + lane;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
-    float* xmax = reinterpret_cast<float*>(smem + kOffXmax);  // [half][row]
-    Walker& w = *reinterpret_cast<Walker*>(smem + kOffState + warp * 128);
-    Item& it = *reinterpret_cast<Item*>(smem + kOffState + warp * 128 + 32);
+    float* xmax = reinterpret_cast<float*>(smem + off_xmax<kSplit>());  // [step % 2][half][row]
+    Walker& w = *reinterpret_cast<Walker*>(smem + off_state<kSplit>() + warp * 128);
+    Item& it = *reinterpret_cast<Item*>(smem + off_state<kSplit>() + warp * 128 + 32);
     walker_init(p, w);
     uint32_t t = 0;    // S_0 tiles seen
     uint32_t nst = 0;  // items whose statistics were written
@@ -320,11 +343,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int lim = p.causal ? min(max(tok + 1 + it.off, 0), it.K) : it.K;
       float m = NEG_INF, l = 0.f;
       for (int j = 0; j < ni; ++j, ++t) {
-        if (!(ok = wait_all(&s_full[0], t & 1))) break;
+        const uint32_t colS = (t & 1) * 128;  // S double buffer
+        if (!(ok = wait_all(&s_full[t & 1], (t >> 1) & 1))) break;
         tc_fence_after();
         float sv[2][32];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) tmem_ld32(taddr + h * 64 + c * 32, sv[c]);
+        for (int c = 0; c < 2; ++c) tmem_ld32(taddr + colS + h * 64 + c * 32, sv[c]);
         tc_wait_ld();
         const int nvis = lim - j * kKeys - h * 64;  // visible columns of this half
         float mx[8];
@@ -352,10 +376,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Exchange the halves' maxima. Both halves' S loads have completed
         // once the other warpgroup's arrival is seen, so warpgroup 1 may then
         // write its P over S columns 32-63 (keys 32-63 of warpgroup 0).
-        xmax[h * kRows + row] = mh;
-        mbar_arrive(&x_full[h]);
-        if (!(ok = wait_all(&x_full[h ^ 1], t & 1))) break;
-        const float mt = fmaxf(mh, xmax[(h ^ 1) * kRows + row]) * sl2;
+        const uint32_t sb = t & 1;
+        xmax[(sb * 2 + h) * kRows + row] = mh;
+        mbar_arrive(&x_full[sb * 2 + h]);
+        if (!(ok = wait_all(&x_full[sb * 2 + (h ^ 1)], (t >> 1) & 1))) break;
+        const float mt = fmaxf(mh, xmax[(sb * 2 + (h ^ 1)) * kRows + row]) * sl2;
         const float m_new = (mt > m + 8.f) ? mt : m;
         const float m_ref = (m_new == NEG_INF) ? 0.f : m_new;
         const float alpha = ex2(m - m_ref);
@@ -375,12 +400,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc2[x & 3] = f2_add(acc2[x & 3], f2_pack(e0, e1));
           pk[x] = __uint_as_float(pack_bf16x2(e0, e1));
         }
-        tmem_st32(taddr + h * 32, pk);  // P of keys 64h..64h+63: columns 32h..32h+31
+        tmem_st32(taddr + colS + h * 32, pk);  // P of keys 64h..64h+63: columns 32h..32h+31
         float ps[8];
 #pragma unroll
         for (int a = 0; a < 4; ++a) f2_unpack(acc2[a], ps[2 * a], ps[2 * a + 1]);
         l = l * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
         if (j >= 1 && __any_sync(0xffffffffu, m_new != m)) {  // this half's 64 columns of O
+          // S(j) may have been issued before PV(j-1): wait for it (the
+          // (t-1)-th PV) before touching O.
+          if (!(ok = wait_all(&s_free[0], (t - 1) & 1))) break;
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < 2; ++c) {
             float o[32];
@@ -394,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         m = m_new;
         tc_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_full[0]);
+        mbar_arrive(&ph_full[h * 2 + sb]);
       }
       if (!ok) break;
       // Row statistics: the two halves' partial sums (same max) in the l
@@ -417,8 +446,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // The walk state lives in shared memory: it is only needed between
     // tiles, and keeping it out of registers leaves them to the
     // exponential loop.
-    Walker& w = *reinterpret_cast<Walker*>(smem + kOffState + warp * 128);
-    Item& it = *reinterpret_cast<Item*>(smem + kOffState + warp * 128 + 32);
+    Walker& w = *reinterpret_cast<Walker*>(smem + off_state<kSplit>() + warp * 128);
+    Item& it = *reinterpret_cast<Item*>(smem + off_state<kSplit>() + warp * 128 + 32);
     walker_init(p, w);
     uint32_t t = 0;      // S_i tiles seen
     uint32_t nst = 0;    // items whose statistics were written
@@ -550,7 +579,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float l = kSplit ? stats[row] + stats[2 * kRows + row] : stats[(i * 2 + 0) * kRows + row];
         const float m = stats[(i * 2 + 1) * kRows + row];
         mbar_arrive(&st_empty[i]);
-        if (!(ok = wait_all(&s_free[i], (cp[i] - 1) & 1))) break;  // the item's last PV_i
+        // the item's last PV_i
+        if (!(ok = kSplit ? wait_all(o_full, items_i[i] & 1) : wait_all(&s_free[i], (cp[i] - 1) & 1))) break;
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
         const int qt0 = it.q0 + i * p.tq;
@@ -681,6 +711,94 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (long long u = (nld > kStages ? nld - kStages : 0); u < nld; ++u)
           mbar_wait(&kv_full[u % kStages], static_cast<uint32_t>(u / kStages) & 1, nullptr, 0);
         if (kq > 0) mbar_wait(q_full, (kq - 1) & 1, nullptr, 0);
+      }
+      __syncwarp();
+    } else if (warp == 12 && kSplit) {
+      // ------------------------------------ MMA issuer, single-tile items (lane 0 issues)
+      // S is double-buffered in TMEM (S(j) in columns 128 (j % 2) + [0, 128),
+      // P(j) over the first 64 of them): S(j+2) is issued right behind PV(j),
+      // which reads P(j) from the same columns (the tensor core executes this
+      // thread's MMAs in order), while the softmax works on S(j+1).
+      Walker w;
+      walker_init(p, w);
+      Item it;
+      int kq = 0;
+      long long nld = 0;  // K/V ring position of the item's K(0)
+      uint32_t sc = 0;    // S tiles issued
+      uint32_t cp = 0;    // PVs issued
+      uint32_t items = 0;
+      bool ok = true;
+      auto slot_of = [&](long long idx) -> int { return static_cast<int>(idx % kStages); };
+      auto wait_full = [&](long long idx) -> bool {
+        return wait_all(&kv_full[slot_of(idx)], static_cast<uint32_t>(idx / kStages) & 1);
+      };
+      // The next S from the K tile at ring position kpos; the item's last S
+      // frees Q.
+      auto issue_s = [&](long long kpos, bool last_s) -> bool {
+        if (!wait_full(kpos)) return false;
+        const uint32_t b = sc & 1;
+        if (lane == 0) {
+          const uint64_t ad = desc_kmajor(sQ, kQHalf, 0);
+          const uint64_t bd = desc_kmajor(sKV + slot_of(kpos) * kKVTile, kKVHalf, 0);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_f16_ss(tmem + b * 128, ad + (((ks >> 2) * kQHalf + (ks & 3) * 32) >> 4),
+                        bd + (((ks >> 2) * kKVHalf + (ks & 3) * 32) >> 4), kIdescQK, ks > 0 ? 1u : 0u);
+          umma_commit(&s_full[b]);
+          umma_commit(&kv_empty[slot_of(kpos)]);
+          if (last_s) umma_commit(q_empty);
+        }
+        __syncwarp();
+        ++sc;
+        return true;
+      };
+      while (ok && walker_next(p, w, it)) {
+        if (!(ok = wait_all(q_full, kq & 1))) break;
+        ++kq;
+        const int n = it.n0;
+        const long long base = nld;  // K(j) at base + 2j, V(j) at base + 2j + 1
+        nld += 2LL * n;
+        const uint32_t b0 = sc & 1;  // S buffer of this item's S(0)
+        if (!(ok = issue_s(base, n == 1))) break;
+        if (n >= 2 && !(ok = issue_s(base + 2, n == 2))) break;
+        for (int j = 0; j < n && ok; ++j) {
+          const long long vi = base + 2 * j + 1;
+          if (!(ok = wait_full(vi))) break;
+          uint8_t* vt = sKV + slot_of(vi) * kKVTile;
+          const int vrows = it.K - j * kKeys;  // valid V rows of this tile
+          if (p.paged && vrows < kKeys) {
+            // Pool slots past the sequence's last key hold whatever was there
+            // (possibly NaN); P is 0 for them but 0 * NaN is not, so zero them.
+            const int r0 = max(vrows, 0);
+            const int n16 = (kKeys - r0) * 8;  // 16-byte chunks per half
+            for (int x = lane; x < 2 * n16; x += 32) {
+              const int half = x / n16, c = x - half * n16;
+              *reinterpret_cast<uint4*>(vt + half * kKVHalf + r0 * 128 + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+          }
+          if (!(ok = wait_all(&ph_full[cp & 1], (cp >> 1) & 1))) break;   // both halves of P(j)
+          if (!(ok = wait_all(&ph_full[2 + (cp & 1)], (cp >> 1) & 1))) break;
+          if (j == 0) {  // O is overwritten: the epilogue must have read the previous item's
+            if (items > 0 && !(ok = wait_all(&o_empty[0], (items - 1) & 1))) break;
+            ++items;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t pt = tmem + ((b0 + j) & 1) * 128;  // P(j): 16 keys per 8 columns
+            const uint64_t vd = desc_v(vt, 0);                 // k-step ks: + 2048 B / 16
+#pragma unroll
+            for (int ks = 0; ks < kKeys / 16; ++ks)
+              umma_f16_ts(tmem + kColO, pt + ks * 8, vd + ks * 128, kIdescPV, (j > 0 || ks > 0) ? 1u : 0u);
+            umma_commit(&s_free[0]);
+            umma_commit(&kv_empty[slot_of(vi)]);
+            if (j + 1 == n) umma_commit(o_full);
+          }
+          __syncwarp();
+          ++cp;
+          if (j + 2 < n && !(ok = issue_s(base + 2 * (j + 2), j + 3 == n))) break;
+        }
       }
       __syncwarp();
     } else if (warp == 12) {
