@@ -30,7 +30,8 @@
 // raised (and O, l rescaled) only when a tile's max exceeds the running one
 // by more than 8 (log2 units), so most tiles skip the rescale.
 //
-// Warps (16): 0-3 softmax of tile 0, 4-7 softmax of tile 1, 8-11 epilogue
+// Warps (16): 0-3 softmax of tile 0, 4-7 softmax of tile 1 (for items of one
+// query tile, both warpgroups work on tile 0: see kSplit), 8-11 epilogue
 // (normalise O_i, store it through shared memory with coalesced rows, lse),
 // 12 MMA issuer + TMEM owner, 13 TMA producer, 14-15 idle. Warp w reads TMEM
 // lanes 32*(w%4)..+31. Registers are moved between warpgroups with
