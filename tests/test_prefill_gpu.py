@@ -26,8 +26,13 @@ def _case(lengths, hq=16, hkv=8, seed=0):
     return q, k, v, cu, int(lens.max()) if len(lengths) else 0
 
 
-def run(pkg, dev, lengths, hq=16, hkv=8, seed=0, causal=True, lse=False):
+def run(pkg, dev, lengths, hq=16, hkv=8, seed=0, causal=True, lse=False, key_ramp=0.0, v_scale=1.0):
     q, k, v, cu, mx = _case(lengths, hq, hkv, seed)
+    if v_scale != 1.0:
+        v = (v.float() * v_scale).to(torch.bfloat16)
+    if key_ramp:  # keys scaled up along each sequence: the running row max keeps rising
+        pos = torch.cat([torch.arange(n, dtype=torch.float32) / max(n, 1) for n in lengths])
+        k = (k.float() * (1 + key_ramp * pos).view(-1, 1, 1)).to(torch.bfloat16)
     cud = cu.to(dev)
     res = pkg.flash_attn_varlen_func(q.to(dev), k.to(dev), v.to(dev), cud, cud, mx, mx, causal=causal,
                                      return_softmax_lse=lse)
@@ -83,6 +88,22 @@ def test_config_b16_packed(pkg, cuda_dev):
 
 def test_config_b1(pkg, cuda_dev):
     run(pkg, cuda_dev, [777], seed=2)
+
+
+@pytest.mark.parametrize("n", [3, 16])
+def test_rising_scores(pkg, cuda_dev, n):
+    """Scores that grow along the keys, so O is rescaled tile after tile.
+    Three prompts of 700 tokens leave too few query-tile pairs to fill the
+    SMs: items are single tiles (both softmax warpgroups on one tile, S
+    double buffered in TMEM) and most CTAs take two of them; sixteen
+    prompts run as pairs. Peaked softmax rows make each output close to one
+    value row, and with the running max raised only past +8 (log2) the
+    dominant P is a rounded bf16 value rather than exactly 1 (about 0.013 on
+    unit-variance values, by a CPU emulation of the algorithm), on top of
+    the bf16 rounding of the output (half an ulp is 2^-8 |out|): the values
+    are scaled by 1/4 to keep both well inside the absolute tolerance. A
+    missing or misplaced rescale would still miss by the size of the output."""
+    run(pkg, cuda_dev, [700] * n, seed=40 + n, lse=True, key_ramp=10.0, v_scale=0.25)
 
 
 @pytest.mark.parametrize("L", [1, 2, 63, 64, 65, 127, 128, 129, 255, 256, 1024, 1100])
