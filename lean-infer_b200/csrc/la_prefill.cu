@@ -71,6 +71,15 @@ static_assert(kRegSoftmax >= 128 && kRegEpilogue <= 128 && kRegOther <= 128,
 static_assert(kRegSoftmax % 8 == 0 && kRegEpilogue % 8 == 0 && kRegOther % 8 == 0 && kRegEpilogue >= 24 &&
                   kRegSoftmax <= 256,
               "setmaxnreg counts are multiples of 8 in [24, 256]");
+// The split instance's softmax holds half an S row per thread: it gives 8
+// registers per thread to the epilogue and the MMA/TMA warps (no spills).
+constexpr int kRegSoftmaxSplit = 152, kRegEpilogueSplit = 104, kRegOtherSplit = 104;
+static_assert(256 * kRegSoftmaxSplit + 128 * kRegEpilogueSplit + 128 * kRegOtherSplit <= kThreads * 128,
+              "the register split must fit in the registers the CTA is launched with");
+static_assert(kRegSoftmaxSplit >= 128 && kRegEpilogueSplit <= 128 && kRegOtherSplit <= 128,
+              "softmax warpgroups use setmaxnreg.inc, the others setmaxnreg.dec");
+static_assert(kRegSoftmaxSplit % 8 == 0 && kRegEpilogueSplit % 8 == 0 && kRegOtherSplit % 8 == 0,
+              "setmaxnreg counts are multiples of 8");
 // Shared memory: Q0 Q1 | K/V ring | O staging (4 KB per epilogue warp) |
 // row statistics (l, m of both tiles) | barriers | softmax walk state | the
 // split softmax's row maxima; base aligned to 1024 B (the 128-byte swizzle
@@ -324,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
 
   if (wg < 2 && kSplit) {
-    regs_inc<kRegSoftmax>();
+    regs_inc<kSplit ? kRegSoftmaxSplit : kRegSoftmax>();
     // ------------------------------------------------- softmax of tile 0, keys 64h..64h+63
     const int h = wg;
     const int quarter = warp & 3;
@@ -436,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++nst;
     }
   } else if (wg < 2) {
-    regs_inc<kRegSoftmax>();
+    regs_inc<kSplit ? kRegSoftmaxSplit : kRegSoftmax>();
     // ------------------------------------------------------------ softmax of tile i = wg
     const int i = wg;
     const int quarter = warp & 3;
@@ -559,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++nst;
     }
   } else if (wg == 2) {
-    regs_dec<kRegEpilogue>();
+    regs_dec<kSplit ? kRegEpilogueSplit : kRegEpilogue>();
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
@@ -636,7 +645,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    regs_dec<kRegOther>();
+    regs_dec<kSplit ? kRegOtherSplit : kRegOther>();
     if (warp == 13) {
       // ---------------------------------------------------------- TMA producer (lane 0 issues)
       // Per item: Q0 (+ Q1), then K(j), V(j) for j = 0..n-1 into the ring, in
