@@ -87,6 +87,39 @@ def test_uniform_chunks_with_kvcache(pkg, cuda_dev, bs, hkv):
     _check(out.view(B * Sq, hq, 128), ref, lse.permute(0, 2, 1).reshape(B * Sq, hq), ref_lse)
 
 
+@pytest.mark.parametrize("bs", [256, 16])
+def test_single_tile_chunks_rising_scores(pkg, cuda_dev, bs):
+    """Three chunks of 448 queries over prefixes of 100-1100 keys: too few
+    query-tile pairs to fill the SMs, so items are single tiles (both softmax
+    warpgroups on one tile, S double buffered in TMEM) and some CTAs take
+    two; keys scaled up along each sequence so that O is rescaled tile after
+    tile; pool slots past each sequence's keys hold NaN. Values are scaled by
+    1/4 for the same reason as in the contiguous rising-score test: peaked
+    rows put whole value rows, rounded, into the bf16 output."""
+    Sq, hq = 448, 16
+    prefix = [100, 600, 1100]
+    k_lens = [p + Sq for p in prefix]
+    B = len(prefix)
+    bt, nb = _tables(k_lens, bs, seed=70 + bs)
+    kc, vc = _pool(nb, bs, 8, seed=71)
+    kc, vc = kc.float(), vc.float() * 0.25
+    for s, K in enumerate(k_lens):
+        t = torch.arange(K)
+        blk, slot = bt[s, t // bs].long(), t % bs
+        kc[blk, slot] = kc[blk, slot] * (1 + 10.0 * t.float() / K).view(-1, 1, 1)
+    kc, vc = _nan_tails(kc.to(torch.bfloat16), vc.to(torch.bfloat16), bt, k_lens, bs)
+    g = torch.Generator().manual_seed(72)
+    q = torch.randn(B, Sq, hq, 128, generator=g).to(torch.bfloat16)
+    kl = torch.tensor(k_lens, dtype=torch.int32)
+    out, lse = pkg.flash_attn_with_kvcache(q.to(cuda_dev), kc.to(cuda_dev), vc.to(cuda_dev), cache_seqlens=kl.to(cuda_dev),
+                                           block_table=bt.to(cuda_dev), causal=True, return_softmax_lse=True)
+    torch.cuda.synchronize()
+    pkg.check_device_errors(cuda_dev.index)
+    cu = torch.arange(B + 1, dtype=torch.int32) * Sq
+    ref, ref_lse = opa.paged_chunk_prefill(q.view(B * Sq, hq, 128), kc, vc, bt, kl, cu, return_lse=True)
+    _check(out.view(B * Sq, hq, 128), ref, lse.permute(0, 2, 1).reshape(B * Sq, hq), ref_lse)
+
+
 @pytest.mark.parametrize("causal", [True, False])
 def test_varlen_chunks_with_block_table(pkg, cuda_dev, causal):
     """flash_attn_varlen_func with a block_table: ragged chunk lengths (1 to
