@@ -210,6 +210,21 @@ def random_model(cfg: ModelConfig, device, seed: int = 0, dtype=torch.bfloat16) 
     return m.to(dtype).eval()
 
 
+def staging_views(buf: torch.Tensor, n_slots: int, max_blocks: int):
+    """(ids [B, 1] i64, pos [B] i64, ctx [B] i32, bt [B, max_blocks] i32) as
+    views of one uint8 buffer of staging_bytes(B, max_blocks) bytes, laid out
+    ids | pos | ctx | bt, so that the four inputs move in a single copy."""
+    B = n_slots
+    o_pos, o_ctx, o_bt = 8 * B, 16 * B, 20 * B
+    assert buf.dtype == torch.uint8 and buf.numel() == staging_bytes(B, max_blocks)
+    return (buf[:o_pos].view(torch.long).view(B, 1), buf[o_pos:o_ctx].view(torch.long),
+            buf[o_ctx:o_bt].view(torch.int32), buf[o_bt:].view(torch.int32).view(B, max_blocks))
+
+
+def staging_bytes(n_slots: int, max_blocks: int) -> int:
+    return 20 * n_slots + 4 * n_slots * max_blocks
+
+
 class DecodeGraph:
     """Fixed-B decode step captured in a CUDA graph — the engine's DecodeGraph
     (leaninfer/engine/llm_engine.py:23-86): pinned host staging buffers,
@@ -223,19 +238,11 @@ class DecodeGraph:
     def __init__(self, model: Qwen3ForCausalLM, cache: BlockCache, n_slots: int, max_blocks: int) -> None:
         self.model, self.cache = model, cache
         dev = cache.device
-        B = n_slots
-        # byte layout: ids [B] i64 | pos [B] i64 | ctx [B] i32 | bt [B, max_blocks] i32
-        o_pos, o_ctx, o_bt = 8 * B, 16 * B, 20 * B
-        nbytes = o_bt + 4 * B * max_blocks
-
-        def views(buf: torch.Tensor):
-            return (buf[:o_pos].view(torch.long).view(B, 1), buf[o_pos:o_ctx].view(torch.long),
-                    buf[o_ctx:o_bt].view(torch.int32), buf[o_bt:].view(torch.int32).view(B, max_blocks))
-
+        nbytes = staging_bytes(n_slots, max_blocks)
         self._host_buf = torch.zeros(nbytes, dtype=torch.uint8, pin_memory=True)
         self._dev_buf = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
-        self.host_ids, self.host_pos, self.host_ctx, self.host_bt = views(self._host_buf)
-        self.ids, self.pos, self.ctx, self.bt = views(self._dev_buf)
+        self.host_ids, self.host_pos, self.host_ctx, self.host_bt = staging_views(self._host_buf, n_slots, max_blocks)
+        self.ids, self.pos, self.ctx, self.bt = staging_views(self._dev_buf, n_slots, max_blocks)
         self.host_ctx.fill_(1)
         self.ctx.fill_(1)
         self.graph: torch.cuda.CUDAGraph | None = None
