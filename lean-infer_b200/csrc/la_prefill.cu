@@ -417,7 +417,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         l = l * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
         if (j >= 1 && __any_sync(0xffffffffu, m_new != m)) {  // this half's 64 columns of O
           // S(j) may have been issued before PV(j-1): wait for it (the
-          // (t-1)-th PV) before touching O.
+          // (t-1)-th PV) before touching O. The parity names that PV: the
+          // tensor core completes this thread's MMAs in order, so PV(t-2)
+          // is done once S(t) is, and PV(t) waits for this warpgroup's P(t).
           if (!(ok = wait_all(&s_free[0], (t - 1) & 1))) break;
           tc_fence_after();
 #pragma unroll 1
