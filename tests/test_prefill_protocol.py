@@ -1,0 +1,293 @@
+"""A CPU model of the synchronisation of the prefill kernel's split instance
+(lean-infer_b200/csrc/la_prefill.cu, prefill_kernel<true>: items of one query
+tile, both softmax warpgroups on the tile's two key halves, S double buffered
+in TMEM), run under many random schedules.
+
+Every actor follows the kernel's order of waits, arrivals and commits: the TMA
+producer, the MMA issuer, softmax warpgroups 0 and 1, the epilogue, plus the
+TMA engine (copies land in any order) and the tensor core (MMAs execute and
+commits arrive in issue order). Barriers behave as mbarriers do: a parity wait
+passes while the number of completed phases has the other parity, so a barrier
+two phases ahead of its waiter passes the wait as well. Shared memory, the K/V
+ring and TMEM carry version tags, and every read checks that it sees the
+version the kernel means, so a wait that passes on the wrong phase, or a write
+that lands before the last read of what it overwrites, fails the run; so does a
+deadlock. Three planted mistakes, each one a bug met while building the
+kernel (the row-max exchange on one barrier and one slot per half, one
+P-ready barrier counting both halves, and the epilogue waiting on the PV
+barrier's parity), must be caught.
+
+The row-max decision to rescale O is data dependent in the kernel; the model
+draws it at random per warpgroup and step, which covers every case."""
+import random
+
+import pytest
+
+
+class Bar:
+    def __init__(self, name, count):
+        self.name, self.count = name, count
+        self.pending, self.tx, self.phases = count, 0, 0
+
+    def _check(self):
+        if self.pending == 0 and self.tx == 0:
+            self.phases += 1
+            self.pending = self.count
+
+    def arrive(self, expect_tx=0):
+        assert self.pending > 0, f"{self.name}: arrival beyond the expected count"
+        self.tx += expect_tx
+        self.pending -= 1
+        self._check()
+
+    def complete_tx(self, n):
+        self.tx -= n
+        self._check()
+
+    def ready(self, parity):
+        return (self.phases & 1) != parity
+
+
+class Hazard(AssertionError):
+    pass
+
+
+class Model:
+    STAGES = 4
+
+    def __init__(self, items, rng, plant=None):
+        self.items, self.rng, self.plant = items, rng, plant
+        B = Bar
+        self.q_full, self.q_empty = B("q_full", 1), B("q_empty", 1)
+        self.kv_full = [B(f"kv_full{i}", 1) for i in range(self.STAGES)]
+        self.kv_empty = [B(f"kv_empty{i}", 1) for i in range(self.STAGES)]
+        self.s_full = [B(f"s_full{i}", 1) for i in range(2)]
+        self.s_free = B("s_free", 1)
+        self.o_empty, self.o_full = B("o_empty", 1), B("o_full", 1)
+        self.st_full, self.st_empty = B("st_full", 2), B("st_empty", 1)
+        self.x_full = [B(f"x_full{i}", 1) for i in range(4)]
+        self.ph_full = [B(f"ph_full{i}", 1) for i in range(4)]
+        self.p_full = B("p_full", 2)  # planted: one P-ready barrier for both halves
+        self.mem = {}          # region -> version tag
+        self.tma = []          # copies in flight: (region, tag, bar, bytes)
+        self.tc = []           # tensor-core queue: ("mma", fn) | ("commit", bar)
+        self.starts = []       # global S / PV index of each item's first tile
+        t = 0
+        for n in items:
+            self.starts.append(t)
+            t += n
+
+    # -- helpers
+    def read(self, region, want):
+        got = self.mem.get(region)
+        if got != want:
+            raise Hazard(f"read {region}: found {got}, expected {want}")
+
+    def write(self, region, tag):
+        self.mem[region] = tag
+
+    # -- actors (generators yielding ("wait", bar, parity) or ("step",))
+    def producer(self):
+        nld = kq = 0
+        for k, n in enumerate(self.items):
+            yield ("wait", self.q_empty, (kq & 1) ^ 1)
+            self.q_full.arrive(expect_tx=1)
+            self.tma.append(("Q", ("Q", k), self.q_full, 1))
+            kq += 1
+            yield ("step",)
+            for j in range(n):
+                for kind in ("K", "V"):
+                    st = nld % self.STAGES
+                    yield ("wait", self.kv_empty[st], ((nld // self.STAGES) & 1) ^ 1)
+                    self.kv_full[st].arrive(expect_tx=1)
+                    self.tma.append((f"R{st}", (kind, k, j), self.kv_full[st], 1))
+                    nld += 1
+                    yield ("step",)
+
+    def mma(self):
+        nld = kq = sc = cp = items_done = 0
+        for k, n in enumerate(self.items):
+            yield ("wait", self.q_full, kq & 1)
+            kq += 1
+            base = nld
+            nld += 2 * n
+            b0 = sc & 1
+
+            def issue_s(kpos, j, last):
+                nonlocal sc
+                b, t = sc & 1, sc
+
+                def run(b=b, t=t, kpos=kpos, j=j, k=k):
+                    self.read("Q", ("Q", k))
+                    self.read(f"R{kpos % self.STAGES}", ("K", k, j))
+                    for r in range(4):
+                        self.write(f"S{b}.{r}", ("S", t))
+                self.tc.append(("mma", run))
+                self.tc.append(("commit", self.s_full[b]))
+                self.tc.append(("commit", self.kv_empty[kpos % self.STAGES]))
+                if last:
+                    self.tc.append(("commit", self.q_empty))
+                sc += 1
+
+            for jj in range(min(n, 2)):
+                kpos = base + 2 * jj
+                yield ("wait", self.kv_full[kpos % self.STAGES], (kpos // self.STAGES) & 1)
+                issue_s(kpos, jj, jj == n - 1)
+                yield ("step",)
+            for j in range(n):
+                vi = base + 2 * j + 1
+                yield ("wait", self.kv_full[vi % self.STAGES], (vi // self.STAGES) & 1)
+                if self.plant == "one_p_barrier":
+                    yield ("wait", self.p_full, cp & 1)
+                else:
+                    yield ("wait", self.ph_full[cp & 1], (cp >> 1) & 1)
+                    yield ("wait", self.ph_full[2 + (cp & 1)], (cp >> 1) & 1)
+                if j == 0:
+                    if items_done > 0:
+                        yield ("wait", self.o_empty, (items_done - 1) & 1)
+                    items_done += 1
+                t, buf = cp, (b0 + j) & 1
+
+                def pv(t=t, buf=buf, vi=vi, j=j, k=k):
+                    self.read(f"S{buf}.0", ("P", t, 0))
+                    self.read(f"S{buf}.1", ("P", t, 1))
+                    self.read(f"R{vi % self.STAGES}", ("V", k, j))
+                    for h in range(2):
+                        if j > 0:
+                            self.read(f"O{h}", ("O", k, j))
+                        self.write(f"O{h}", ("O", k, j + 1))
+                self.tc.append(("mma", pv))
+                self.tc.append(("commit", self.s_free))
+                self.tc.append(("commit", self.kv_empty[vi % self.STAGES]))
+                if j == n - 1:
+                    self.tc.append(("commit", self.o_full))
+                cp += 1
+                yield ("step",)
+                if j + 2 < n:
+                    kpos = base + 2 * (j + 2)
+                    yield ("wait", self.kv_full[kpos % self.STAGES], (kpos // self.STAGES) & 1)
+                    issue_s(kpos, j + 2, j + 3 == n)
+                    yield ("step",)
+
+    def softmax(self, h):
+        t = nst = 0
+        for k, n in enumerate(self.items):
+            for j in range(n):
+                buf = t & 1
+                yield ("wait", self.s_full[buf], (t >> 1) & 1)
+                self.read(f"S{buf}.{2 * h}", ("S", t))       # this half's 64 columns
+                self.read(f"S{buf}.{2 * h + 1}", ("S", t))
+                yield ("step",)
+                sb = t & 1
+                if self.plant == "one_exchange_barrier":  # one slot and one barrier per half
+                    xw, xr, xbar, xpar = f"xmax.{h}", f"xmax.{h ^ 1}", self.x_full[h ^ 1], t & 1
+                    mine = self.x_full[h]
+                else:
+                    xw, xr, xbar, xpar = f"xmax{sb}.{h}", f"xmax{sb}.{h ^ 1}", self.x_full[sb * 2 + (h ^ 1)], (t >> 1) & 1
+                    mine = self.x_full[sb * 2 + h]
+                self.write(xw, t)
+                mine.arrive()
+                yield ("step",)
+                yield ("wait", xbar, xpar)
+                self.read(xr, t)
+                yield ("step",)
+                self.write(f"S{buf}.{h}", ("P", t, h))       # P of keys 64h..64h+63: columns 32h..32h+31
+                yield ("step",)
+                if j >= 1 and self.rng.random() < 0.5:      # this half of O is rescaled
+                    yield ("wait", self.s_free, (t - 1) & 1)
+                    self.read(f"O{h}", ("O", k, j))
+                    yield ("step",)
+                (self.p_full if self.plant == "one_p_barrier" else self.ph_full[h * 2 + sb]).arrive()
+                t += 1
+                yield ("step",)
+            yield ("wait", self.st_empty, (nst & 1) ^ 1)
+            self.write(f"stats{h}", k)
+            self.st_full.arrive()
+            nst += 1
+            yield ("step",)
+
+    def epilogue(self):
+        cp = 0
+        for k, n in enumerate(self.items):
+            cp += n
+            yield ("wait", self.st_full, k & 1)
+            self.read("stats0", k)
+            self.read("stats1", k)
+            self.st_empty.arrive()
+            yield ("step",)
+            if self.plant == "epilogue_on_pv_parity":
+                yield ("wait", self.s_free, (cp - 1) & 1)
+            else:
+                yield ("wait", self.o_full, k & 1)
+            self.read("O0", ("O", k, n))
+            self.read("O1", ("O", k, n))
+            self.o_empty.arrive()
+            yield ("step",)
+
+    # -- scheduler
+    def run(self, max_ticks=200000):
+        actors = [self.producer(), self.mma(), self.softmax(0), self.softmax(1), self.epilogue()]
+        blocked = [None] * len(actors)  # (bar, parity) an actor waits on
+        done = [False] * len(actors)
+
+        def advance(i):
+            try:
+                cmd = next(actors[i])
+            except StopIteration:
+                done[i] = True
+                return
+            blocked[i] = (cmd[1], cmd[2]) if cmd[0] == "wait" else None
+
+        for i in range(len(actors)):
+            advance(i)
+        # Each run gives every actor and engine its own speed, from 1/64 to
+        # 64, so that some schedules let one side run far ahead of another.
+        speed = {key: 2.0 ** self.rng.uniform(-6, 6) for key in [("actor", i) for i in range(len(actors))] +
+                 [("tma", None), ("tc", None)]}
+        for _ in range(max_ticks):
+            choices = [("actor", i) for i in range(len(actors))
+                       if not done[i] and (blocked[i] is None or blocked[i][0].ready(blocked[i][1]))]
+            if self.tma:
+                choices.append(("tma", None))
+            if self.tc:
+                choices.append(("tc", None))
+            if not choices:
+                if all(done):
+                    return
+                waits = [f"{blocked[i][0].name}/{blocked[i][1]}" for i in range(len(actors)) if not done[i]]
+                raise Hazard(f"deadlock: waiting on {waits}")
+            kind, i = self.rng.choices(choices, weights=[speed[c] for c in choices])[0]
+            if kind == "actor":
+                blocked[i] = None
+                advance(i)
+            elif kind == "tma":
+                region, tag, bar, nbytes = self.tma.pop(self.rng.randrange(len(self.tma)))
+                self.write(region, tag)
+                bar.complete_tx(nbytes)
+            else:
+                op, arg = self.tc.pop(0)
+                if op == "mma":
+                    arg()
+                else:
+                    arg.arrive()
+        raise Hazard("schedule did not finish")
+
+
+ITEM_SETS = [[1], [2], [3], [4, 1], [1, 3, 2], [5, 1, 1, 4], [2, 2, 2, 2, 2]]
+
+
+@pytest.mark.parametrize("items", ITEM_SETS)
+def test_split_instance_protocol(items):
+    for seed in range(150):
+        Model(items, random.Random(seed * 7919 + len(items))).run()
+
+
+@pytest.mark.parametrize("plant", ["one_exchange_barrier", "one_p_barrier", "epilogue_on_pv_parity"])
+def test_planted_mistakes_are_caught(plant):
+    caught = 0
+    for seed in range(300):
+        try:
+            Model([5, 1, 4, 3], random.Random(seed), plant=plant).run()
+        except Hazard:
+            caught += 1
+    assert caught > 0, f"the planted mistake {plant} went unnoticed in 300 schedules"
