@@ -1,7 +1,9 @@
-"""A CPU model of the synchronisation of the prefill kernel's split instance
-(lean-infer_b200/csrc/la_prefill.cu, prefill_kernel<true>: items of one query
-tile, both softmax warpgroups on the tile's two key halves, S double buffered
-in TMEM), run under many random schedules.
+"""CPU models of the synchronisation of the prefill kernel
+(lean-infer_b200/csrc/la_prefill.cu), run under many random schedules: the
+split instance (prefill_kernel<true>: items of one query tile, both softmax
+warpgroups on the tile's two key halves, S double buffered in TMEM) and the
+pair instance (prefill_kernel<false>: items of two query tiles sharing the
+K/V tiles).
 
 Every actor follows the kernel's order of waits, arrivals and commits: the TMA
 producer, the MMA issuer, softmax warpgroups 0 and 1, the epilogue, plus the
@@ -12,10 +14,12 @@ two phases ahead of its waiter passes the wait as well. Shared memory, the K/V
 ring and TMEM carry version tags, and every read checks that it sees the
 version the kernel means, so a wait that passes on the wrong phase, or a write
 that lands before the last read of what it overwrites, fails the run; so does a
-deadlock. Three planted mistakes, each one a bug met while building the
-kernel (the row-max exchange on one barrier and one slot per half, one
-P-ready barrier counting both halves, and the epilogue waiting on the PV
-barrier's parity), must be caught.
+deadlock. Planted mistakes must be caught: for the split instance the three
+bugs met while building it (the row-max exchange on one barrier and one slot
+per half, one P-ready barrier counting both halves, the epilogue waiting on
+the PV barrier's parity); for the pair instance the orderings it relies on
+(S_i(j+1) behind PV_i(j), the O-empty wait before an item's first PV, Q
+released after an item's last S).
 
 The row-max decision to rescale O is data dependent in the kernel; the model
 draws it at random per warpgroup and step, which covers every case."""
@@ -50,6 +54,56 @@ class Bar:
 
 class Hazard(AssertionError):
     pass
+
+
+def run_schedule(m, actors, max_ticks=200000):
+    """Run the actors, the TMA engine and the tensor core of model m under a
+    random schedule drawn from m.rng; raise Hazard on a bad read, a deadlock
+    or a schedule that does not end."""
+    blocked = [None] * len(actors)  # (bar, parity) an actor waits on
+    done = [False] * len(actors)
+
+    def advance(i):
+        try:
+            cmd = next(actors[i])
+        except StopIteration:
+            done[i] = True
+            return
+        blocked[i] = (cmd[1], cmd[2]) if cmd[0] == "wait" else None
+
+    for i in range(len(actors)):
+        advance(i)
+    # Each run gives every actor and engine its own speed, from 1/64 to 64,
+    # so that some schedules let one side run far ahead of another.
+    speed = {key: 2.0 ** m.rng.uniform(-6, 6) for key in [("actor", i) for i in range(len(actors))] +
+             [("tma", None), ("tc", None)]}
+    for _ in range(max_ticks):
+        choices = [("actor", i) for i in range(len(actors))
+                   if not done[i] and (blocked[i] is None or blocked[i][0].ready(blocked[i][1]))]
+        if m.tma:
+            choices.append(("tma", None))
+        if m.tc:
+            choices.append(("tc", None))
+        if not choices:
+            if all(done):
+                return
+            waits = [f"{blocked[i][0].name}/{blocked[i][1]}" for i in range(len(actors)) if not done[i]]
+            raise Hazard(f"deadlock: waiting on {waits}")
+        kind, i = m.rng.choices(choices, weights=[speed[c] for c in choices])[0]
+        if kind == "actor":
+            blocked[i] = None
+            advance(i)
+        elif kind == "tma":
+            region, tag, bar, nbytes = m.tma.pop(m.rng.randrange(len(m.tma)))
+            m.write(region, tag)
+            bar.complete_tx(nbytes)
+        else:
+            op, arg = m.tc.pop(0)
+            if op == "mma":
+                arg()
+            else:
+                arg.arrive()
+    raise Hazard("schedule did not finish")
 
 
 class Model:
@@ -224,53 +278,184 @@ class Model:
             self.o_empty.arrive()
             yield ("step",)
 
-    # -- scheduler
-    def run(self, max_ticks=200000):
-        actors = [self.producer(), self.mma(), self.softmax(0), self.softmax(1), self.epilogue()]
-        blocked = [None] * len(actors)  # (bar, parity) an actor waits on
-        done = [False] * len(actors)
+    def run(self):
+        run_schedule(self, [self.producer(), self.mma(), self.softmax(0), self.softmax(1), self.epilogue()])
 
-        def advance(i):
-            try:
-                cmd = next(actors[i])
-            except StopIteration:
-                done[i] = True
-                return
-            blocked[i] = (cmd[1], cmd[2]) if cmd[0] == "wait" else None
 
-        for i in range(len(actors)):
-            advance(i)
-        # Each run gives every actor and engine its own speed, from 1/64 to
-        # 64, so that some schedules let one side run far ahead of another.
-        speed = {key: 2.0 ** self.rng.uniform(-6, 6) for key in [("actor", i) for i in range(len(actors))] +
-                 [("tma", None), ("tc", None)]}
-        for _ in range(max_ticks):
-            choices = [("actor", i) for i in range(len(actors))
-                       if not done[i] and (blocked[i] is None or blocked[i][0].ready(blocked[i][1]))]
-            if self.tma:
-                choices.append(("tma", None))
-            if self.tc:
-                choices.append(("tc", None))
-            if not choices:
-                if all(done):
-                    return
-                waits = [f"{blocked[i][0].name}/{blocked[i][1]}" for i in range(len(actors)) if not done[i]]
-                raise Hazard(f"deadlock: waiting on {waits}")
-            kind, i = self.rng.choices(choices, weights=[speed[c] for c in choices])[0]
-            if kind == "actor":
-                blocked[i] = None
-                advance(i)
-            elif kind == "tma":
-                region, tag, bar, nbytes = self.tma.pop(self.rng.randrange(len(self.tma)))
-                self.write(region, tag)
-                bar.complete_tx(nbytes)
-            else:
-                op, arg = self.tc.pop(0)
-                if op == "mma":
-                    arg()
+class PairModel(Model):
+    """The pair instance (prefill_kernel<false>): items of two query tiles that
+    share every K/V tile; S_i in its own TMEM columns with P_i written over
+    them; the MMA issuer interleaves PV_0(j), S_0(j+1), PV_1(j), S_1(j+1), so
+    S_i(j+1) overwrites P_i(j) only because it is issued behind PV_i(j); the
+    epilogue names an item's last PV_i by the PV barrier's parity. Items are
+    (n0, n1): K/V tiles of tile 0 and of tile 1 (0: no second tile; tile 1,
+    the later queries, may need one tile more)."""
+
+    def __init__(self, items, rng, plant=None):
+        super().__init__([max(a, b) for a, b in items], rng, plant)
+        self.pairs = items
+        B = Bar
+        self.s_full = [B(f"s_full{i}", 1) for i in range(2)]
+        self.s_free = [B(f"s_free{i}", 1) for i in range(2)]
+        self.p_full = [B(f"p_full{i}", 1) for i in range(2)]
+        self.o_empty = [B(f"o_empty{i}", 1) for i in range(2)]
+        self.st_full = [B(f"st_full{i}", 1) for i in range(2)]
+        self.st_empty = [B(f"st_empty{i}", 1) for i in range(2)]
+
+    def producer(self):
+        nld = kq = 0
+        for k, (n0, n1) in enumerate(self.pairs):
+            yield ("wait", self.q_empty, (kq & 1) ^ 1)
+            tiles = 2 if n1 else 1
+            self.q_full.arrive(expect_tx=tiles)
+            for i in range(tiles):
+                self.tma.append((f"Q{i}", ("Q", k, i), self.q_full, 1))
+            kq += 1
+            yield ("step",)
+            for j in range(max(n0, n1)):
+                for kind in ("K", "V"):
+                    st = nld % self.STAGES
+                    yield ("wait", self.kv_empty[st], ((nld // self.STAGES) & 1) ^ 1)
+                    self.kv_full[st].arrive(expect_tx=1)
+                    self.tma.append((f"R{st}", (kind, k, j), self.kv_full[st], 1))
+                    nld += 1
+                    yield ("step",)
+
+    def mma(self):
+        nld = kq = 0
+        sc, cp, items_i = [0, 0], [0, 0], [0, 0]
+        for k, (n0, n1) in enumerate(self.pairs):
+            n = max(n0, n1)
+            yield ("wait", self.q_full, kq & 1)
+            base = nld
+            nld += 2 * n
+
+            def issue_s(i, kpos, j):
+                t = sc[i]
+
+                def run(i=i, t=t, kpos=kpos, j=j, k=k):
+                    self.read(f"Q{i}", ("Q", k, i))
+                    self.read(f"R{kpos % self.STAGES}", ("K", k, j))
+                    self.write(f"S{i}", ("S", i, t))
+                self.tc.append(("mma", run))
+                self.tc.append(("commit", self.s_full[i]))
+                sc[i] += 1
+
+            def issue_pv(i, j, vi):
+                yield ("wait", self.p_full[i], cp[i] & 1)
+                if j == 0:
+                    if items_i[i] > 0 and self.plant != "no_o_empty_wait":
+                        yield ("wait", self.o_empty[i], (items_i[i] - 1) & 1)
+                    items_i[i] += 1
+                t = cp[i]
+
+                def pv(i=i, t=t, vi=vi, j=j, k=k):
+                    self.read(f"S{i}", ("P", i, t))
+                    self.read(f"R{vi % self.STAGES}", ("V", k, j))
+                    if j > 0:
+                        self.read(f"O{i}", ("O", k, j))
+                    self.write(f"O{i}", ("O", k, j + 1))
+                self.tc.append(("mma", pv))
+                self.tc.append(("commit", self.s_free[i]))
+                cp[i] += 1
+
+            yield ("wait", self.kv_full[base % self.STAGES], (base // self.STAGES) & 1)
+            issue_s(0, base, 0)
+            if n1 > 0:
+                issue_s(1, base, 0)
+            self.tc.append(("commit", self.kv_empty[base % self.STAGES]))
+            if n == 1 or self.plant == "q_empty_early":
+                self.tc.append(("commit", self.q_empty))
+            yield ("step",)
+            for j in range(n):
+                vi, ki = base + 2 * j + 1, base + 2 * j + 2
+                a0, a1, nx0, nx1 = j < n0, j < n1, j + 1 < n0, j + 1 < n1
+                yield ("wait", self.kv_full[vi % self.STAGES], (vi // self.STAGES) & 1)
+                if nx0 or nx1:
+                    yield ("wait", self.kv_full[ki % self.STAGES], (ki // self.STAGES) & 1)
+                if self.plant == "s_before_pv":  # S_0(j+1) ahead of PV_0(j): P_0(j) overwritten
+                    if nx0:
+                        issue_s(0, ki, j + 1)
+                    if a0:
+                        yield from issue_pv(0, j, vi)
                 else:
-                    arg.arrive()
-        raise Hazard("schedule did not finish")
+                    if a0:
+                        yield from issue_pv(0, j, vi)
+                    if nx0:
+                        issue_s(0, ki, j + 1)
+                yield ("step",)
+                if a1:
+                    yield from issue_pv(1, j, vi)
+                self.tc.append(("commit", self.kv_empty[vi % self.STAGES]))
+                if nx1:
+                    issue_s(1, ki, j + 1)
+                if j + 1 < n:
+                    self.tc.append(("commit", self.kv_empty[ki % self.STAGES]))
+                    if j + 2 == n and self.plant != "q_empty_early":
+                        self.tc.append(("commit", self.q_empty))
+                yield ("step",)
+            kq += 1
+
+    def softmax(self, i):
+        t = nst = 0
+        for k, (n0, n1) in enumerate(self.pairs):
+            ni = n1 if i else n0
+            for j in range(ni):
+                yield ("wait", self.s_full[i], t & 1)
+                self.read(f"S{i}", ("S", i, t))
+                yield ("step",)
+                self.write(f"S{i}", ("P", i, t))
+                yield ("step",)
+                if j >= 1 and self.rng.random() < 0.5:  # O_i rescaled in place: PV_i(j-1) is in
+                    self.read(f"O{i}", ("O", k, j))
+                    yield ("step",)
+                self.p_full[i].arrive()
+                t += 1
+                yield ("step",)
+            if ni:
+                yield ("wait", self.st_empty[i], (nst & 1) ^ 1)
+                self.write(f"stats{i}", k)
+                self.st_full[i].arrive()
+                nst += 1
+                yield ("step",)
+
+    def epilogue(self):
+        cp, items_i = [0, 0], [0, 0]
+        for k, (n0, n1) in enumerate(self.pairs):
+            for i, ni in enumerate((n0, n1)):
+                if ni == 0:
+                    continue
+                cp[i] += ni
+                yield ("wait", self.st_full[i], items_i[i] & 1)
+                self.read(f"stats{i}", k)
+                self.st_empty[i].arrive()
+                yield ("step",)
+                yield ("wait", self.s_free[i], (cp[i] - 1) & 1)
+                self.read(f"O{i}", ("O", k, ni))
+                self.o_empty[i].arrive()
+                items_i[i] += 1
+                yield ("step",)
+
+
+PAIR_SETS = [[(1, 1)], [(3, 3)], [(2, 0)], [(1, 2), (3, 4)], [(4, 4), (1, 0), (2, 3), (1, 1)],
+             [(5, 5), (2, 2), (1, 2), (3, 0), (2, 2)]]
+
+
+@pytest.mark.parametrize("items", PAIR_SETS)
+def test_pair_instance_protocol(items):
+    for seed in range(150):
+        PairModel(items, random.Random(seed * 104729 + len(items))).run()
+
+
+@pytest.mark.parametrize("plant", ["s_before_pv", "no_o_empty_wait", "q_empty_early"])
+def test_pair_planted_mistakes_are_caught(plant):
+    caught = 0
+    for seed in range(300):
+        try:
+            PairModel([(4, 4), (1, 2), (3, 3), (2, 0)], random.Random(seed), plant=plant).run()
+        except Hazard:
+            caught += 1
+    assert caught > 0, f"the planted mistake {plant} went unnoticed in 300 schedules"
 
 
 ITEM_SETS = [[1], [2], [3], [4, 1], [1, 3, 2], [5, 1, 1, 4], [2, 2, 2, 2, 2]]
