@@ -1,9 +1,10 @@
-"""CPU models of the synchronisation of the prefill kernel
-(lean-infer_b200/csrc/la_prefill.cu), run under many random schedules: the
-split instance (prefill_kernel<true>: items of one query tile, both softmax
-warpgroups on the tile's two key halves, S double buffered in TMEM) and the
-pair instance (prefill_kernel<false>: items of two query tiles sharing the
-K/V tiles).
+"""CPU models of the synchronisation inside the attention kernels, run under
+many random schedules: the prefill kernel's split instance
+(lean-infer_b200/csrc/la_prefill.cu, prefill_kernel<true>: items of one query
+tile, both softmax warpgroups on the tile's two key halves, S double buffered
+in TMEM) and pair instance (prefill_kernel<false>: items of two query tiles
+sharing the K/V tiles), and the decode kernel's stage ring and sub-chunk merge
+(la_decode.cu).
 
 Every actor follows the kernel's order of waits, arrivals and commits: the TMA
 producer, the MMA issuer, softmax warpgroups 0 and 1, the epilogue, plus the
@@ -19,7 +20,8 @@ bugs met while building it (the row-max exchange on one barrier and one slot
 per half, one P-ready barrier counting both halves, the epilogue waiting on
 the PV barrier's parity); for the pair instance the orderings it relies on
 (S_i(j+1) behind PV_i(j), the O-empty wait before an item's first PV, Q
-released after an item's last S).
+released after an item's last S); for decode, a merge slot rewritten before
+it was read, in both directions.
 
 The row-max decision to rescale O is data dependent in the kernel; the model
 draws it at random per warpgroup and step, which covers every case."""
@@ -453,6 +455,94 @@ def test_pair_planted_mistakes_are_caught(plant):
     for seed in range(300):
         try:
             PairModel([(4, 4), (1, 2), (3, 3), (2, 0)], random.Random(seed), plant=plant).run()
+        except Hazard:
+            caught += 1
+    assert caught > 0, f"the planted mistake {plant} went unnoticed in 300 schedules"
+
+
+class DecodeModel:
+    """The decode kernel's stage ring and sub-chunk merge
+    (lean-infer_b200/csrc/la_decode.cu, paged_decode_kernel): the producer
+    warp waits a stage's empty barrier (one arrival per consumer warp), writes
+    the stage descriptor into shared memory and starts its copies; consumer
+    warps wait the full barrier, read descriptor and tiles, release the stage;
+    at each segment end the warps of sub-chunks j > 0 leave their softmax
+    state in a merge slot (after the previous merge was read: mg_empty, one
+    arrival per kv head) and warp j = 0 of each kv head reads them once all
+    warps have written (mg_full, one arrival per warp)."""
+
+    STAGES = 3
+
+    def __init__(self, units, seg_ends, hkv, warps, rng, plant=None):
+        self.units, self.ends, self.hkv, self.warps = units, seg_ends, hkv, warps
+        self.rng, self.plant = rng, plant
+        self.full = [Bar(f"full{i}", 1) for i in range(self.STAGES)]
+        self.empty = [Bar(f"empty{i}", warps) for i in range(self.STAGES)]
+        self.mg_full, self.mg_empty = Bar("mg_full", warps), Bar("mg_empty", hkv)
+        self.mem, self.tma, self.tc = {}, [], []
+
+    read = Model.read
+    write = Model.write
+
+    def producer(self):
+        for k in range(self.units):
+            s = k % self.STAGES
+            yield ("wait", self.empty[s], ((k // self.STAGES) & 1) ^ 1)
+            self.write(f"D{s}", k)
+            self.full[s].arrive(expect_tx=1)
+            self.tma.append((f"R{s}", k, self.full[s], 1))
+            yield ("step",)
+
+    def consumer(self, w):
+        j, h = w // self.hkv, w % self.hkv
+        nsub = self.warps // self.hkv
+        seg = 0
+        for k in range(self.units):
+            s = k % self.STAGES
+            yield ("wait", self.full[s], (k // self.STAGES) & 1)
+            self.read(f"D{s}", k)
+            self.read(f"R{s}", k)
+            yield ("step",)
+            self.empty[s].arrive()
+            yield ("step",)
+            if k in self.ends and nsub > 1:
+                if not (self.plant == "no_mg_empty_wait" and j > 0):
+                    yield ("wait", self.mg_empty, (seg & 1) ^ 1)
+                self.write(f"M{w}", seg)
+                self.mg_full.arrive()
+                yield ("step",)
+                if j == 0:
+                    yield ("wait", self.mg_full, seg & 1)
+                    if self.plant == "release_before_read":
+                        self.mg_empty.arrive()
+                        yield ("step",)
+                    for jj in range(1, nsub):
+                        self.read(f"M{jj * self.hkv + h}", seg)
+                        yield ("step",)
+                    if self.plant != "release_before_read":
+                        self.mg_empty.arrive()
+                    yield ("step",)
+                seg += 1
+
+    def run(self):
+        run_schedule(self, [self.producer()] + [self.consumer(w) for w in range(self.warps)])
+
+
+@pytest.mark.parametrize("hkv,warps", [(8, 8), (4, 8), (2, 8), (1, 8)])
+def test_decode_ring_and_merge_protocol(hkv, warps):
+    for seed in range(100):
+        rng = random.Random(seed * 31 + hkv)
+        units = rng.randrange(1, 12)
+        ends = {k for k in range(units) if rng.random() < 0.4} | {units - 1}
+        DecodeModel(units, ends, hkv, warps, rng).run()
+
+
+@pytest.mark.parametrize("plant", ["no_mg_empty_wait", "release_before_read"])
+def test_decode_planted_mistakes_are_caught(plant):
+    caught = 0
+    for seed in range(300):
+        try:
+            DecodeModel(10, {1, 2, 4, 5, 7, 9}, 2, 8, random.Random(seed), plant=plant).run()
         except Hazard:
             caught += 1
     assert caught > 0, f"the planted mistake {plant} went unnoticed in 300 schedules"
