@@ -3,8 +3,9 @@ many random schedules: the prefill kernel's split instance
 (lean-infer_b200/csrc/la_prefill.cu, prefill_kernel<true>: items of one query
 tile, both softmax warpgroups on the tile's two key halves, S double buffered
 in TMEM) and pair instance (prefill_kernel<false>: items of two query tiles
-sharing the K/V tiles), and the decode kernel's stage ring and sub-chunk merge
-(la_decode.cu).
+sharing the K/V tiles), the decode kernel's stage ring and sub-chunk merge
+(la_decode.cu), and the KV-head-sharded decode's all-gather over peer memory
+(la_p2p.cu).
 
 Every actor follows the kernel's order of waits, arrivals and commits: the TMA
 producer, the MMA issuer, softmax warpgroups 0 and 1, the epilogue, plus the
@@ -546,6 +547,75 @@ def test_decode_planted_mistakes_are_caught(plant):
         except Hazard:
             caught += 1
     assert caught > 0, f"the planted mistake {plant} went unnoticed in 300 schedules"
+
+
+class GatherModel:
+    """The KV-head-sharded decode's fused all-gather
+    (lean-infer_b200/csrc/la_p2p.cu, sharding.NVLinkAllGatherDecode): in call
+    n every rank stores its heads' outputs into slot n % slots of every rank's
+    gather buffer (the decode kernels, finished and fenced before the barrier
+    kernel starts on the same stream), then publishes epoch n + 1 into every
+    rank's signal words and waits until each peer's epoch in its own words
+    has reached n + 1; the o_proj that follows reads its own slot, and only
+    after it does the rank's stream reach the next call's kernels."""
+
+    def __init__(self, world, calls, slots, rng):
+        self.world, self.calls, self.slots, self.rng = world, calls, slots, rng
+        self.sig = [[0] * world for _ in range(world)]  # sig[q][r]: last epoch rank r published to rank q
+        self.mem, self.tma, self.tc = {}, [], []
+
+    read = Model.read
+    write = Model.write
+
+    def rank(self, r):
+        for n in range(self.calls):
+            slot = n % self.slots
+            for q in range(self.world):  # this rank's heads into every rank's slot
+                self.write(f"G{q}.{slot}.{r}", n)
+                yield ("step",)
+            for q in range(self.world):  # publish epoch n + 1
+                self.sig[q][r] = n + 1
+                yield ("step",)
+            for q in range(self.world):  # wait for every peer's epoch
+                yield ("until", lambda q=q, n=n: self.sig[r][q] >= n + 1)
+            for q in range(self.world):  # o_proj reads the gathered heads
+                self.read(f"G{r}.{slot}.{q}", n)
+                yield ("step",)
+
+    def run(self, max_ticks=200000):
+        actors = [self.rank(r) for r in range(self.world)]
+        done = [False] * self.world
+        until = [None] * self.world  # condition a rank spins on
+        speed = [2.0 ** self.rng.uniform(-6, 6) for _ in range(self.world)]
+        for _ in range(max_ticks):
+            live = [r for r in range(self.world) if not done[r] and (until[r] is None or until[r]())]
+            if not live:
+                if all(done):
+                    return
+                raise Hazard("deadlock: every unfinished rank waits for an epoch")
+            r = self.rng.choices(live, weights=[speed[i] for i in live])[0]
+            try:
+                cmd = next(actors[r])
+                until[r] = cmd[1] if cmd[0] == "until" else None
+            except StopIteration:
+                done[r] = True
+        raise Hazard("schedule did not finish")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_gather_slots_protocol(world):
+    for seed in range(100):
+        GatherModel(world, 6, 2, random.Random(seed * 13 + world)).run()
+
+
+def test_gather_single_slot_is_caught():
+    caught = 0
+    for seed in range(300):
+        try:
+            GatherModel(4, 6, 1, random.Random(seed)).run()
+        except Hazard:
+            caught += 1
+    assert caught > 0, "one gather slot for consecutive calls went unnoticed in 300 schedules"
 
 
 ITEM_SETS = [[1], [2], [3], [4, 1], [1, 3, 2], [5, 1, 1, 4], [2, 2, 2, 2, 2]]
