@@ -19,20 +19,32 @@ seeded random weights, KV pool, token ids and lengths. Every step streams
                KV bytes per launch / launch duration, against the measured
                HBM copy bandwidth.
   cpu_baseline the reference's decode step in fp32 on the host cores
-               (oracle.qwen3_step), on a layer sample scaled to 28 layers.
+               (oracle.qwen3_step), all 28 layers, median of --cpu-steps.
+  secondary    (N=1) one line per other workload, each timed with CUDA events
+               after an L2 flush and checked against the fp32 oracle on
+               sampled rows (max_abs_err), beside the reference's own kernels
+               on the same GPU where they run (flash-attn 2.8.3, torch SDPA)
+               and its CPU attention path on the host cores: single-layer
+               decode B=8 and B=128, long-context decode B=32 with 256- and
+               16-token blocks, prefill of 16 packed prompts and of one
+               prompt, chunked prefill, and the whole step over 16-token
+               blocks.
+  kv_head_sharded  (N>1) the KV-head-sharded partition per layer (NCCL and
+               the fused NVLink gather), with its parity on every rank.
 
---impl reference times that CPU path alone (rank 0), with the same metric.
+--impl reference times the CPU step alone (rank 0), with the same metric and
+config.
 """
 from __future__ import annotations
 
 import argparse
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
 import threading
+import time
 from pathlib import Path
 
 import torch
@@ -61,16 +73,6 @@ def measured_peak_hbm():
         except Exception:
             pass
     return FALLBACK_HBM_GBS, "fallback"
-
-
-def profiled_traffic():
-    """DRAM bytes per launch of the decode kernel from the committed ncu
-    summary (profiles/decode_attention_b128.md), or None."""
-    p = REPO / "profiles" / "decode_attention_b128.md"
-    if not p.exists():
-        return None
-    m = re.search(r"dram_bytes_per_launch:\s*([0-9.]+)", p.read_text())
-    return float(m.group(1)) if m else None
 
 
 class ClockSampler:
@@ -133,6 +135,20 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def bench_config(world: int) -> dict:
+    """The workload description both arms print (identical for a given N)."""
+    return {"workload": WORKLOAD, "global_batch": world * B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
+            "parallelism": f"request-sharded x{world} (no collective)",
+            "l2": "inputs larger than L2 (~11.6 GB KV streamed per step)", "cuda_graph": True}
+
+
+DATA = "synthetic (seeded random weights, KV pool, ids, lengths)"
+
+
+def host_cores() -> dict:
+    return {"cores": len(os.sched_getaffinity(0)), "threads": torch.get_num_threads()}
+
+
 def synth_inputs(rank: int, seed: int = 0):
     """Seeded per-rank decode inputs: lengths, block tables, ids."""
     import __graft_entry__
@@ -153,40 +169,344 @@ def synth_inputs(rank: int, seed: int = 0):
     return ids, (L - 1).long(), bt, L.to(torch.int32)
 
 
-def cpu_reference_run(steps: int, warmup: int, sample_layers: int = 4):
-    """The reference's fp32 decode step on the host cores; returns tok/s and
-    a description of the sample."""
+def cpu_reference_run(steps: int, warmup: int):
+    """The reference's fp32 decode step, all 28 layers, on the host cores;
+    returns tok/s and a description of what was timed."""
     from oracle.qwen3_step import CpuQwen3Decode
 
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
-    m = CpuQwen3Decode(sample_layers=sample_layers)
+    m = CpuQwen3Decode()
     ids, pos, bt, ctx = synth_inputs(0)
     times = []
     for i in range(warmup + steps):
+        t0 = time.perf_counter()
         m.decode_step(ids, pos, bt, ctx)
+        dt = time.perf_counter() - t0
         if i >= warmup:
-            times.append(m.full_step_seconds())
+            times.append(dt)
     sec = statistics.median(times)
     return {
         "value": B_PER_GPU / sec,
         "unit": "tok/s",
         "cores": cores,
         "kind": "port",
-        "sample": (f"fp32 torch on {cores} host threads; B=128 rows, {sample_layers} of 28 layers per step "
-                   f"(layer time scaled x{28 / sample_layers:g}, embedding and lm_head timed once), "
-                   f"median of {steps} steps after {warmup} warm-up"),
+        "sample": (f"the whole fp32 decode step (28 layers, embedding, lm_head) for B=128 rows of the benchmark "
+                   f"workload on {cores} host threads; median of {steps} timed steps after {warmup} warm-up"),
         "ms_per_step": sec * 1e3,
+        "steps_timed": steps,
     }
+
+
+# --------------------------------------------------------------------------
+# timing and checking helpers for the per-kernel lines
+# --------------------------------------------------------------------------
+class L2Flush:
+    """Flushes the 126 MB L2 before a timed call: writes a 512 MB buffer, then
+    reads another 512 MB one, so the L2 holds clean lines of the read buffer
+    and the timed kernel pays no write-back of the flush's dirty lines."""
+
+    def __init__(self, dev):
+        self.wbuf = torch.empty(256 << 20, dtype=torch.bfloat16, device=dev)
+        self.rbuf = torch.zeros(128 << 20, dtype=torch.float32, device=dev)
+        self.sink = torch.zeros((), dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.wbuf.zero_()
+        torch.sum(self.rbuf, dtype=torch.float32, out=self.sink)
+
+
+def flushed_us(fn, flush, reps: int = 10) -> float:
+    """Median device time of one fn() call, L2 flushed before every call.
+    fn is captured in a CUDA graph; each replay is bracketed by CUDA events on
+    the current stream (the flush runs longer than the host needs to enqueue
+    the replay, so the events see no launch gap)."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    g.replay()
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(reps):
+        flush()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    t = statistics.median(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
+    del g
+    return t
+
+
+def compact_rows(q, k_cache, v_cache, block_table, seqlens, rows):
+    """CPU copies of the given rows' queries, lengths and only the pool blocks
+    they read, with their block tables renumbered into the compact pool (the
+    oracle then reads exactly what the kernel read)."""
+    rows = torch.as_tensor(rows, dtype=torch.long)
+    BS = k_cache.shape[1]
+    L = seqlens.cpu()[rows].long()
+    btr = block_table.cpu()[rows]
+    nblk = [max(1, -(-int(n) // BS)) for n in L]
+    ids = torch.cat([btr[i, :n].long() for i, n in enumerate(nblk)])
+    kc = k_cache[ids.to(k_cache.device)].cpu()
+    vc = v_cache[ids.to(v_cache.device)].cpu()
+    bt = torch.zeros(len(rows), max(nblk), dtype=torch.int32)
+    o = 0
+    for i, n in enumerate(nblk):
+        bt[i, :n] = torch.arange(o, o + n, dtype=torch.int32)
+        o += n
+    return q.cpu()[rows], kc, vc, bt, L.to(torch.int32)
+
+
+def decode_err(out, w, rows):
+    """max |out - oracle| over the given rows of a decode batch."""
+    from oracle import paged_attention as opa
+
+    q, kc, vc, bt, L = compact_rows(w.q, w.k_cache, w.v_cache, w.block_table, w.cache_seqlens, rows)
+    ref = opa.paged_decode(q, kc, vc, bt, L)
+    return float((out.cpu()[torch.as_tensor(rows)].float() - ref).abs().max())
+
+
+def cpu_decode_us(w, rows, reps: int = 3) -> float:
+    """The reference's CPU decode attention (fp32: gather the rows' keys and
+    values through the block table, one masked SDPA) timed on the host cores
+    for `rows`, in microseconds."""
+    from oracle import paged_attention as opa
+
+    q, kc, vc, bt, L = compact_rows(w.q, w.k_cache, w.v_cache, w.block_table, w.cache_seqlens, rows)
+    kc, vc = kc.float(), vc.float()
+    opa.paged_decode_padded(q, kc, vc, bt, L)
+    t = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        opa.paged_decode_padded(q, kc, vc, bt, L)
+        t.append(time.perf_counter() - t0)
+    return statistics.median(t) * 1e6
+
+
+def flash_attn_module():
+    """flash-attn 2.8.3, the reference's attention dependency, if it imports."""
+    try:
+        import flash_attn
+
+        return flash_attn
+    except Exception:
+        return None
+
+
+def secondary_metrics(pkg, dev):
+    """The metric's other components on one GPU, each with its own parity
+    check against the fp32 oracle and, where they run, the reference's GPU
+    kernels (flash-attn 2.8.3, torch SDPA) and its CPU path on the host cores.
+    Every time is the median of CUDA-event times with L2 flushed before each
+    call (CUDA graph replays)."""
+    from lean_infer_b200 import workloads as W
+    from oracle import paged_attention as opa
+
+    out = {}
+    flush = L2Flush(dev)
+    fa = flash_attn_module()
+    hbm, hbm_kind = measured_peak_hbm()
+    peak, peak_kind = measured_peak_bf16()
+    cores = host_cores()
+
+    def decode_line(w, name, workload, rows, cpu_rows, fa_ok):
+        B, _, Hq, D = w.q.shape
+        alg = w.kv_bytes + 2 * B * Hq * D * 2
+
+        def ours():
+            return pkg.flash_attn_with_kvcache(w.q, w.k_cache, w.v_cache, cache_seqlens=w.cache_seqlens,
+                                               block_table=w.block_table, causal=True, num_splits=1)
+
+        us = flushed_us(ours, flush)
+        o = ours()
+        torch.cuda.synchronize()
+        line = {"workload": workload, "us": us, "gbs": alg / (us * 1e-6) / 1e9, "peak_gbs": hbm,
+                "frac": alg / (us * 1e-6) / 1e9 / hbm, "peak_source": hbm_kind, "alg_bytes": alg,
+                "max_abs_err": decode_err(o, w, rows), "checked_rows": len(rows), "tolerance": 2e-2}
+        if fa is not None and fa_ok:
+            def theirs():
+                return fa.flash_attn_with_kvcache(w.q, w.k_cache, w.v_cache, cache_seqlens=w.cache_seqlens,
+                                                  block_table=w.block_table, causal=True, num_splits=1)
+
+            try:
+                fus = flushed_us(theirs, flush)
+                line["flash_attn_us"] = fus
+                line["flash_attn_max_abs_err"] = decode_err(theirs(), w, rows)
+                line["speedup_vs_flash_attn"] = fus / us
+            except Exception as e:  # a kernel image missing for this GPU, say
+                line["flash_attn"] = f"did not run: {type(e).__name__}: {str(e)[:120]}"
+        cpu_us = cpu_decode_us(w, cpu_rows)
+        frac_keys = float(w.cache_seqlens[torch.as_tensor(cpu_rows, device=w.cache_seqlens.device)].sum()) / \
+            float(w.cache_seqlens.sum())
+        line["cpu_reference"] = {"us": cpu_us / frac_keys, **cores,
+                                 "sample": f"fp32 gather + masked SDPA over {len(cpu_rows)} of {B} rows, "
+                                           f"scaled by the key count to all rows"}
+        out[name] = line
+
+    # C1: single-layer decode, B=8, 512x256 pool, contexts U[512,1024]
+    w = W.decode_batch(8, CTX_LO, CTX_HI, num_blocks=NUM_BLOCKS, block_size=BLOCK_SIZE, seed=11, device=dev)
+    decode_line(w, "decode_c1_b8", "B=8, contexts U[512,1024], pool 512x256, one layer", list(range(8)),
+                list(range(8)), True)
+    del w
+    # one layer of the headline step: B=128
+    w = W.decode_batch(B_PER_GPU, CTX_LO, CTX_HI, num_blocks=NUM_BLOCKS, block_size=BLOCK_SIZE, seed=1, device=dev)
+    decode_line(w, "decode_b128_layer", "B=128, contexts U[512,1024], pool 512x256, one layer",
+                list(range(0, 128, 8)), list(range(0, 128, 16)), True)
+    del w
+    # C4: long-context split-KV decode, B=32, contexts U[8192,32768], 256- and 16-token blocks
+    for bs in (256, 16):
+        w = W.decode_batch(32, 8192, 32768, num_blocks=None, block_size=bs, seed=40, device=dev)
+        L = w.cache_seqlens.cpu()
+        rows = sorted({int(L.argmin()), int(L.argmax()), int(L.argsort()[16])})
+        decode_line(w, "decode_long_b32" if bs == 256 else "decode_long_b32_bs16",
+                    f"B=32, contexts U[8192,32768], {bs}-token blocks (split-KV)", rows, rows[:2], bs % 256 == 0)
+        del w
+    torch.cuda.synchronize()
+
+    # C3: causal varlen prefill, 16 packed prompts of U[512,1024]
+    w = W.prefill_batch(16, CTX_LO, CTX_HI, seed=3, device=dev)
+    mx = int(w.lengths.max())
+    us = flushed_us(lambda: pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx,
+                                                       causal=True), flush)
+    o = pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx, causal=True)
+    qc, kc, vc, cu = w.q.cpu(), w.k.cpu(), w.v.cpu(), w.cu_seqlens.cpu()
+    t0 = time.perf_counter()
+    ref = opa.varlen_causal_prefill(qc, kc, vc, cu)
+    cpu_s = time.perf_counter() - t0
+    tf = w.causal_flops / (us * 1e-6) / 1e12
+    line = {"workload": "16 packed prompts, lengths U[512,1024], causal, 16/8 heads, D=128", "us": us, "tflops": tf,
+            "peak_tflops": peak, "frac": tf / peak, "peak_source": peak_kind, "flops": w.causal_flops,
+            "max_abs_err": float((o.float().cpu() - ref).abs().max()), "tolerance": 2e-2,
+            "cpu_reference": {"us": cpu_s * 1e6, **cores, "sample": "fp32 causal SDPA per prompt, all 16 prompts"}}
+    if fa is not None:
+        try:
+            fus = flushed_us(lambda: fa.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx,
+                                                               causal=True), flush)
+            line["flash_attn_varlen_us"] = fus
+            line["speedup_vs_flash_attn"] = fus / us
+        except Exception as e:
+            line["flash_attn"] = f"did not run: {type(e).__name__}: {str(e)[:120]}"
+    # the reference engine prefills one prompt per step with torch SDPA
+    # (model.py:56-57): the 16 prompts as 16 such calls
+    views = []
+    for s in range(16):
+        a, b = int(cu[s]), int(cu[s + 1])
+        views.append((w.q[a:b].unsqueeze(0).transpose(1, 2), w.k[a:b].unsqueeze(0).transpose(1, 2),
+                      w.v[a:b].unsqueeze(0).transpose(1, 2)))
+
+    def sdpa_all():
+        for q_, k_, v_ in views:
+            torch.nn.functional.scaled_dot_product_attention(q_, k_, v_, is_causal=True, enable_gqa=True)
+
+    sus = flushed_us(sdpa_all, flush)
+    line["torch_sdpa_per_prompt_us"] = sus
+    line["speedup_vs_torch_sdpa"] = sus / us
+    out["prefill_b16"] = line
+    del w, o, ref, views
+
+    # C3 at B=1: one prompt per call, the reference's own prefill call shape
+    # q [1, 16, L, 128] (a transposed view of the [1, L, 16, 128] projection)
+    pts = []
+    g = torch.Generator(device=dev).manual_seed(31)
+    for L in (512, 768, 1024):
+        q_ = torch.randn(1, L, 16, 128, generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
+        k_ = torch.randn(1, L, 8, 128, generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
+        v_ = torch.randn(1, L, 8, 128, generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
+
+        def ours():
+            return pkg.scaled_dot_product_attention(q_, k_, v_, is_causal=True, enable_gqa=True)
+
+        def torch_sdpa():
+            return torch.nn.functional.scaled_dot_product_attention(q_, k_, v_, is_causal=True, enable_gqa=True)
+
+        us = flushed_us(ours, flush, reps=20)
+        tus = flushed_us(torch_sdpa, flush, reps=20)
+        o = ours()
+        ref = torch.nn.functional.scaled_dot_product_attention(q_.float().cpu(), k_.float().cpu(), v_.float().cpu(),
+                                                               is_causal=True, enable_gqa=True)
+        t0 = time.perf_counter()
+        torch.nn.functional.scaled_dot_product_attention(q_.float().cpu(), k_.float().cpu(), v_.float().cpu(),
+                                                         is_causal=True, enable_gqa=True)
+        cpu_us = (time.perf_counter() - t0) * 1e6
+        flops = 2 * 16 * 128 * L * L
+        pt = {"L": L, "us": us, "tflops": flops / (us * 1e-6) / 1e12, "torch_sdpa_us": tus,
+              "speedup_vs_torch_sdpa": tus / us, "max_abs_err": float((o.float().cpu() - ref).abs().max()),
+              "cpu_reference_us": cpu_us}
+        if fa is not None:
+            try:
+                qv, kv, vv = (x.transpose(1, 2)[0] for x in (q_, k_, v_))
+                cu1 = torch.tensor([0, L], dtype=torch.int32, device=dev)
+                pt["flash_attn_varlen_us"] = flushed_us(
+                    lambda: fa.flash_attn_varlen_func(qv, kv, vv, cu1, cu1, L, L, causal=True), flush, reps=20)
+            except Exception as e:
+                pt["flash_attn"] = f"did not run: {type(e).__name__}: {str(e)[:120]}"
+        pts.append(pt)
+    out["prefill_b1"] = {"workload": "one prompt per call, q [1,16,L,128] / k,v [1,8,L,128] views of [1,L,H,128] "
+                                     "(model.py:56-57), L = 512 / 768 / 1024", "points": pts, "tolerance": 2e-2,
+                         "cpu_reference": {**cores, "sample": "fp32 causal SDPA of the same prompt"},
+                         "peak_tflops": peak, "peak_source": peak_kind}
+
+    # chunked prefill (row f1): 16 chunks of 512 over cached prefixes U[512,1536]
+    c = W.chunk_batch(16, 512, 512, 1536, seed=4, device=dev)
+
+    def chunk():
+        return pkg.flash_attn_with_kvcache(c.q, c.k_cache, c.v_cache, cache_seqlens=c.cache_seqlens,
+                                           block_table=c.block_table, causal=True)
+
+    us = flushed_us(chunk, flush)
+    o = chunk()
+    rows = [0, 7, 15]
+    qr, kc, vc, bt, L = compact_rows(c.q, c.k_cache, c.v_cache, c.block_table, c.cache_seqlens, rows)
+    n = c.q.shape[1]
+    cu = torch.arange(0, (len(rows) + 1) * n, n, dtype=torch.int32)
+    ref = opa.paged_chunk_prefill(qr.reshape(-1, *qr.shape[2:]), kc, vc, bt, L, cu)
+    err = float((o.cpu()[torch.as_tensor(rows)].reshape(-1, *o.shape[2:]).float() - ref).abs().max())
+    tf = c.causal_flops / (us * 1e-6) / 1e12
+    out["chunk_prefill_b16"] = {"workload": "16 chunks of 512 tokens over cached prefixes U[512,1536] (paged, "
+                                            "256-token blocks, bottom-right causal)",
+                                "us": us, "tflops": tf, "peak_tflops": peak, "frac": tf / peak,
+                                "peak_source": peak_kind, "flops": c.causal_flops, "max_abs_err": err,
+                                "checked_rows": rows, "tolerance": 2e-2}
+    del c
+    del flush
+    torch.cuda.synchronize()
+    pkg.check_device_errors(dev.index)
+    return out
+
+
+def relayout_pool(cache_src, bt_src, cache_dst, bt_dst, ctx):
+    """Copy every sequence's cached tokens 0..ctx-1 from one paged pool into
+    another of a different block size (block tables bt_src / bt_dst)."""
+    bs_s, bs_d = cache_src.block_size, cache_dst.block_size
+    src, dst = [], []
+    for b in range(bt_src.shape[0]):
+        t = torch.arange(int(ctx[b]))
+        src.append(bt_src[b, t // bs_s].long() * bs_s + t % bs_s)
+        dst.append(bt_dst[b, t // bs_d].long() * bs_d + t % bs_d)
+    src, dst = torch.cat(src).to(cache_src.device), torch.cat(dst).to(cache_dst.device)
+    for pool_s, pool_d in ((cache_src.k, cache_dst.k), (cache_src.v, cache_dst.v)):
+        for layer in range(pool_s.shape[0]):
+            s = pool_s[layer].view(-1, *pool_s.shape[3:])
+            d = pool_d[layer].view(-1, *pool_d.shape[3:])
+            d[dst] = s[src]
 
 
 def kv_head_sharded_layer(pkg, dist, world, rank, dev, reps, max_over_ranks):
     """The KV-head-sharded partition at `world` GPUs: 128*world requests, each
     rank holding 8/world kv heads of all of them; one 'layer' = the decode
-    kernel on the local heads + NCCL all-gather of the [B, 16/world, 128]
-    outputs into [B, 16, 128]. Times are CUDA events, max over ranks."""
+    kernel on the local heads + the all-gather of the [B, 16/world, 128]
+    outputs into [B, 16, 128], by NCCL or fused into the decode kernels over
+    NVLink. Times are CUDA events, max over ranks. Parity: on every rank the
+    fused gather must equal the NCCL gather bit for bit, and this rank's heads
+    in it must match the fp32 oracle on 16 sampled rows (max over ranks)."""
     from lean_infer_b200 import sharding as S
     from lean_infer_b200 import workloads as W
+    from oracle import paged_attention as opa
 
     sh = S.kv_head_shard(rank, world, 8, 16)
     B = B_PER_GPU * world
@@ -248,6 +568,25 @@ def kv_head_sharded_layer(pkg, dist, world, rank, dev, reps, max_over_ranks):
     t_fused_graph = graph_timed(fused_layer)
     t_attn_graph = graph_timed(attn)
     t_layer_graph = graph_timed(lambda i: dec.gather(attn(i)))  # NCCL all-gather captured too
+
+    # parity, pool 0, both forms on every rank
+    o_nccl = dec.gather(attn(0)).clone()
+    o_fused = fused_layer(0).clone()
+    torch.cuda.synchronize()
+    dist.barrier()
+    same = bool(torch.equal(o_nccl, o_fused))
+    fused_vs_nccl = float((o_nccl.float() - o_fused.float()).abs().max())
+    Lc = L.to(torch.int32)
+    rows = sorted(set(torch.randperm(B, generator=torch.Generator().manual_seed(77))[:14].tolist())
+                  | {int(Lc.argmax()), int(Lc.argmin())})
+    kc, vc = pools[0]
+    qr, kcr, vcr, btr, Lr = compact_rows(q, kc, vc, btd, seq, rows)
+    ref = opa.paged_decode(qr, kcr, vcr, btr, Lr)  # this rank's heads only
+    mine = o_fused[torch.as_tensor(rows, device=dev)][:, :, sh.q_lo:sh.q_hi].float().cpu()
+    err_fused = max_over_ranks(float((mine - ref).abs().max()))
+    mine = o_nccl[torch.as_tensor(rows, device=dev)][:, :, sh.q_lo:sh.q_hi].float().cpu()
+    err_nccl = max_over_ranks(float((mine - ref).abs().max()))
+    n_diff = max_over_ranks(0.0 if same else 1.0)
     fused.close()
     kv_total = int(L.sum()) * 8 * 128 * 2 * 2
     pkg.check_device_errors(dev.index)
@@ -259,7 +598,12 @@ def kv_head_sharded_layer(pkg, dist, world, rank, dev, reps, max_over_ranks):
             "fused_nvlink_us_per_layer": t_fused, "fused_nvlink_graph_us_per_layer": t_fused_graph,
             "allgather_bytes_per_gpu": B * sh.num_q_heads * 128 * 2,
             "kv_gbs_total": kv_total / (best * 1e-6) / 1e9,
-            "tok_per_s_attention_only": B / (best * 28 * 1e-6)}
+            "kv_gbs_per_gpu_decode": kv_total / world / (t_attn_graph * 1e-6) / 1e9,
+            "tok_per_s_attention_only": B / (best * 28 * 1e-6),
+            "parity": {"max_abs_err_fused": err_fused, "max_abs_err_nccl": err_nccl,
+                       "fused_equals_nccl_all_ranks": n_diff == 0.0, "fused_vs_nccl_max_abs": fused_vs_nccl,
+                       "checked_rows_per_rank": len(rows), "tolerance": 2e-2,
+                       "oracle": "fp32 paged decode over each rank's own kv heads"}}
 
 
 def measured_peak_bf16():
@@ -272,83 +616,65 @@ def measured_peak_bf16():
     return 1590.0, "fallback"
 
 
-def graph_time_us(fn, reps):
-    """Mean device time of fn() over `reps` graph-captured calls (CUDA events)."""
-    fn()
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        for _ in range(reps):
-            fn()
-    g.replay()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    g.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    del g
-    return e0.elapsed_time(e1) * 1e3 / reps
-
-
-def secondary_metrics(pkg, dev):
-    """The metric's other components, on one GPU: causal varlen prefill
-    TFLOP/s (16 packed prompts, lengths U[512,1024]) and long-context
-    split-KV decode GB/s (B=32, contexts U[8192,32768], 256-token blocks)."""
-    from lean_infer_b200 import workloads as W
-
-    out = {}
-    w = W.prefill_batch(16, CTX_LO, CTX_HI, seed=3, device=dev)
-    mx = int(w.lengths.max())
-    us = graph_time_us(lambda: pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx,
-                                                          causal=True), 20)
-    peak, kind = measured_peak_bf16()
-    tf = w.causal_flops / (us * 1e-6) / 1e12
-    out["prefill_b16"] = {"workload": "16 packed prompts, lengths U[512,1024], causal, 16/8 heads, D=128",
-                          "us": us, "tflops": tf, "peak_tflops": peak, "frac": tf / peak, "peak_source": kind,
-                          "flops": w.causal_flops}
-    del w
-    c = W.chunk_batch(16, 512, 512, 1536, seed=4, device=dev)
-    us = graph_time_us(lambda: pkg.flash_attn_with_kvcache(c.q, c.k_cache, c.v_cache, cache_seqlens=c.cache_seqlens,
-                                                           block_table=c.block_table, causal=True), 20)
-    tf = c.causal_flops / (us * 1e-6) / 1e12
-    out["chunk_prefill_b16"] = {"workload": "16 chunks of 512 tokens over cached prefixes U[512,1536] (paged, "
-                                            "256-token blocks, bottom-right causal)",
-                                "us": us, "tflops": tf, "peak_tflops": peak, "frac": tf / peak, "peak_source": kind,
-                                "flops": c.causal_flops}
-    del c
-    d = W.decode_batch(32, 8192, 32768, num_blocks=None, block_size=BLOCK_SIZE, seed=40, device=dev)
-    us = graph_time_us(lambda: pkg.flash_attn_with_kvcache(d.q, d.k_cache, d.v_cache, cache_seqlens=d.cache_seqlens,
-                                                           block_table=d.block_table, causal=True), 5)
-    hbm, kind = measured_peak_hbm()
-    gbs = d.kv_bytes / (us * 1e-6) / 1e9
-    out["decode_long_b32"] = {"workload": "B=32, contexts U[8192,32768], 256-token blocks (split-KV)",
-                              "us": us, "gbs": gbs, "peak_gbs": hbm, "frac": gbs / hbm, "kv_bytes": d.kv_bytes}
-    del d
-    torch.cuda.synchronize()
-    pkg.check_device_errors(dev.index)
-    return out
-
-
 def run_reference(args):
     rank = env_int("RANK", 0)
     if rank != 0:
         return
-    # K timed steps after W warm-up, each a bounded sample: fewer layers per
-    # step as K grows so the whole run stays within a few minutes
-    layers = args.sample_layers if args.steps <= 30 else (2 if args.steps <= 100 else 1)
-    r = cpu_reference_run(args.steps, args.warmup, layers)
+    r = cpu_reference_run(args.steps, args.warmup)
     out = {
         "metric": METRIC, "value": r["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
-                   "parallelism": "host cores"},
+        "vs_baseline": None, "dtype": "f32", "data": DATA,
+        "config": bench_config(args.gpus),
         "impl": "reference",
         "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": r["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out), flush=True)
+
+
+def step_bs16(pkg, model, cache, dg, ids, pos, bt, ctx, dev, steps):
+    """Row f2 end to end: the same decode step over a pool of 16-token blocks
+    (same token capacity, the same cached tokens copied into it), timed like
+    the headline; parity = its logits against the 256-token-block step's."""
+    from lean_infer_b200 import qwen3
+    from lean_infer_b200 import workloads as W
+    from lean_infer_b200.cache import BlockCache
+
+    cfg = model.config
+    nb16 = NUM_BLOCKS * BLOCK_SIZE // 16
+    cache16 = BlockCache(cfg.num_hidden_layers, nb16, 16, cfg.num_key_value_heads, cfg.head_dim, dev, zero=False)
+    bt16, _ = W.deal_blocks(ctx.long(), 16, nb16, 123)
+    relayout_pool(cache, bt, cache16, bt16, ctx)
+    dg16 = qwen3.DecodeGraph(model, cache16, B_PER_GPU, -(-CTX_HI // 16))
+    dg16.stage(ids, pos, bt16, ctx)
+    dg16.upload()
+    dg16.capture()
+    for _ in range(3):
+        dg16.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        dg16.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    # parity: one more step of each graph on identical inputs
+    dg.stage(ids, pos, bt, ctx)
+    dg.upload()
+    dg.replay()
+    dg16.replay()
+    torch.cuda.synchronize()
+    a, b = dg16.logits[:, 0].detach().float(), dg.logits[:, 0].detach().float()
+    err = float((a - b).abs().max())
+    agree = float((dg16.next_tokens == dg.next_tokens).float().mean())
+    pkg.check_device_errors(dev.index)
+    dg16.release()
+    del cache16
+    return {"workload": WORKLOAD.replace("512x256-token", "8192x16-token"), "ms_per_step": ms,
+            "tok_per_s": B_PER_GPU / (ms / 1e3), "logits_max_abs_diff_vs_bs256": err,
+            "next_token_agreement_vs_bs256": agree}
 
 
 def run_ours(args):
@@ -369,7 +695,7 @@ def run_ours(args):
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
     def barrier():
         if dist is not None:
@@ -474,15 +800,17 @@ def run_ours(args):
     achieved = alg_bytes / (us_per_launch * 1e-6) / 1e9
     peak, peak_kind = measured_peak_hbm()
     del g_attn
+
+    bs16 = None
+    if world == 1 and not args.no_secondary:
+        bs16 = step_bs16(pkg, model, cache, dg, ids, pos, bt, ctx, dev, max(3, args.steps))
     dg.release()
 
     result = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random weights, KV pool, ids, lengths)",
-        "config": {"workload": WORKLOAD, "global_batch": world * B_PER_GPU, "seq_len": f"U[{CTX_LO},{CTX_HI}]",
-                   "parallelism": f"request-sharded x{world} (no collective)",
-                   "l2": "inputs larger than L2 (~11.6 GB KV streamed per step)", "cuda_graph": True},
+        "vs_baseline": None, "dtype": "bf16", "data": DATA,
+        "config": bench_config(world),
         "e2e": {"value": world * B_PER_GPU / (e2e_ms / 1e3), "unit": "tok/s",
                 "h2d_bytes_per_step": dg.h2d_bytes, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches_per_step * args.steps,
@@ -490,18 +818,21 @@ def run_ours(args):
                      "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6650 GB/s",
-                     "traffic": profiled_traffic(), "alg_bytes_per_launch": alg_bytes,
+                     "traffic": None, "alg_bytes_per_launch": alg_bytes,
                      "us_per_launch": us_per_launch},
         "clocks": clk.summary(),
     }
-    if rank == 0:
+    del cache, model, qs
+    torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and not args.no_secondary:
         result["secondary"] = secondary_metrics(pkg, dev)
+        result["secondary"]["step_bs16"] = bs16
     if world > 1:
         dist.barrier()
         result["kv_head_sharded"] = kv_head_sharded_layer(pkg, dist, world, rank, dev, max(8, args.steps // 10),
                                                           max_over_ranks)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = cpu_reference_run(args.cpu_steps, 1, args.sample_layers)
+        r = cpu_reference_run(args.cpu_steps, 1)
         result["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
     if dist is not None:
         dist.barrier()
@@ -512,7 +843,7 @@ def run_ours(args):
 
 def run_case(args):
     """Single-kernel cases for profilers (ncu): run one op a few times on a
-    small, fixed input and exit. --case decode-b128 | decode-long |
+    small, fixed input and exit. --case decode-b128 | decode-c1 | decode-long |
     prefill-b16 | prefill-b1 | prefill-long | chunk-prefill-b16 | pre-attn-b128."""
     import __graft_entry__
 
@@ -521,9 +852,11 @@ def run_case(args):
 
     dev = torch.device("cuda", 0)
     reps = 3
-    if args.case in ("decode-b128", "decode-long"):
+    if args.case in ("decode-b128", "decode-long", "decode-c1"):
         if args.case == "decode-b128":  # one layer of the benchmark step: 408 MB of KV, > L2
             w = W.decode_batch(128, CTX_LO, CTX_HI, num_blocks=NUM_BLOCKS, block_size=BLOCK_SIZE, seed=1, device=dev)
+        elif args.case == "decode-c1":  # B=8, one layer, 512x256 pool
+            w = W.decode_batch(8, CTX_LO, CTX_HI, num_blocks=NUM_BLOCKS, block_size=BLOCK_SIZE, seed=11, device=dev)
         else:  # B=32, contexts U[8192, 32768]
             w = W.decode_batch(32, 8192, 32768, num_blocks=None, block_size=BLOCK_SIZE, seed=40, device=dev)
         for _ in range(reps):
@@ -573,9 +906,9 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--sample-layers", type=int, default=4, help="layers per CPU reference step (scaled to 28)")
-    ap.add_argument("--cpu-steps", type=int, default=2, help="timed CPU steps for cpu_baseline")
+    ap.add_argument("--cpu-steps", type=int, default=5, help="timed CPU steps for cpu_baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the per-kernel lines and the BS=16 step")
     ap.add_argument("--case", default=None, help="run one kernel case for a profiler and exit")
     args = ap.parse_args()
     if args.case:

@@ -223,7 +223,9 @@ int la_p2p_free(void* ptr);
  * that overlap on the GPU (other streams or threads) race; nothing in it must
  * start at zero. The first call on each device resolves the array's device
  * address (and loads the module there): make that first call before any
- * stream capture. */
+ * stream capture. The address is resolved again whenever the current CUDA
+ * context differs from the one it was resolved in (after a device reset, or
+ * under a caller's own non-primary context). */
 #define LA_NOALLOC_SCRATCH_BYTES (4u << 20)
 
 int la_paged_decode_noalloc(

@@ -24,6 +24,14 @@ def blocks_for(n_tokens: int, block_size: int) -> int:
     return -(-n_tokens // block_size)
 
 
+class InsufficientBlocksError(RuntimeError, AssertionError):
+    """allocate(n) with fewer than n free blocks. The reference signals this
+    with an assert (cache_manager.py:38, an AssertionError); this error is an
+    AssertionError too, so callers catching that keep working, and a
+    RuntimeError like the package's other errors. It is raised under -O as
+    well, where the reference's assert would vanish."""
+
+
 class BlockAllocator:
     """FIFO free list of physical block ids; block 0 is reserved as trash."""
 
@@ -36,7 +44,7 @@ class BlockAllocator:
 
     def allocate(self, n: int) -> list[int]:
         if n > len(self.free):
-            raise RuntimeError(f"Insufficient free blocks: asked {n}, free {len(self.free)}")
+            raise InsufficientBlocksError(f"Insufficient free blocks: asked {n}, free {len(self.free)}")
         return [self.free.popleft() for _ in range(n)]
 
     def release(self, blocks: list[int]) -> None:

@@ -81,8 +81,9 @@ struct Params {
   // row to outs[0..nouts): `out` alone, or, for the KV-head-sharded
   // all-gather, every rank's gather buffer (peer pointers over NVLink; rows
   // the decode pass finished are forwarded from `out` with coalesced 8-byte
-  // stores). With peer_stores set, each combine thread then fences at system
-  // scope, so the epoch a later barrier publishes orders after its stores.
+  // stores). With peer_stores set, each combine CTA then fences once at
+  // system scope, so the epoch a later barrier publishes orders after its
+  // stores.
   __nv_bfloat16* outs[kMaxPeers];
   int nouts;
   int peer_stores;
@@ -733,7 +734,14 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
       if (lse && lane == 0) *lse = l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
     }
   }
-  if (p.peer_stores) __threadfence_system();
+  if (p.peer_stores) {
+    // One system-scope fence per CTA: __syncwarp orders every lane's peer
+    // stores before lane 0's fence, which is cumulative over them, so the
+    // epoch the barrier kernel publishes next on this stream (a release at
+    // system scope, after this grid completes) orders after all of them.
+    __syncwarp();
+    if (lane == 0) __threadfence_system();
+  }
 }
 
 // ------------------------------------------------------------------ host

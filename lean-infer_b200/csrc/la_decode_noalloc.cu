@@ -19,6 +19,7 @@
 // streams, different threads) race on it.
 // Nothing in it has to start at zero, because every partial the combine pass
 // reads was written earlier in the same call.
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -32,18 +33,44 @@ static __device__ __align__(256) unsigned char g_scratch[LA_NOALLOC_SCRATCH_BYTE
 
 constexpr int kMaxDevices = 64;
 static std::mutex g_mutex;
-static void* g_scratch_addr[kMaxDevices];  // device address of g_scratch, per device
+// Per device: the device address of g_scratch and the context it was
+// resolved in. The address belongs to the module loaded in that context; a
+// device reset, or a caller that makes another context current, loads the
+// module again at a new address, so a changed context resolves it again.
+static void* g_scratch_addr[kMaxDevices];
+static CUcontext g_scratch_ctx[kMaxDevices];
 
-// The device address of g_scratch on the current device. In host code the
+static PFN_cuCtxGetCurrent_v4000 ctx_get_current_fn() {
+  static std::once_flag once;
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  });
+  return fn;
+}
+
+// The device address of g_scratch in the current context. In host code the
 // name g_scratch is a host-side stand-in, not a device address; the runtime
-// resolves the real address once per device (this loads the module there).
+// resolves the real address (loading the module there on first use).
 static int scratch_address(int device, void** out) {
+  auto get_ctx = ctx_get_current_fn();
+  if (!get_ctx) return LA_ERR_CUDA;
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return LA_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (g_scratch_addr[device] == nullptr) {
+  if (ctx == nullptr || g_scratch_addr[device] == nullptr || g_scratch_ctx[device] != ctx) {
+    // With no context current yet, this first runtime call makes the
+    // device's primary context current; the context is read again after it.
     void* addr = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&addr, g_scratch);
     if (e != cudaSuccess) return cuda_status(e);
+    if (get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) return LA_ERR_CUDA;
     g_scratch_addr[device] = addr;
+    g_scratch_ctx[device] = ctx;
   }
   *out = g_scratch_addr[device];
   return LA_OK;

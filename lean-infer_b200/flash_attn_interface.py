@@ -86,11 +86,24 @@ def check_device_errors(device: Optional[int] = None, clear: bool = True) -> Non
 
 
 def _workspace(device: int, nbytes: int) -> torch.Tensor:
+    """The per-device decode workspace, grown to `nbytes` if needed.
+
+    Its size depends only on head counts and the SM count, so it is created
+    by the first call and normally never grows. If it must grow, kernels
+    queued earlier (any stream) may still use the old buffer, so the device
+    is synchronised before the old tensor is dropped; growing inside a CUDA
+    graph capture is refused, since a captured graph would keep the freed
+    pointer (warm up with the largest head count before capturing)."""
     ws = _workspaces.get(device)
     if ws is None or ws.numel() < nbytes:
         with _state_lock:
             ws = _workspaces.get(device)
             if ws is None or ws.numel() < nbytes:
+                if ws is not None:
+                    if torch.cuda.is_current_stream_capturing():
+                        raise RuntimeError("the decode workspace must grow during a CUDA graph capture: call "
+                                           "once with these head counts before capturing")
+                    torch.cuda.synchronize(device)
                 ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", device))
                 _workspaces[device] = ws
     return ws

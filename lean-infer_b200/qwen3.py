@@ -207,7 +207,8 @@ def random_model(cfg: ModelConfig, device, seed: int = 0, dtype=torch.bfloat16) 
         for layer in m.layers:
             layer.self_attn.q_norm.copy_(1 + 0.1 * torch.randn(cfg.head_dim, generator=g, device=device))
             layer.self_attn.k_norm.copy_(1 + 0.1 * torch.randn(cfg.head_dim, generator=g, device=device))
-    return m.to(dtype).eval()
+    # inference only: no autograd bookkeeping in eager calls or graph captures
+    return m.to(dtype).eval().requires_grad_(False)
 
 
 def staging_views(buf: torch.Tensor, n_slots: int, max_blocks: int):

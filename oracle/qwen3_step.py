@@ -26,6 +26,55 @@ from . import paged_attention as opa
 from . import pre_attention as opre
 
 
+def seeded_weights(layers, hidden, heads, kv_heads, head_dim, inter, vocab, seed):
+    """fp32 weights drawn in a fixed order from one seeded generator, in the
+    dict form CpuQwen3Decode.from_weights takes. The golden-fixture script
+    loads the same values into the reference's own Qwen3ForCausalLM
+    (model.py:104-112), so the port and the reference run identical weights.
+    Linear weights are N(0, 1/fan_in); norm weights 1 + N(0, 0.1^2)."""
+    g = torch.Generator().manual_seed(seed)
+
+    def lin(o, i):
+        return torch.randn(o, i, generator=g) / i ** 0.5
+
+    def norm(n):
+        return 1.0 + 0.1 * torch.randn(n, generator=g)
+
+    w = {"embed": torch.randn(vocab, hidden, generator=g), "norm": norm(hidden)}
+    names = ("wq", "wk", "wv", "wo", "qn", "kn", "wg", "wu", "wd", "ln1", "ln2")
+    for k in names:
+        w[k] = []
+    for _ in range(layers):
+        w["wq"].append(lin(heads * head_dim, hidden))
+        w["wk"].append(lin(kv_heads * head_dim, hidden))
+        w["wv"].append(lin(kv_heads * head_dim, hidden))
+        w["wo"].append(lin(hidden, heads * head_dim))
+        w["qn"].append(norm(head_dim))
+        w["kn"].append(norm(head_dim))
+        w["wg"].append(lin(inter, hidden))
+        w["wu"].append(lin(inter, hidden))
+        w["wd"].append(lin(hidden, inter))
+        w["ln1"].append(norm(hidden))
+        w["ln2"].append(norm(hidden))
+    return w
+
+
+REFERENCE_NAMES = dict(wq="self_attn.q_proj", wk="self_attn.k_proj", wv="self_attn.v_proj",
+                       wo="self_attn.o_proj", qn="self_attn.q_norm", kn="self_attn.k_norm", wg="mlp.gate_proj",
+                       wu="mlp.up_proj", wd="mlp.down_proj", ln1="input_layernorm",
+                       ln2="post_attention_layernorm")
+
+
+def reference_state_dict(w: dict) -> dict:
+    """The weights of seeded_weights() under the parameter names of the
+    reference's Qwen3ForCausalLM (the checkpoint names at model.py:10-22)."""
+    sd = {"model.embed_tokens.weight": w["embed"], "model.norm.weight": w["norm"]}
+    for i in range(len(w["wq"])):
+        for k, n in REFERENCE_NAMES.items():
+            sd[f"model.layers.{i}.{n}.weight"] = w[k][i]
+    return sd
+
+
 class CpuQwen3Decode:
     def __init__(self, num_layers=28, hidden=1024, heads=16, kv_heads=8, head_dim=128, inter=3072, vocab=151936,
                  eps=1e-6, theta=1e6, num_blocks=512, block_size=256, seed=0, sample_layers=None):

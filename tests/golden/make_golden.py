@@ -1,6 +1,6 @@
 """Generate golden fixtures by running the reference's own code on the CPU.
 
-Usage: python tests/golden/make_golden.py [/path/to/lean-infer]   (default /root/reference)
+Usage: python tests/golden/make_golden.py /path/to/lean-infer-checkout
 
 Imports leaninfer.qwen3.model / layers / model_config and
 leaninfer.engine.cache_manager / engine_config from the reference checkout
@@ -19,6 +19,15 @@ tensors at the boundaries the kernels replace:
                              enable_gqa=True) and its output (model.py:56-57).
   rope.npz                   build_rope(...) cos/sin in bf16 at positions up to
                              40000 (layers.py:7-15).
+  model_step.npz             the whole Qwen3ForCausalLM (model.py:87-112) in
+                             fp32, 2 layers of Qwen3-0.6B shapes (vocab cut to
+                             2048), weights from oracle.qwen3_step.seeded_weights:
+                             two prompts prefilled one at a time through its
+                             SDPA path, then one decode step of both rows with
+                             its flash-attn call (CUDA only) answered by the
+                             oracle's paged decode. Saved: prefill logits of
+                             each prompt's last 3 tokens, the decode logits, and
+                             K/V pool rows of both layers at sampled positions.
 """
 from __future__ import annotations
 
@@ -29,8 +38,11 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+if len(sys.argv) < 2:
+    sys.exit("usage: make_golden.py /path/to/lean-infer-checkout")
+REF = Path(sys.argv[1])
 sys.path.insert(0, str(REF))
+sys.path.insert(0, str(HERE.parent.parent))  # the oracle package (seeded weights, paged decode)
 
 from leaninfer.engine import cache_manager, engine_config  # noqa: E402
 from leaninfer.qwen3 import layers, model  # noqa: E402
@@ -151,6 +163,73 @@ def rope_fixture(name):
     print(name, cos.shape)
 
 
+MODEL_CFG = dict(layers=2, hidden=1024, heads=16, kv_heads=8, head_dim=128, inter=3072, vocab=2048, eps=1e-6,
+                 theta=1e6, seed=21, num_blocks=8, block_size=256, prompts=(300, 77))
+
+
+def model_fixture(name):
+    from oracle import paged_attention as opa
+    from oracle.qwen3_step import reference_state_dict, seeded_weights
+
+    c = MODEL_CFG
+    cfg = ModelConfig(num_hidden_layers=c["layers"], hidden_size=c["hidden"], num_attention_heads=c["heads"],
+                      num_key_value_heads=c["kv_heads"], head_dim=c["head_dim"], intermediate_size=c["inter"],
+                      vocab_size=c["vocab"], rms_norm_eps=c["eps"], rope_theta=c["theta"])
+    w = seeded_weights(c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"], c["vocab"],
+                       c["seed"])
+    m = model.Qwen3ForCausalLM(cfg).float()
+    m.load_state_dict(reference_state_dict(w), strict=True)
+    ecfg = engine_config.EngineConfig(num_blocks=c["num_blocks"], block_size=c["block_size"],
+                                      device=torch.device("cpu"), dtype=torch.float32)
+    cache = cache_manager.BlockCache(cfg, ecfg)
+    alloc = cache_manager.BlockAllocator(c["num_blocks"])
+    g = torch.Generator().manual_seed(c["seed"] + 1)
+    lens = list(c["prompts"])
+    tables = [alloc.allocate(-(-(L + 1) // c["block_size"])) for L in lens]
+    bt = torch.zeros(len(lens), max(len(t) for t in tables), dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    prompts = [torch.randint(0, c["vocab"], (L,), generator=g) for L in lens]
+    out = {"block_table": bt.numpy(), "lens": np.array(lens)}
+    for i, p in enumerate(prompts):
+        out[f"prompt{i}"] = p.numpy()
+    orig_fa = model.flash_attn_with_kvcache
+
+    def fa_stub(q, k_cache, v_cache, cache_seqlens=None, block_table=None, **kw):
+        return opa.paged_decode(q, k_cache, v_cache, block_table, cache_seqlens).to(q.dtype)
+
+    try:
+        model.flash_attn_with_kvcache = fa_stub
+        with torch.no_grad():
+            nxt = []
+            for i, p in enumerate(prompts):  # the engine prefills one prompt per step (B=1)
+                lg = m(p.view(1, -1), cache, bt[i:i + 1], torch.zeros(1, dtype=torch.long), None)[0]
+                out[f"prefill_logits{i}"] = lg[-3:].numpy()
+                nxt.append(int(lg[-1].argmax()))
+            ids = torch.tensor(nxt).view(-1, 1)
+            pos = torch.tensor(lens, dtype=torch.long)
+            lg = m(ids, cache, bt, pos, (pos + 1).to(torch.int32))
+            out["decode_ids"] = ids.numpy()
+            out["decode_logits"] = lg[:, 0].numpy()
+    finally:
+        model.flash_attn_with_kvcache = orig_fa
+    # pool rows (both layers, K and V) at sampled positions of each sequence
+    sample = []
+    for i, L in enumerate(lens):
+        for t in (0, L // 2, L - 1, L):  # L: the token the decode step wrote
+            sample.append((i, t))
+    out["pool_positions"] = np.array(sample)
+    ks, vs = [], []
+    for i, t in sample:
+        blk, off = int(bt[i, t // c["block_size"]]), t % c["block_size"]
+        ks.append(cache.k[:, blk, off].numpy())
+        vs.append(cache.v[:, blk, off].numpy())
+    out["pool_k"] = np.stack(ks)
+    out["pool_v"] = np.stack(vs)
+    np.savez_compressed(HERE / name, **out)
+    print(name, {k: v.shape for k, v in out.items()})
+
+
 if __name__ == "__main__":
     pre_attention_fixture("pre_attention_decode.npz", B=4, q_len=1,
                           pos=torch.tensor([0, 255, 256, 700], dtype=torch.long), num_blocks=8, block_size=256,
@@ -159,3 +238,4 @@ if __name__ == "__main__":
                           num_blocks=4, block_size=16, seed=12, decode=False)
     attention_fixture("attention_prefill.npz", L=80, seed=13)
     rope_fixture("rope.npz")
+    model_fixture("model_step.npz")

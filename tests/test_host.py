@@ -42,3 +42,29 @@ def test_staging_views_rejects_wrong_size(pkg):
 
     with pytest.raises(AssertionError):
         qwen3.staging_views(torch.zeros(qwen3.staging_bytes(4, 2) + 8, dtype=torch.uint8), 4, 2)
+
+
+def test_block_allocator_fifo_and_trash_block(pkg):
+    """The package's BlockAllocator against the reference's behaviour
+    (cache_manager.py:13-42): ids 1..NB-1 in FIFO order, block 0 never handed
+    out, released blocks appended at the tail, over-allocation refused with
+    an AssertionError (the reference's assert) without taking any block."""
+    from lean_infer_b200.cache import BlockAllocator, InsufficientBlocksError, blocks_for
+
+    a = BlockAllocator(8)
+    assert a.num_free == 7
+    assert a.allocate(3) == [1, 2, 3]
+    assert a.allocate(0) == []
+    a.release([2, 1])
+    assert a.allocate(4) == [4, 5, 6, 7]
+    assert a.num_free == 2
+    with pytest.raises(AssertionError):
+        a.allocate(3)
+    with pytest.raises(InsufficientBlocksError):
+        a.allocate(3)
+    assert a.num_free == 2
+    assert a.allocate(2) == [2, 1]
+    assert a.num_free == 0
+    a.release([3])
+    assert a.allocate(1) == [3]
+    assert [blocks_for(n, 256) for n in (0, 1, 256, 257, 1024)] == [0, 1, 1, 2, 4]

@@ -46,14 +46,16 @@ def _weights(model):
     return w
 
 
-def test_prefill_then_graph_decode_matches_reference_model(pkg, cuda_dev):
+@pytest.mark.parametrize("NB,BS", [(24, 256), (64, 16)])
+def test_prefill_then_graph_decode_matches_reference_model(pkg, cuda_dev, NB, BS):
+    """256-token blocks (the engine's) and 16-token blocks (row f2: the
+    kernels lift flash-attn's 256 minimum), same prompts and weights."""
     from lean_infer_b200 import qwen3
     from lean_infer_b200.cache import BlockAllocator, BlockCache
     from oracle.qwen3_step import CpuQwen3Decode
 
     cfg = qwen3.ModelConfig(num_hidden_layers=2, vocab_size=4096)
     model = qwen3.random_model(cfg, cuda_dev, seed=5)
-    NB, BS = 24, 256
     cache = BlockCache(cfg.num_hidden_layers, NB, BS, 8, 128, cuda_dev)
     ref = CpuQwen3Decode.from_weights(_weights(model), dict(layers=2, hidden=1024, heads=16, kv_heads=8,
                                                             head_dim=128, eps=1e-6, theta=1e6), NB, BS)

@@ -197,3 +197,37 @@ def test_chunk_prefill_oracle_rows_without_keys():
                                        return_lse=True)
     assert torch.count_nonzero(out[:2]) == 0 and torch.isinf(lse[:2]).all()
     assert torch.isfinite(out[2:]).all() and torch.count_nonzero(out[2]) > 0
+
+
+def test_full_step_port_matches_reference_model():
+    """oracle/qwen3_step.py (the CPU baseline and the model tests' oracle)
+    against the reference's own Qwen3ForCausalLM on the same seeded fp32
+    weights (tests/golden/model_step.npz): two prompts prefilled one at a
+    time, then one decode step of both rows. Both sides are fp32 on the CPU
+    and differ only in summation order, so the bound is tight: 1e-4 relative
+    to the largest logit, identical argmax, and the pool rows the same to 1e-5."""
+    from oracle.qwen3_step import CpuQwen3Decode, seeded_weights
+
+    g = _load("model_step.npz")
+    c = dict(layers=2, hidden=1024, heads=16, kv_heads=8, head_dim=128, inter=3072, vocab=2048, eps=1e-6, theta=1e6)
+    w = seeded_weights(c["layers"], c["hidden"], c["heads"], c["kv_heads"], c["head_dim"], c["inter"], c["vocab"], 21)
+    port = CpuQwen3Decode.from_weights(w, c, 8, 256)
+    bt = torch.from_numpy(g["block_table"]).int()
+    lens = [int(x) for x in g["lens"]]
+    for i, L in enumerate(lens):
+        ids = torch.from_numpy(g[f"prompt{i}"]).long().view(1, L)
+        lg = port.forward(ids, torch.zeros(1, dtype=torch.long), bt[i:i + 1], None)[0, -3:]
+        want = torch.from_numpy(g[f"prefill_logits{i}"])
+        assert (lg - want).abs().max().item() <= 1e-4 * want.abs().max().item()
+        assert torch.equal(lg.argmax(-1), want.argmax(-1))
+    ids = torch.from_numpy(g["decode_ids"]).long()
+    pos = torch.tensor(lens, dtype=torch.long)
+    lg = port.forward(ids, pos, bt, (pos + 1).to(torch.int32))[:, 0]
+    want = torch.from_numpy(g["decode_logits"])
+    assert (lg - want).abs().max().item() <= 1e-4 * want.abs().max().item()
+    assert torch.equal(lg.argmax(-1), want.argmax(-1))
+    for j, (i, t) in enumerate(g["pool_positions"]):
+        blk, off = int(bt[i, t // 256]), int(t % 256)
+        for layer in range(2):
+            assert (port.k_pools[layer, blk, off] - torch.from_numpy(g["pool_k"][j, layer])).abs().max() <= 1e-5
+            assert (port.v_pools[layer, blk, off] - torch.from_numpy(g["pool_v"][j, layer])).abs().max() <= 1e-5

@@ -134,3 +134,45 @@ def test_kv_head_sharded_decode_nvlink_allgather(pkg):
         w = W.decode_batch(40 + call, 1, 3000, num_blocks=None, seed=seed)
         ref = opa.paged_decode(w.q, w.k_cache, w.v_cache, w.block_table, w.cache_seqlens)
         assert (outs[call].float() - ref).abs().max().item() <= TOL, call
+
+
+def _barrier_call(lib, bufs, world, rank, err, dev):
+    import ctypes
+
+    sig = (ctypes.c_void_p * world)(*[b.data_ptr() for b in bufs])
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    return lib.la_p2p_barrier(sig, world, rank, ctypes.c_void_p(err.data_ptr()), stream)
+
+
+def test_p2p_barrier_reports_a_peer_that_never_arrives(pkg, cuda_dev):
+    """Rank 0 of a 2-rank gather waits for an epoch that nothing publishes
+    (the peer skipped its barrier): the bounded wait runs out, the kernel
+    returns with LA_DEVERR_WAIT_TIMEOUT in the error word, the host raises on
+    check_device_errors, and the context stays usable. One GPU: both ranks'
+    signal words are plain buffers on this device and nothing runs as rank 1."""
+    import time
+
+    from lean_infer_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.la_init(cuda_dev.index) == 0
+    bufs = [torch.zeros(64, dtype=torch.int32, device=cuda_dev) for _ in range(2)]
+    err = pkg.error_word(cuda_dev.index)
+    pkg.check_device_errors(cuda_dev.index)  # start from a clear word
+    t0 = time.perf_counter()
+    assert _barrier_call(lib, bufs, 2, 0, err, cuda_dev) == 0
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert int(err.item()) == 1  # LA_DEVERR_WAIT_TIMEOUT
+    with pytest.raises(_lib.LeanAttnError, match="bounded wait timed out"):
+        pkg.check_device_errors(cuda_dev.index)
+    assert waited >= 1.0  # it waited for its bound, it did not return early
+    # rank 0 published epoch 1 into both ranks' words
+    assert int(bufs[0][0].item()) == 1 and int(bufs[1][0].item()) == 1 and int(bufs[0][2].item()) == 1
+    # the peer now publishes its epoch 1 (as its own barrier would): the next
+    # wait of rank 0 is for epoch 2, so publish that too and the call passes
+    bufs[0][1] = 2
+    assert _barrier_call(lib, bufs, 2, 0, err, cuda_dev) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    pkg.check_device_errors(cuda_dev.index)
