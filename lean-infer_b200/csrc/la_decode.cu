@@ -639,10 +639,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------------ combine
 // Grid (batch, Hq), one warp per (sequence, query head); lane l owns dims
 // 4l..4l+3. Sequences whose key range lies inside one CTA's range were
-// written directly by the decode kernel and are skipped. The
-// others merge their partials in slot order with an online (max, sum) merge;
-// slots are fetched 8 at a time so their loads overlap.
+// written directly by the decode kernel and are skipped. The others merge
+// their partials: up to 32 slots per round, one per lane (each lane finds
+// its CTA's slot with its own two divisions and loads that slot's lse, so a
+// round costs one division latency whatever the slot count); the round's
+// max and weight sum are warp reductions, then the O rows are read 8 at a
+// time with independent loads.
 constexpr int kCombineBatch = 8;
+
+__device__ __forceinline__ float warp_max_all(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum_all(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
 
 __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p, int grid) {
   const int b = blockIdx.x;
@@ -689,40 +703,55 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
     } else {
       float m = NEG_INF, l = 0.f;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      long long c = cf;
-      while (true) {
-        long long slots[kCombineBatch];
-        int n = 0;
-        while (n < kCombineBatch && c <= cl) {
+      for (long long c0 = cf; c0 <= cl; c0 += 32) {
+        const long long c = c0 + lane;
+        int slot = -1;
+        float ls = NEG_INF;
+        if (c <= cl) {
           const long long s0 = cta_start(c, T, Gl);
-          if (s0 == cta_start(c + 1, T, Gl)) {  // empty range (T < G): wrote nothing
-            ++c;
-            continue;
-          }
-          slots[n++] = 2 * c + (s0 >= Pb ? 0 : 1);
-          ++c;
-        }
-        if (n == 0) break;
-        float ls[kCombineBatch];
-        float4 ov[kCombineBatch];
-#pragma unroll
-        for (int u = 0; u < kCombineBatch; ++u) {
-          if (u < n) {
-            ls[u] = p.part_lse[slots[u] * p.hq + hh];
-            ov[u] = *reinterpret_cast<const float4*>(p.part_o + (slots[u] * p.hq + hh) * kD + lane * 4);
+          if (s0 != cta_start(c + 1, T, Gl)) {  // an empty range (T < G) wrote nothing
+            slot = 2 * static_cast<int>(c) + (s0 >= Pb ? 0 : 1);
+            ls = p.part_lse[static_cast<long long>(slot) * p.hq + hh];
           }
         }
+        const float mr = warp_max_all(ls);
+        if (mr == NEG_INF) continue;  // warp-uniform: no keys in this round
+        const float mn = fmaxf(m, mr);
+        const float a = ex2(m - mn);  // 0 while m is -inf
+        const bool use = slot >= 0 && ls != NEG_INF;
+        const float wl = use ? ex2(ls - mn) : 0.f;
+        l = l * a + warp_sum_all(wl);
 #pragma unroll
-        for (int u = 0; u < kCombineBatch; ++u) {
-          if (u < n && ls[u] != NEG_INF) {
-            const float mn = fmaxf(m, ls[u]);
-            const float a = ex2(m - mn), w = ex2(ls[u] - mn);
-            acc[0] = acc[0] * a + w * ov[u].x;
-            acc[1] = acc[1] * a + w * ov[u].y;
-            acc[2] = acc[2] * a + w * ov[u].z;
-            acc[3] = acc[3] * a + w * ov[u].w;
-            l = l * a + w;
-            m = mn;
+        for (int k = 0; k < 4; ++k) acc[k] *= a;
+        m = mn;
+        unsigned todo = __ballot_sync(0xffffffffu, use);
+        while (todo) {
+          int su[kCombineBatch];
+          float wu[kCombineBatch];
+#pragma unroll
+          for (int k = 0; k < kCombineBatch; ++k) {
+            const int u = todo ? __ffs(todo) - 1 : 0;
+            const bool have = todo != 0;
+            todo &= todo - 1u;
+            const int sv = __shfl_sync(0xffffffffu, slot, u);
+            const float wv = __shfl_sync(0xffffffffu, wl, u);
+            su[k] = have ? sv : -1;
+            wu[k] = have ? wv : 0.f;
+          }
+          float4 ov[kCombineBatch];
+#pragma unroll
+          for (int k = 0; k < kCombineBatch; ++k)
+            ov[k] = su[k] >= 0 ? *reinterpret_cast<const float4*>(
+                                     p.part_o + (static_cast<long long>(su[k]) * p.hq + hh) * kD + lane * 4)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int k = 0; k < kCombineBatch; ++k) {
+            if (su[k] >= 0) {
+              acc[0] += wu[k] * ov[k].x;
+              acc[1] += wu[k] * ov[k].y;
+              acc[2] += wu[k] * ov[k].z;
+              acc[3] += wu[k] * ov[k].w;
+            }
           }
         }
       }

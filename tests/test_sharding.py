@@ -57,6 +57,9 @@ def _worker(rank, world, port, q, k_cache, v_cache, bt, seqlens, out_q):
         out = dec(q[:, :, sh.q_lo:sh.q_hi].contiguous(), kc, vc, seqlens, bt)
         if rank == 0:
             out_q.put(out)
+        # rank 0 hosts the rendezvous store: no rank may still be talking to
+        # it when rank 0 tears its process group down
+        dist.barrier()
     finally:
         dist.destroy_process_group()
 
