@@ -21,7 +21,8 @@ seeded random weights, KV pool, token ids and lengths. Every step streams
   cpu_baseline the reference's decode step in fp32 on the host cores
                (oracle.qwen3_step), all 28 layers, median of --cpu-steps.
   secondary    (N=1) one line per other workload, each timed with CUDA events
-               after an L2 flush and checked against the fp32 oracle on
+               over input sets larger than the L2 together (CUDA graph,
+               back to back) and checked against the fp32 oracle on
                sampled rows (max_abs_err), beside the reference's own kernels
                on the same GPU where they run (flash-attn 2.8.3, torch SDPA)
                and its CPU attention path on the host cores: single-layer
@@ -201,45 +202,39 @@ def cpu_reference_run(steps: int, warmup: int):
 # --------------------------------------------------------------------------
 # timing and checking helpers for the per-kernel lines
 # --------------------------------------------------------------------------
-class L2Flush:
-    """Flushes the 126 MB L2 before a timed call: writes a 512 MB buffer, then
-    reads another 512 MB one, so the L2 holds clean lines of the read buffer
-    and the timed kernel pays no write-back of the flush's dirty lines."""
-
-    def __init__(self, dev):
-        self.wbuf = torch.empty(256 << 20, dtype=torch.bfloat16, device=dev)
-        self.rbuf = torch.zeros(128 << 20, dtype=torch.float32, device=dev)
-        self.sink = torch.zeros((), dtype=torch.float32, device=dev)
-
-    def __call__(self):
-        self.wbuf.zero_()
-        torch.sum(self.rbuf, dtype=torch.float32, out=self.sink)
+L2_BYTES = 126 << 20
 
 
-def flushed_us(fn, flush, reps: int = 10) -> float:
-    """Median device time of one fn() call, L2 flushed before every call.
-    fn is captured in a CUDA graph; each replay is bracketed by CUDA events on
-    the current stream (the flush runs longer than the host needs to enqueue
-    the replay, so the events see no launch gap)."""
-    fn()
+def rotating_us(fns, reps: int = 5) -> float:
+    """Mean device time of one call when calls over distinct input sets run
+    back to back: every fn in `fns` works on its own inputs, chosen so that
+    all of them together exceed the 126 MB L2 (a call never finds its inputs
+    left in L2 by the previous one, as in the 28-layer decode step). The
+    calls are captured in one CUDA graph; CUDA events bracket `reps` replays
+    on the current stream."""
+    for f in fns:
+        f()
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        fn()
+        for f in fns:
+            f()
     g.replay()
     torch.cuda.synchronize()
-    evs = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
     for _ in range(reps):
-        flush()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
         g.replay()
-        e1.record()
-        evs.append((e0, e1))
+    e1.record()
     torch.cuda.synchronize()
-    t = statistics.median(e0.elapsed_time(e1) * 1e3 for e0, e1 in evs)
+    t = e0.elapsed_time(e1) * 1e3 / (reps * len(fns))
     del g
     return t
+
+
+def sets_for(bytes_per_set: int, minimum: int = 1) -> int:
+    """Input sets whose total exceeds the L2 (at least `minimum`)."""
+    return max(minimum, L2_BYTES // max(bytes_per_set, 1) + 1)
 
 
 def compact_rows(q, k_cache, v_cache, block_table, seqlens, rows):
@@ -302,41 +297,44 @@ def secondary_metrics(pkg, dev):
     """The metric's other components on one GPU, each with its own parity
     check against the fp32 oracle and, where they run, the reference's GPU
     kernels (flash-attn 2.8.3, torch SDPA) and its CPU path on the host cores.
-    Every time is the median of CUDA-event times with L2 flushed before each
-    call (CUDA graph replays)."""
+    Every time is a CUDA-graph mean over input sets that together exceed the
+    L2 (rotating_us), the same for every implementation compared."""
     from lean_infer_b200 import workloads as W
     from oracle import paged_attention as opa
 
     out = {}
-    flush = L2Flush(dev)
     fa = flash_attn_module()
     hbm, hbm_kind = measured_peak_hbm()
     peak, peak_kind = measured_peak_bf16()
     cores = host_cores()
+    torch.set_num_threads(cores["cores"])
+    cores = host_cores()
 
-    def decode_line(w, name, workload, rows, cpu_rows, fa_ok):
+    def decode_line(ws, name, workload, rows, cpu_rows, fa_ok):
+        w = ws[0]
         B, _, Hq, D = w.q.shape
         alg = w.kv_bytes + 2 * B * Hq * D * 2
 
-        def ours():
-            return pkg.flash_attn_with_kvcache(w.q, w.k_cache, w.v_cache, cache_seqlens=w.cache_seqlens,
-                                               block_table=w.block_table, causal=True, num_splits=1)
+        def ours(x):
+            return pkg.flash_attn_with_kvcache(x.q, x.k_cache, x.v_cache, cache_seqlens=x.cache_seqlens,
+                                               block_table=x.block_table, causal=True, num_splits=1)
 
-        us = flushed_us(ours, flush)
-        o = ours()
+        us = rotating_us([lambda x=x: ours(x) for x in ws])
+        o = ours(w)
         torch.cuda.synchronize()
         line = {"workload": workload, "us": us, "gbs": alg / (us * 1e-6) / 1e9, "peak_gbs": hbm,
                 "frac": alg / (us * 1e-6) / 1e9 / hbm, "peak_source": hbm_kind, "alg_bytes": alg,
-                "max_abs_err": decode_err(o, w, rows), "checked_rows": len(rows), "tolerance": 2e-2}
+                "input_sets": len(ws), "max_abs_err": decode_err(o, w, rows), "checked_rows": len(rows),
+                "tolerance": 2e-2}
         if fa is not None and fa_ok:
-            def theirs():
-                return fa.flash_attn_with_kvcache(w.q, w.k_cache, w.v_cache, cache_seqlens=w.cache_seqlens,
-                                                  block_table=w.block_table, causal=True, num_splits=1)
+            def theirs(x):
+                return fa.flash_attn_with_kvcache(x.q, x.k_cache, x.v_cache, cache_seqlens=x.cache_seqlens,
+                                                  block_table=x.block_table, causal=True, num_splits=1)
 
             try:
-                fus = flushed_us(theirs, flush)
+                fus = rotating_us([lambda x=x: theirs(x) for x in ws])
                 line["flash_attn_us"] = fus
-                line["flash_attn_max_abs_err"] = decode_err(theirs(), w, rows)
+                line["flash_attn_max_abs_err"] = decode_err(theirs(w), w, rows)
                 line["speedup_vs_flash_attn"] = fus / us
             except Exception as e:  # a kernel image missing for this GPU, say
                 line["flash_attn"] = f"did not run: {type(e).__name__}: {str(e)[:120]}"
@@ -349,44 +347,55 @@ def secondary_metrics(pkg, dev):
         out[name] = line
 
     # C1: single-layer decode, B=8, 512x256 pool, contexts U[512,1024]
-    w = W.decode_batch(8, CTX_LO, CTX_HI, num_blocks=NUM_BLOCKS, block_size=BLOCK_SIZE, seed=11, device=dev)
-    decode_line(w, "decode_c1_b8", "B=8, contexts U[512,1024], pool 512x256, one layer", list(range(8)),
+    ws = [W.decode_batch(8, CTX_LO, CTX_HI, num_blocks=NUM_BLOCKS, block_size=BLOCK_SIZE, seed=11 + i, device=dev)
+          for i in range(sets_for(8 * 768 * 4096))]
+    decode_line(ws, "decode_c1_b8", "B=8, contexts U[512,1024], pool 512x256, one layer", list(range(8)),
                 list(range(8)), True)
-    del w
+    del ws
     # one layer of the headline step: B=128
-    w = W.decode_batch(B_PER_GPU, CTX_LO, CTX_HI, num_blocks=NUM_BLOCKS, block_size=BLOCK_SIZE, seed=1, device=dev)
-    decode_line(w, "decode_b128_layer", "B=128, contexts U[512,1024], pool 512x256, one layer",
+    ws = [W.decode_batch(B_PER_GPU, CTX_LO, CTX_HI, num_blocks=NUM_BLOCKS, block_size=BLOCK_SIZE, seed=1 + i,
+                         device=dev) for i in range(2)]
+    decode_line(ws, "decode_b128_layer", "B=128, contexts U[512,1024], pool 512x256, one layer",
                 list(range(0, 128, 8)), list(range(0, 128, 16)), True)
-    del w
+    del ws
     # C4: long-context split-KV decode, B=32, contexts U[8192,32768], 256- and 16-token blocks
     for bs in (256, 16):
         w = W.decode_batch(32, 8192, 32768, num_blocks=None, block_size=bs, seed=40, device=dev)
         L = w.cache_seqlens.cpu()
         rows = sorted({int(L.argmin()), int(L.argmax()), int(L.argsort()[16])})
-        decode_line(w, "decode_long_b32" if bs == 256 else "decode_long_b32_bs16",
+        decode_line([w], "decode_long_b32" if bs == 256 else "decode_long_b32_bs16",
                     f"B=32, contexts U[8192,32768], {bs}-token blocks (split-KV)", rows, rows[:2], bs % 256 == 0)
         del w
     torch.cuda.synchronize()
 
     # C3: causal varlen prefill, 16 packed prompts of U[512,1024]
-    w = W.prefill_batch(16, CTX_LO, CTX_HI, seed=3, device=dev)
-    mx = int(w.lengths.max())
-    us = flushed_us(lambda: pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx,
-                                                       causal=True), flush)
-    o = pkg.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx, causal=True)
+    ws = [W.prefill_batch(16, CTX_LO, CTX_HI, seed=3 + 100 * i, device=dev) for i in range(3)]
+    w = ws[0]
+
+    def ours_p(x):
+        mx = int(x.lengths.max())
+        return pkg.flash_attn_varlen_func(x.q, x.k, x.v, x.cu_seqlens, x.cu_seqlens, mx, mx, causal=True)
+
+    us = rotating_us([lambda x=x: ours_p(x) for x in ws])
+    flops = sum(x.causal_flops for x in ws) / len(ws)
+    o = ours_p(w)
     qc, kc, vc, cu = w.q.cpu(), w.k.cpu(), w.v.cpu(), w.cu_seqlens.cpu()
     t0 = time.perf_counter()
     ref = opa.varlen_causal_prefill(qc, kc, vc, cu)
     cpu_s = time.perf_counter() - t0
-    tf = w.causal_flops / (us * 1e-6) / 1e12
+    tf = flops / (us * 1e-6) / 1e12
     line = {"workload": "16 packed prompts, lengths U[512,1024], causal, 16/8 heads, D=128", "us": us, "tflops": tf,
-            "peak_tflops": peak, "frac": tf / peak, "peak_source": peak_kind, "flops": w.causal_flops,
-            "max_abs_err": float((o.float().cpu() - ref).abs().max()), "tolerance": 2e-2,
-            "cpu_reference": {"us": cpu_s * 1e6, **cores, "sample": "fp32 causal SDPA per prompt, all 16 prompts"}}
+            "peak_tflops": peak, "frac": tf / peak, "peak_source": peak_kind, "flops": flops,
+            "input_sets": len(ws), "max_abs_err": float((o.float().cpu() - ref).abs().max()), "tolerance": 2e-2,
+            "cpu_reference": {"us": cpu_s * 1e6 * flops / w.causal_flops, **cores,
+                              "sample": "fp32 causal SDPA per prompt, all 16 prompts of one set"}}
     if fa is not None:
+        def theirs_p(x):
+            mx = int(x.lengths.max())
+            return fa.flash_attn_varlen_func(x.q, x.k, x.v, x.cu_seqlens, x.cu_seqlens, mx, mx, causal=True)
+
         try:
-            fus = flushed_us(lambda: fa.flash_attn_varlen_func(w.q, w.k, w.v, w.cu_seqlens, w.cu_seqlens, mx, mx,
-                                                               causal=True), flush)
+            fus = rotating_us([lambda x=x: theirs_p(x) for x in ws])
             line["flash_attn_varlen_us"] = fus
             line["speedup_vs_flash_attn"] = fus / us
         except Exception as e:
@@ -394,86 +403,94 @@ def secondary_metrics(pkg, dev):
     # the reference engine prefills one prompt per step with torch SDPA
     # (model.py:56-57): the 16 prompts as 16 such calls
     views = []
-    for s in range(16):
-        a, b = int(cu[s]), int(cu[s + 1])
-        views.append((w.q[a:b].unsqueeze(0).transpose(1, 2), w.k[a:b].unsqueeze(0).transpose(1, 2),
-                      w.v[a:b].unsqueeze(0).transpose(1, 2)))
+    for x in ws:
+        cux = x.cu_seqlens.cpu()
+        vx = []
+        for s_ in range(16):
+            a, b = int(cux[s_]), int(cux[s_ + 1])
+            vx.append((x.q[a:b].unsqueeze(0).transpose(1, 2), x.k[a:b].unsqueeze(0).transpose(1, 2),
+                       x.v[a:b].unsqueeze(0).transpose(1, 2)))
+        views.append(vx)
 
-    def sdpa_all():
-        for q_, k_, v_ in views:
+    def sdpa_all(vx):
+        for q_, k_, v_ in vx:
             torch.nn.functional.scaled_dot_product_attention(q_, k_, v_, is_causal=True, enable_gqa=True)
 
-    sus = flushed_us(sdpa_all, flush)
+    sus = rotating_us([lambda vx=vx: sdpa_all(vx) for vx in views])
     line["torch_sdpa_per_prompt_us"] = sus
     line["speedup_vs_torch_sdpa"] = sus / us
     out["prefill_b16"] = line
-    del w, o, ref, views
+    del ws, w, o, ref, views
 
     # C3 at B=1: one prompt per call, the reference's own prefill call shape
     # q [1, 16, L, 128] (a transposed view of the [1, L, 16, 128] projection)
     pts = []
     g = torch.Generator(device=dev).manual_seed(31)
     for L in (512, 768, 1024):
-        q_ = torch.randn(1, L, 16, 128, generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
-        k_ = torch.randn(1, L, 8, 128, generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
-        v_ = torch.randn(1, L, 8, 128, generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
+        sets = []
+        for _ in range(sets_for(L * 32 * 256 + L * 16 * 256)):
+            sets.append(tuple(torch.randn(1, L, h, 128, generator=g, device=dev).to(torch.bfloat16).transpose(1, 2)
+                              for h in (16, 8, 8)))
 
-        def ours():
-            return pkg.scaled_dot_product_attention(q_, k_, v_, is_causal=True, enable_gqa=True)
+        def ours_1(x):
+            return pkg.scaled_dot_product_attention(*x, is_causal=True, enable_gqa=True)
 
-        def torch_sdpa():
-            return torch.nn.functional.scaled_dot_product_attention(q_, k_, v_, is_causal=True, enable_gqa=True)
+        def torch_1(x):
+            return torch.nn.functional.scaled_dot_product_attention(*x, is_causal=True, enable_gqa=True)
 
-        us = flushed_us(ours, flush, reps=20)
-        tus = flushed_us(torch_sdpa, flush, reps=20)
-        o = ours()
-        ref = torch.nn.functional.scaled_dot_product_attention(q_.float().cpu(), k_.float().cpu(), v_.float().cpu(),
-                                                               is_causal=True, enable_gqa=True)
+        us = rotating_us([lambda x=x: ours_1(x) for x in sets])
+        tus = rotating_us([lambda x=x: torch_1(x) for x in sets])
+        o = ours_1(sets[0])
+        qf, kf, vf = (t.float().cpu() for t in sets[0])
         t0 = time.perf_counter()
-        torch.nn.functional.scaled_dot_product_attention(q_.float().cpu(), k_.float().cpu(), v_.float().cpu(),
-                                                         is_causal=True, enable_gqa=True)
+        ref = torch.nn.functional.scaled_dot_product_attention(qf, kf, vf, is_causal=True, enable_gqa=True)
         cpu_us = (time.perf_counter() - t0) * 1e6
         flops = 2 * 16 * 128 * L * L
         pt = {"L": L, "us": us, "tflops": flops / (us * 1e-6) / 1e12, "torch_sdpa_us": tus,
               "speedup_vs_torch_sdpa": tus / us, "max_abs_err": float((o.float().cpu() - ref).abs().max()),
-              "cpu_reference_us": cpu_us}
+              "cpu_reference_us": cpu_us, "input_sets": len(sets)}
         if fa is not None:
+            cu1 = torch.tensor([0, L], dtype=torch.int32, device=dev)
+
+            def fa_1(x, cu1=cu1, L=L):
+                qv, kv, vv = (t.transpose(1, 2)[0] for t in x)
+                return fa.flash_attn_varlen_func(qv, kv, vv, cu1, cu1, L, L, causal=True)
+
             try:
-                qv, kv, vv = (x.transpose(1, 2)[0] for x in (q_, k_, v_))
-                cu1 = torch.tensor([0, L], dtype=torch.int32, device=dev)
-                pt["flash_attn_varlen_us"] = flushed_us(
-                    lambda: fa.flash_attn_varlen_func(qv, kv, vv, cu1, cu1, L, L, causal=True), flush, reps=20)
+                pt["flash_attn_varlen_us"] = rotating_us([lambda x=x: fa_1(x) for x in sets])
             except Exception as e:
                 pt["flash_attn"] = f"did not run: {type(e).__name__}: {str(e)[:120]}"
         pts.append(pt)
+        del sets
     out["prefill_b1"] = {"workload": "one prompt per call, q [1,16,L,128] / k,v [1,8,L,128] views of [1,L,H,128] "
                                      "(model.py:56-57), L = 512 / 768 / 1024", "points": pts, "tolerance": 2e-2,
                          "cpu_reference": {**cores, "sample": "fp32 causal SDPA of the same prompt"},
                          "peak_tflops": peak, "peak_source": peak_kind}
 
     # chunked prefill (row f1): 16 chunks of 512 over cached prefixes U[512,1536]
-    c = W.chunk_batch(16, 512, 512, 1536, seed=4, device=dev)
+    cs = [W.chunk_batch(16, 512, 512, 1536, seed=4 + 100 * i, device=dev) for i in range(2)]
+    c = cs[0]
 
-    def chunk():
-        return pkg.flash_attn_with_kvcache(c.q, c.k_cache, c.v_cache, cache_seqlens=c.cache_seqlens,
-                                           block_table=c.block_table, causal=True)
+    def chunk(x):
+        return pkg.flash_attn_with_kvcache(x.q, x.k_cache, x.v_cache, cache_seqlens=x.cache_seqlens,
+                                           block_table=x.block_table, causal=True)
 
-    us = flushed_us(chunk, flush)
-    o = chunk()
+    us = rotating_us([lambda x=x: chunk(x) for x in cs])
+    flops = sum(x.causal_flops for x in cs) / len(cs)
+    o = chunk(c)
     rows = [0, 7, 15]
     qr, kc, vc, bt, L = compact_rows(c.q, c.k_cache, c.v_cache, c.block_table, c.cache_seqlens, rows)
     n = c.q.shape[1]
     cu = torch.arange(0, (len(rows) + 1) * n, n, dtype=torch.int32)
     ref = opa.paged_chunk_prefill(qr.reshape(-1, *qr.shape[2:]), kc, vc, bt, L, cu)
     err = float((o.cpu()[torch.as_tensor(rows)].reshape(-1, *o.shape[2:]).float() - ref).abs().max())
-    tf = c.causal_flops / (us * 1e-6) / 1e12
+    tf = flops / (us * 1e-6) / 1e12
     out["chunk_prefill_b16"] = {"workload": "16 chunks of 512 tokens over cached prefixes U[512,1536] (paged, "
                                             "256-token blocks, bottom-right causal)",
                                 "us": us, "tflops": tf, "peak_tflops": peak, "frac": tf / peak,
-                                "peak_source": peak_kind, "flops": c.causal_flops, "max_abs_err": err,
-                                "checked_rows": rows, "tolerance": 2e-2}
-    del c
-    del flush
+                                "peak_source": peak_kind, "flops": flops, "input_sets": len(cs),
+                                "max_abs_err": err, "checked_rows": rows, "tolerance": 2e-2}
+    del cs, c
     torch.cuda.synchronize()
     pkg.check_device_errors(dev.index)
     return out
@@ -569,6 +586,35 @@ def kv_head_sharded_layer(pkg, dist, world, rank, dev, reps, max_over_ranks):
     t_attn_graph = graph_timed(attn)
     t_layer_graph = graph_timed(lambda i: dec.gather(attn(i)))  # NCCL all-gather captured too
 
+    # Row f4: the layer up to o_proj's output (model.py:68-69), three ways:
+    # NCCL gather + cuBLAS, fused NVLink gather + barrier + cuBLAS, and the
+    # fused gather with o_proj on the GEMM that waits for each peer's heads.
+    wo = (torch.randn(1024, 16 * 128, generator=torch.Generator().manual_seed(8)) / 2048 ** 0.5)
+    wo = wo.to(torch.bfloat16).to(dev)
+
+    def nccl_oproj(i):
+        return torch.nn.functional.linear(dec.gather(attn(i)).view(B, 16 * 128), wo)
+
+    def fused_barrier_oproj(i):
+        return torch.nn.functional.linear(fused_layer(i).view(B, 16 * 128), wo)
+
+    def fused_oproj(i):
+        kc, vc = pools[i % 4]
+        return fused.attention_o_proj(q, kc, vc, seq, btd, wo, slot=i % 2)
+
+    t_op_nccl = graph_timed(nccl_oproj)
+    t_op_barrier = graph_timed(fused_barrier_oproj)
+    t_op_fused = graph_timed(fused_oproj)
+    y_ref = nccl_oproj(0).clone()
+    y_fused = fused_oproj(0).clone()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ys = [torch.empty_like(y_fused) for _ in range(world)]
+    dist.all_gather(ys, y_fused)
+    y_same = all(torch.equal(ys[0], y) for y in ys)
+    y_err = max_over_ranks(float((y_fused.float() - y_ref.float()).abs().max()))
+    y_scale = float(y_ref.float().abs().max())
+
     # parity, pool 0, both forms on every rank
     o_nccl = dec.gather(attn(0)).clone()
     o_fused = fused_layer(0).clone()
@@ -600,6 +646,11 @@ def kv_head_sharded_layer(pkg, dist, world, rank, dev, reps, max_over_ranks):
             "kv_gbs_total": kv_total / (best * 1e-6) / 1e9,
             "kv_gbs_per_gpu_decode": kv_total / world / (t_attn_graph * 1e-6) / 1e9,
             "tok_per_s_attention_only": B / (best * 28 * 1e-6),
+            "o_proj": {"nccl_cublas_us_per_layer": t_op_nccl, "fused_gather_barrier_cublas_us_per_layer": t_op_barrier,
+                       "fused_gather_o_proj_us_per_layer": t_op_fused,
+                       "max_abs_diff_vs_nccl_cublas": y_err, "y_max_abs": y_scale,
+                       "identical_on_all_ranks": y_same,
+                       "what": "decode + all-gather + o_proj [B,2048]x[2048,1024] per layer, graph-captured"},
             "parity": {"max_abs_err_fused": err_fused, "max_abs_err_nccl": err_nccl,
                        "fused_equals_nccl_all_ranks": n_diff == 0.0, "fused_vs_nccl_max_abs": fused_vs_nccl,
                        "checked_rows_per_rank": len(rows), "tolerance": 2e-2,

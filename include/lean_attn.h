@@ -164,8 +164,8 @@ int la_paged_decode(
  * [r*Hkv/P, (r+1)*Hkv/P) of every request: rank r runs la_paged_decode on
  * its heads (num_q_heads / num_kv_heads = this rank's counts) and stores
  * each output row into every rank's gather buffer [batch, P*num_q_heads, D]
- * at heads [r*num_q_heads, (r+1)*num_q_heads), over NVLink; every thread
- * that stored fences at system scope. la_p2p_barrier, next on the same
+ * at heads [r*num_q_heads, (r+1)*num_q_heads), over NVLink; every combine
+ * CTA that stored fences once at system scope. la_p2p_barrier, next on the same
  * stream, completes the exchange: after it the gather buffer holds all
  * heads. Replaces the NCCL all-gather of the attention outputs before
  * o_proj (leaninfer/qwen3/model.py:68-69) for the KV-head-sharded variant;
@@ -199,6 +199,33 @@ int la_paged_decode_allgather(
  * device pointers to each rank's signal words (world + 1 uint32, zeroed once
  * by la_p2p_alloc), rank order. */
 int la_p2p_barrier(unsigned int* const* signals, int world, int rank, int* dev_error, cudaStream_t stream);
+
+/* The publishing half of la_p2p_barrier alone: this rank's next epoch goes to
+ * every rank's word [rank]; nothing waits. For a consumer that waits for each
+ * peer's epoch itself, as la_o_proj_gathered does. */
+int la_p2p_publish(unsigned int* const* signals, int world, int rank, int* dev_error, cudaStream_t stream);
+
+/* o_proj of the KV-head-sharded partition, fused with its all-gather:
+ *   out[m, n] = sum_k gathered[m, k] * weight[n, k]   (bf16 in, fp32
+ * accumulation on tcgen05, bf16 out), the o_proj Linear of
+ * leaninfer/qwen3/model.py:68-69 applied to this rank's gather buffer
+ * [m, k = P*num_q_heads*D] right after la_paged_decode_allgather and
+ * la_p2p_publish on the same stream. Columns [q*k/P, (q+1)*k/P) belong to
+ * rank q: the kernel reads them only after rank q's epoch in `signals` (this
+ * rank's signal words: [q] rank q's epoch, [world] this rank's own) has
+ * reached this rank's own, waiting for each peer separately (bounded:
+ * LA_DEVERR_WAIT_TIMEOUT after 2 s, the output is then invalid), so the
+ * peers' transfers overlap the GEMM and no barrier is needed. The columns are
+ * summed in one fixed order on every rank (all ranks get the same bits). With
+ * world = 1 it is a plain GEMM. k a multiple of 64 * world, n of 32; rows
+ * 16-byte aligned. No counterpart in the single-GPU reference beyond the
+ * Linear itself. */
+int la_o_proj_gathered(const void* gathered, int64_t gathered_row_stride,
+                       const void* weight, int64_t weight_row_stride,
+                       void* out, int64_t out_row_stride,
+                       int m, int n, int k,
+                       const unsigned int* signals, int world, int rank,
+                       int* dev_error, cudaStream_t stream);
 
 /* Peer-memory setup (host-side, outside the hot path; these allocate):
  * la_p2p_alloc: cudaMalloc + zero + CUDA IPC handle (64 bytes) to share;

@@ -106,6 +106,9 @@ _SIGNATURES = {
         c_void_p, c_void_p,
     ],
     "la_p2p_barrier": [c_void_p, c_int, c_int, c_void_p, c_void_p],
+    "la_p2p_publish": [c_void_p, c_int, c_int, c_void_p, c_void_p],
+    "la_o_proj_gathered": [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int, c_int, c_int,
+                           c_void_p, c_int, c_int, c_void_p, c_void_p],
     "la_p2p_alloc": [c_size_t, POINTER(c_void_p), c_void_p],
     "la_p2p_open": [c_void_p, POINTER(c_void_p)],
     "la_p2p_close": [c_void_p],

@@ -18,7 +18,7 @@ INCLUDE = REPO_DIR / "include"
 LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "liblean_attn.so"
 
-SOURCES = ["la_host.cu", "la_pre_attn.cu", "la_decode.cu", "la_decode_noalloc.cu", "la_prefill.cu", "la_p2p.cu", "la_elementwise.cu"]
+SOURCES = ["la_host.cu", "la_pre_attn.cu", "la_decode.cu", "la_decode_noalloc.cu", "la_prefill.cu", "la_p2p.cu", "la_elementwise.cu", "la_oproj.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

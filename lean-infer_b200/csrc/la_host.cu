@@ -103,6 +103,7 @@ int la_init(int device) {
   if (st == LA_OK) st = la::decode_init(device);
   if (st == LA_OK) st = la::pre_attn_init(device);
   if (st == LA_OK) st = la::prefill_init(device);
+  if (st == LA_OK) st = la::oproj_init(device);
   if (prev >= 0 && prev != device) cudaSetDevice(prev);
   return st;
 }

@@ -49,5 +49,6 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 int decode_init(int device);
 int pre_attn_init(int device);
 int prefill_init(int device);
+int oproj_init(int device);
 
 }  // namespace la

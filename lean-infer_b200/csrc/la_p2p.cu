@@ -29,7 +29,9 @@ struct Signals {
 // scope). Lane q then waits until rank q's epoch in this rank's word [q] has
 // reached the same value: from then on rank q's stores of the same call are
 // visible here.
-__global__ void __launch_bounds__(32) barrier_kernel(Signals s, int world, int rank, int* err) {
+// With wait == 0 (la_p2p_publish) the kernel only publishes: a later kernel
+// waits for each peer's epoch itself (la_o_proj_gathered).
+__global__ void __launch_bounds__(32) barrier_kernel(Signals s, int world, int rank, int wait, int* err) {
   const int q = threadIdx.x;
   unsigned int* own = s.words[rank];
   unsigned int epoch = 0;
@@ -42,7 +44,7 @@ __global__ void __launch_bounds__(32) barrier_kernel(Signals s, int world, int r
       asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(s.words[r] + rank), "r"(epoch) : "memory");
   }
   epoch = __shfl_sync(0xffffffffu, epoch, 0);
-  if (q >= world || q == rank) return;
+  if (!wait || q >= world || q == rank) return;
   const unsigned int* sig = own;
   const uint64_t t0 = globaltimer_ns();
   while (true) {
@@ -88,15 +90,27 @@ extern "C" int la_p2p_close(void* peer_ptr) { return la::cuda_status(cudaIpcClos
 
 extern "C" int la_p2p_free(void* ptr) { return la::cuda_status(cudaFree(ptr)); }
 
-extern "C" int la_p2p_barrier(unsigned int* const* signals, int world, int rank, int* dev_error,
-                              cudaStream_t stream) {
-  if (!signals || world < 1 || world > la::p2p::kMaxPeers || rank < 0 || rank >= world)
-    return LA_ERR_INVALID_ARGUMENT;
-  la::p2p::Signals s{};
+namespace la {
+namespace p2p {
+static int launch_barrier(unsigned int* const* signals, int world, int rank, int wait, int* dev_error,
+                          cudaStream_t stream) {
+  if (!signals || world < 1 || world > kMaxPeers || rank < 0 || rank >= world) return LA_ERR_INVALID_ARGUMENT;
+  Signals s{};
   for (int r = 0; r < world; ++r) {
-    if (!signals[r] || !la::aligned(signals[r], 4)) return LA_ERR_INVALID_ARGUMENT;
+    if (!signals[r] || !aligned(signals[r], 4)) return LA_ERR_INVALID_ARGUMENT;
     s.words[r] = signals[r];
   }
-  return la::cuda_status(la::launch_pdl(la::p2p::barrier_kernel, dim3(1), dim3(32), 0, stream, s, world, rank,
-                                        dev_error));
+  return cuda_status(launch_pdl(barrier_kernel, dim3(1), dim3(32), 0, stream, s, world, rank, wait, dev_error));
+}
+}  // namespace p2p
+}  // namespace la
+
+extern "C" int la_p2p_barrier(unsigned int* const* signals, int world, int rank, int* dev_error,
+                              cudaStream_t stream) {
+  return la::p2p::launch_barrier(signals, world, rank, 1, dev_error, stream);
+}
+
+extern "C" int la_p2p_publish(unsigned int* const* signals, int world, int rank, int* dev_error,
+                              cudaStream_t stream) {
+  return la::p2p::launch_barrier(signals, world, rank, 0, dev_error, stream);
 }

@@ -179,9 +179,12 @@ class NVLinkAllGatherDecode:
 
     def __call__(self, q_local: torch.Tensor, k_cache_local: torch.Tensor, v_cache_local: torch.Tensor,
                  cache_seqlens: torch.Tensor, block_table: torch.Tensor, slot: int = 0,
-                 softmax_scale: Optional[float] = None) -> torch.Tensor:
+                 softmax_scale: Optional[float] = None, wait: bool = True) -> torch.Tensor:
         """q_local [B, 1, Hq/P, D] -> gathered [B, 1, Hq, D] (a view of this
-        rank's gather slot, valid until the slot is reused)."""
+        rank's gather slot, valid until the slot is reused). With wait=False
+        the call only publishes this rank's epoch: the slot may still be
+        filling, and the next kernel on the stream must wait for each peer
+        itself (o_proj does)."""
         from . import flash_attn_interface as fai
 
         ct, lib = self._ct, self._lib
@@ -207,8 +210,44 @@ class NVLinkAllGatherDecode:
                  self.rank, self.P,
                  ct.c_void_p(ws.data_ptr()), ws.numel(),
                  ct.c_void_p(err.data_ptr()), stream)
-        lib.call("la_p2p_barrier", self._signals, self.P, self.rank, ct.c_void_p(err.data_ptr()), stream)
+        lib.call("la_p2p_barrier" if wait else "la_p2p_publish", self._signals, self.P, self.rank,
+                 ct.c_void_p(err.data_ptr()), stream)
         return self.local[slot][:B].view(B, 1, self.hq_total, D)
+
+    def o_proj(self, gathered: torch.Tensor, weight: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """o_proj (model.py:68-69) of a gathered slot on the tcgen05 GEMM that
+        waits for each peer's heads as they land (la_o_proj_gathered):
+        gathered [B, 1, Hq, D] from __call__(..., wait=False), weight
+        [hidden, Hq*D] bf16 -> [B, hidden] bf16, the same on every rank."""
+        from . import flash_attn_interface as fai
+
+        ct, lib = self._ct, self._lib
+        B = gathered.shape[0]
+        K = self.hq_total * self.D
+        if weight.dim() != 2 or weight.shape[1] != K or weight.dtype != torch.bfloat16 or weight.stride(1) != 1:
+            raise RuntimeError("weight must be bf16 [hidden, Hq*D] with a contiguous last axis")
+        a = gathered.view(B, K)
+        N = weight.shape[0]
+        if out is None:
+            out = torch.empty(B, N, dtype=torch.bfloat16, device=gathered.device)
+        dev = gathered.device.index
+        stream = ct.c_void_p(torch.cuda.current_stream(gathered.device).cuda_stream)
+        lib.call("la_o_proj_gathered", ct.c_void_p(a.data_ptr()), a.stride(0), ct.c_void_p(weight.data_ptr()),
+                 weight.stride(0), ct.c_void_p(out.data_ptr()), out.stride(0), B, N, K,
+                 ct.c_void_p(self._bases[self.rank]), self.P, self.rank,
+                 ct.c_void_p(fai.error_word(dev).data_ptr()), stream)
+        return out
+
+    def attention_o_proj(self, q_local: torch.Tensor, k_cache_local: torch.Tensor, v_cache_local: torch.Tensor,
+                         cache_seqlens: torch.Tensor, block_table: torch.Tensor, o_proj_weight: torch.Tensor,
+                         slot: int = 0, softmax_scale: Optional[float] = None) -> torch.Tensor:
+        """One KV-head-sharded attention layer up to o_proj's output: decode on
+        this rank's heads with the all-gather stores fused in, an epoch
+        publish, and the o_proj GEMM consuming the peers' heads as they land.
+        Returns [B, hidden] (identical on every rank)."""
+        g = self(q_local, k_cache_local, v_cache_local, cache_seqlens, block_table, slot=slot,
+                 softmax_scale=softmax_scale, wait=False)
+        return self.o_proj(g, o_proj_weight)
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (collective)."""
