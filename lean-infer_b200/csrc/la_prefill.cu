@@ -96,7 +96,15 @@ template <bool kSplit>
 __host__ __device__ constexpr int off_state() { return kOffBar + (kSplit ? 512 : 256); }
 template <bool kSplit>
 __host__ __device__ constexpr int off_xmax() { return off_state<kSplit>() + 8 * 128; }
-constexpr size_t kSmemBytes = off_xmax<true>() + 2 * 2 * kRows * 4 + 1024;  // both instances
+// The split instance's item walk table: the total item count, then the
+// query-tile levels of each sequence (uint16) for up to kMaxSeqs sequences.
+// That instance runs only when the items do not fill the SMs (fewer than
+// #SMs sequence x kv-head tiles), so 256 sequences cover it; more fall back
+// to cu_seqlens. Kept small: shared memory taken here is L1 cache lost.
+constexpr int kOffWalk = off_xmax<true>() + 2 * 2 * kRows * 4;
+constexpr int kMaxSeqs = 256;
+constexpr size_t kSmemBytes = kOffWalk + 16 + 2 * kMaxSeqs + 1024;  // + the run-time 1024-byte alignment
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 
 struct Params {
   const int* cu;  // query starts [num_seqs + 1], or null: sequence s has q_len queries from token s * q_len
@@ -176,24 +184,64 @@ struct Walker {
 __device__ __forceinline__ int q_start(const Params& p, int s) { return p.cu ? p.cu[s] : s * p.q_len; }
 __device__ __forceinline__ int q_count(const Params& p, int s) { return p.cu ? p.cu[s + 1] - p.cu[s] : p.q_len; }
 
+// The walk table, built once per CTA after the dependency wait: lv[s] = the
+// number of levels of sequence s (its query tiles, or tile pairs, capped at
+// n_qp), held in shared memory, so that level counts and the search for an
+// item's sequence read shared memory rather than cu_seqlens in global memory
+// (a dependent global round trip per level, which every role paid at each
+// item boundary and, walking down every remaining level, at the end of the
+// kernel); total = all items, so a walker past it stops at once. With more
+// than kMaxSeqs sequences lv is null and the levels come from cu_seqlens.
+// Laid out at kOffWalk of the CTA's shared memory: [0] total (int64), [8]
+// lv cached (int32), [16] lv[kMaxSeqs] (uint16). Read through the shared
+// memory base at each use, so nothing of it stays live in registers.
+struct WalkTable {
+  const uint8_t* smem;
+  __device__ __forceinline__ long long total() const { return *reinterpret_cast<const long long*>(smem + kOffWalk); }
+  __device__ __forceinline__ bool cached() const { return *reinterpret_cast<const int*>(smem + kOffWalk + 8) != 0; }
+  __device__ __forceinline__ int lv(int s) const {
+    return reinterpret_cast<const uint16_t*>(smem + kOffWalk + 16)[s];
+  }
+};
+
+__device__ __forceinline__ int levels_of(const Params& p, int s) {
+  const int per = p.pair * p.tq;
+  return min((q_count(p, s) + per - 1) / per, p.n_qp);
+}
+
+// kTable: levels from the shared-memory table (the split instance, whose
+// CTAs hold one item each, most at high levels, so the walk down to the end
+// dominated its tail); otherwise from cu_seqlens (the pair instance, whose
+// hot loops measured slower with the table's code in the kernel).
 __device__ __forceinline__ bool seq_has_pair(const Params& p, int s, int q0) {
   return s < p.num_seqs && q_count(p, s) > q0;
 }
 
+// Whether sequence s has an item at `level` (its query tiles, or pairs, reach it).
+template <bool kTable>
+__device__ __forceinline__ bool seq_at_level(const Params& p, const WalkTable& t, int s, int level) {
+  if constexpr (kTable) {
+    if (t.cached()) return s < p.num_seqs && static_cast<int>(t.lv(s)) > level;
+  }
+  return seq_has_pair(p, s, level * p.pair * p.tq);
+}
+
 // Items at one level (warp-collective).
-__device__ __forceinline__ int level_count(const Params& p, int level) {
+template <bool kTable>
+__device__ __forceinline__ int level_count(const Params& p, const WalkTable& t, int level) {
   const int lane = threadIdx.x & 31;
-  const int q0 = level * p.pair * p.tq;
   int n = 0;
-  for (int b = 0; b < p.num_seqs; b += 32) n += __popc(__ballot_sync(0xffffffffu, seq_has_pair(p, b + lane, q0)));
+  for (int b = 0; b < p.num_seqs; b += 32)
+    n += __popc(__ballot_sync(0xffffffffu, seq_at_level<kTable>(p, t, b + lane, level)));
   return n * p.hkv;
 }
 
-__device__ __forceinline__ void walker_init(const Params& p, Walker& w) {
+template <bool kTable>
+__device__ __forceinline__ void walker_init(const Params& p, const WalkTable& t, Walker& w) {
   w.taken = 0;
   w.level = p.n_qp - 1;
   w.base = 0;
-  w.count = level_count(p, w.level);
+  w.count = level_count<kTable>(p, t, w.level);
 }
 
 // KV tiles a query tile starting at token q0 needs (at least one, so every
@@ -204,23 +252,27 @@ __device__ __forceinline__ int kv_tiles(const Params& p, const Item& it, int q0)
 }
 
 // Next item of this CTA (warp-collective; identical result in every lane).
-__device__ __forceinline__ bool walker_next(const Params& p, Walker& w, Item& it) {
+template <bool kTable>
+__device__ __forceinline__ bool walker_next(const Params& p, const WalkTable& t, Walker& w, Item& it) {
   const int lane = threadIdx.x & 31;
   const long long g2 = 2LL * gridDim.x;
   const long long r = static_cast<long long>(w.taken >> 1) * g2 +
                       ((w.taken & 1) ? (g2 - 1 - blockIdx.x) : static_cast<long long>(blockIdx.x));
+  if constexpr (kTable) {
+    if (r >= t.total()) return false;
+  }
   while (r >= w.base + w.count) {
     if (w.level == 0) return false;
     w.base += w.count;
     --w.level;
-    w.count = level_count(p, w.level);
+    w.count = level_count<kTable>(p, t, w.level);
   }
   const int idx = static_cast<int>(r - w.base);
   const int ord = idx / p.hkv;  // the ord-th sequence (index order) that has this level's pair
   const int q0 = w.level * p.pair * p.tq;
   int seen = 0, s = 0;
   for (int b = 0; b < p.num_seqs; b += 32) {
-    const unsigned m = __ballot_sync(0xffffffffu, seq_has_pair(p, b + lane, q0));
+    const unsigned m = __ballot_sync(0xffffffffu, seq_at_level<kTable>(p, t, b + lane, w.level));
     const int c = __popc(m);
     if (ord < seen + c) {
       unsigned mm = m;
@@ -289,11 +341,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float NEG_INF = -__int_as_float(0x7f800000);
 
   grid_dependency_wait();
-  {  // a CTA without work leaves before touching barriers or TMEM
+  const WalkTable wt{smem};
+  if (kSplit) {
+    uint16_t* lv = reinterpret_cast<uint16_t*>(smem + kOffWalk + 16);
+    long long* total = reinterpret_cast<long long*>(smem + kOffWalk);
+    const bool cached = p.num_seqs <= kMaxSeqs && p.n_qp <= 65535;
+    if (threadIdx.x == 0) *reinterpret_cast<int*>(smem + kOffWalk + 8) = cached ? 1 : 0;
+    if (cached)
+      for (int s = threadIdx.x; s < p.num_seqs; s += kThreads) lv[s] = static_cast<uint16_t>(levels_of(p, s));
+    __syncthreads();
+    if (warp == 0) {
+      long long tot = 0;
+      for (int b = 0; b < p.num_seqs; b += 32) {
+        int n = (b + lane < p.num_seqs) ? (cached ? static_cast<int>(lv[b + lane]) : levels_of(p, b + lane)) : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+        tot += n;
+      }
+      if (lane == 0) *total = tot * p.hkv;
+    }
+    __syncthreads();
+    // a CTA without work (its first item's rank is blockIdx.x) leaves before
+    // touching barriers or TMEM
+    if (static_cast<long long>(blockIdx.x) >= wt.total()) return;
+  } else {  // the same exit from one walk
     Walker w;
-    walker_init(p, w);
+    walker_init<false>(p, wt, w);
     Item it;
-    if (!walker_next(p, w, it)) return;
+    if (!walker_next<false>(p, wt, w, it)) return;
   }
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -343,11 +418,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* xmax = reinterpret_cast<float*>(smem + off_xmax<kSplit>());  // [step % 2][half][row]
     Walker& w = *reinterpret_cast<Walker*>(smem + off_state<kSplit>() + warp * 128);
     Item& it = *reinterpret_cast<Item*>(smem + off_state<kSplit>() + warp * 128 + 32);
-    walker_init(p, w);
+    walker_init<kSplit>(p, wt, w);
     uint32_t t = 0;    // S_0 tiles seen
     uint32_t nst = 0;  // items whose statistics were written
     bool ok = true;
-    while (ok && walker_next(p, w, it)) {
+    while (ok && walker_next<kSplit>(p, wt, w, it)) {
       const int ni = it.n0;
       const int tok = it.q0 + (row & (p.tq - 1));
       const int lim = p.causal ? min(max(tok + 1 + it.off, 0), it.K) : it.K;
@@ -460,11 +535,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // exponential loop.
     Walker& w = *reinterpret_cast<Walker*>(smem + off_state<kSplit>() + warp * 128);
     Item& it = *reinterpret_cast<Item*>(smem + off_state<kSplit>() + warp * 128 + 32);
-    walker_init(p, w);
+    walker_init<kSplit>(p, wt, w);
     uint32_t t = 0;      // S_i tiles seen
     uint32_t nst = 0;    // items whose statistics were written
     bool ok = true;
-    while (ok && walker_next(p, w, it)) {
+    while (ok && walker_next<kSplit>(p, wt, w, it)) {
       const int ni = i ? it.n1 : it.n0;
       if (ni == 0) continue;
       const int tok = it.q0 + i * p.tq + (row & (p.tq - 1));        // token index within the sequence
@@ -577,12 +652,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     uint8_t* stage = smem + kOffStage + quarter * kStageBytes;
     Walker w;
-    walker_init(p, w);
+    walker_init<kSplit>(p, wt, w);
     Item it;
     uint32_t cp[2] = {0, 0};       // PV_i so far (through this item)
     uint32_t items_i[2] = {0, 0};  // items in which tile i ran
     bool ok = true;
-    while (ok && walker_next(p, w, it)) {
+    while (ok && walker_next<kSplit>(p, wt, w, it)) {
       for (int i = 0; i < 2 && ok; ++i) {
         const int ni = i ? it.n1 : it.n0;
         if (ni == 0) continue;
@@ -689,12 +764,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       Walker w;
-      walker_init(p, w);
+      walker_init<kSplit>(p, wt, w);
       Item it;
       int kq = 0;
       long long nld = 0;  // K/V tiles loaded
       bool ok = true;
-      while (ok && walker_next(p, w, it)) {
+      while (ok && walker_next<kSplit>(p, wt, w, it)) {
         if (lane == 0 && it.q0 + p.pair * p.tq >= p.n_qp * p.pair * p.tq && it.L > p.n_qp * p.pair * p.tq && p.err)
           atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);  // longer than max_seqlen: the tail is not computed
         if (!(ok = wait_all(q_empty, (kq & 1) ^ 1u))) break;
@@ -732,7 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // which reads P(j) from the same columns (the tensor core executes this
       // thread's MMAs in order), while the softmax works on S(j+1).
       Walker w;
-      walker_init(p, w);
+      walker_init<kSplit>(p, wt, w);
       Item it;
       int kq = 0;
       long long nld = 0;  // K/V ring position of the item's K(0)
@@ -764,7 +839,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++sc;
         return true;
       };
-      while (ok && walker_next(p, w, it)) {
+      while (ok && walker_next<kSplit>(p, wt, w, it)) {
         if (!(ok = wait_all(q_full, kq & 1))) break;
         ++kq;
         const int n = it.n0;
@@ -816,7 +891,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 12) {
       // ---------------------------------------------------------- MMA issuer (lane 0 issues)
       Walker w;
-      walker_init(p, w);
+      walker_init<kSplit>(p, wt, w);
       Item it;
       int kq = 0;
       long long nld = 0;               // K/V ring position of the item's K(0)
@@ -864,7 +939,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto wait_full = [&](long long idx) -> bool {
         return wait_all(&kv_full[slot_of(idx)], static_cast<uint32_t>(idx / kStages) & 1);
       };
-      while (ok && walker_next(p, w, it)) {
+      while (ok && walker_next<kSplit>(p, wt, w, it)) {
         if (!(ok = wait_all(q_full, kq & 1))) break;
         const long long base = nld;  // K(j) at base + 2j, V(j) at base + 2j + 1
         nld += 2LL * it.n;
