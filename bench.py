@@ -684,10 +684,13 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
-def step_bs16(pkg, model, cache, dg, ids, pos, bt, ctx, dev, steps):
+def step_bs16(pkg, model, cache, dg, ids, pos, bt, ctx, dev, steps, order="random"):
     """Row f2 end to end: the same decode step over a pool of 16-token blocks
     (same token capacity, the same cached tokens copied into it), timed like
-    the headline; parity = its logits against the 256-token-block step's."""
+    the headline; parity = its logits against the 256-token-block step's.
+    order: "random" deals the blocks from a seeded permutation of the pool
+    (as the 256-token step does), "fifo" in allocator order (each sequence's
+    blocks one after another, as a fresh BlockAllocator hands them out)."""
     from lean_infer_b200 import qwen3
     from lean_infer_b200 import workloads as W
     from lean_infer_b200.cache import BlockCache
@@ -695,7 +698,15 @@ def step_bs16(pkg, model, cache, dg, ids, pos, bt, ctx, dev, steps):
     cfg = model.config
     nb16 = NUM_BLOCKS * BLOCK_SIZE // 16
     cache16 = BlockCache(cfg.num_hidden_layers, nb16, 16, cfg.num_key_value_heads, cfg.head_dim, dev, zero=False)
-    bt16, _ = W.deal_blocks(ctx.long(), 16, nb16, 123)
+    if order == "random":
+        bt16, _ = W.deal_blocks(ctx.long(), 16, nb16, 123)
+    else:
+        need = [-(-int(n) // 16) for n in ctx]
+        bt16 = torch.zeros(len(need), max(need), dtype=torch.int32)
+        o = 1
+        for b, n in enumerate(need):
+            bt16[b, :n] = torch.arange(o, o + n, dtype=torch.int32)
+            o += n
     relayout_pool(cache, bt, cache16, bt16, ctx)
     dg16 = qwen3.DecodeGraph(model, cache16, B_PER_GPU, -(-CTX_HI // 16))
     dg16.stage(ids, pos, bt16, ctx)
@@ -723,8 +734,8 @@ def step_bs16(pkg, model, cache, dg, ids, pos, bt, ctx, dev, steps):
     pkg.check_device_errors(dev.index)
     dg16.release()
     del cache16
-    return {"workload": WORKLOAD.replace("512x256-token", "8192x16-token"), "ms_per_step": ms,
-            "tok_per_s": B_PER_GPU / (ms / 1e3), "logits_max_abs_diff_vs_bs256": err,
+    return {"workload": WORKLOAD.replace("512x256-token", "8192x16-token") + f", blocks in {order} order",
+            "ms_per_step": ms, "tok_per_s": B_PER_GPU / (ms / 1e3), "logits_max_abs_diff_vs_bs256": err,
             "next_token_agreement_vs_bs256": agree}
 
 
@@ -854,7 +865,9 @@ def run_ours(args):
 
     bs16 = None
     if world == 1 and not args.no_secondary:
-        bs16 = step_bs16(pkg, model, cache, dg, ids, pos, bt, ctx, dev, max(3, args.steps))
+        bs16 = {o: step_bs16(pkg, model, cache, dg, ids, pos, bt, ctx, dev, max(3, args.steps), order=o)
+                for o in ("random", "fifo")}
+        bs16["bs256_ms_per_step"] = ms
     dg.release()
 
     result = {
