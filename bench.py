@@ -39,6 +39,7 @@ config.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -907,7 +908,7 @@ def run_ours(args):
 
 def run_case(args):
     """Single-kernel cases for profilers (ncu): run one op a few times on a
-    small, fixed input and exit. --case decode-b128 | decode-c1 | decode-long |
+    small, fixed input and exit. --case decode-b128 | decode-c1 | decode-kvshard8 | o-proj | decode-long |
     prefill-b16 | prefill-b1 | prefill-long | chunk-prefill-b16 | pre-attn-b128."""
     import __graft_entry__
 
@@ -942,6 +943,35 @@ def run_case(args):
             pkg.flash_attn_with_kvcache(c.q, c.k_cache, c.v_cache, cache_seqlens=c.cache_seqlens,
                                         block_table=c.block_table, causal=True)
         info = {"causal_flops": c.causal_flops}
+    elif args.case == "o-proj":  # the gathered o_proj of the KV-head-sharded layer, world = 1: B=1024 and 256
+        from lean_infer_b200 import _lib
+        from lean_infer_b200 import flash_attn_interface as fai
+
+        lib = _lib.load()
+        fai.ensure_init(0)
+        g = torch.Generator(device=dev).manual_seed(6)
+        w_o = (torch.randn(1024, 2048, generator=g, device=dev) / 45).to(torch.bfloat16)
+        sig = torch.zeros(8, dtype=torch.int32, device=dev)
+        err = fai.error_word(0)
+        stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        for m in (1024, 256):
+            a = torch.randn(m, 2048, generator=g, device=dev).to(torch.bfloat16)
+            o = torch.empty(m, 1024, dtype=torch.bfloat16, device=dev)
+            for _ in range(reps):
+                rc = lib.la_o_proj_gathered(ctypes.c_void_p(a.data_ptr()), 2048, ctypes.c_void_p(w_o.data_ptr()), 2048,
+                                            ctypes.c_void_p(o.data_ptr()), 1024, m, 1024, 2048,
+                                            ctypes.c_void_p(sig.data_ptr()), 1, 0, ctypes.c_void_p(err.data_ptr()),
+                                            stream)
+                assert rc == 0
+        info = {"flops": 2 * 1280 * 1024 * 2048}
+    elif args.case == "decode-kvshard8":  # one rank of the KV-head-sharded partition at 8 GPUs
+        L = W.seq_lengths(1024, CTX_LO, CTX_HI, 500)
+        w = W.decode_batch(1024, CTX_LO, CTX_HI, num_blocks=None, block_size=BLOCK_SIZE, num_q_heads=2,
+                           num_kv_heads=1, seed=500, device=dev, lengths=L)
+        for _ in range(reps):
+            pkg.flash_attn_with_kvcache(w.q, w.k_cache, w.v_cache, cache_seqlens=w.cache_seqlens,
+                                        block_table=w.block_table, causal=True)
+        info = {"kv_bytes": w.kv_bytes}
     elif args.case == "pre-attn-b128":
         from lean_infer_b200 import qwen3
 

@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&empty[s], kCWarps);
     }
     mbar_init(mg_full, kCWarps);
-    mbar_init(mg_empty, kCWarps);
+    mbar_init(mg_empty, p.hkv);
     fence_barrier_init();
   }
   if (threadIdx.x < 32) reinterpret_cast<uint32_t*>(zero_row)[threadIdx.x] = 0u;
@@ -533,14 +533,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (d.flags & kFlagLast) {
       float L0 = warp_sum_g(l0), L1 = warp_sum_g(l1);
       const int c0 = 2 * tq, c1 = 2 * tq + 1;
-      int mt_lo = 0, mt_hi = 8;  // 16-dim slices of O this warp writes
-      bool lse_writer = true;
+      bool writer = true;
       if (p.nsub > 1) {
         // Several warps hold partial states of the same kv head (one per
-        // sub-chunk j). Each leaves its state in shared memory; then every
-        // one of them merges all nsub states for its own 8/nsub slices of
-        // the 128 dims (the row statistics are merged by all of them), so
-        // the merge is spread over the warps instead of serialised on one.
+        // sub-chunk j). Merge them in shared memory into warp j = 0 so every
+        // segment leaves one state per head, as with nsub == 1.
         const int TQ = (G + 1) >> 1;  // lanes (per g) that hold real columns
         const uint32_t par = static_cast<uint32_t>(seg_ends & 1);
         if (!mbar_wait(mg_empty, par ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) return;
@@ -557,56 +554,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(mg_full);
-        if (!mbar_wait(mg_full, par, p.err, LA_DEVERR_WAIT_TIMEOUT)) return;
-        const int per = 8 / p.nsub;
-        mt_lo = j * per;
-        mt_hi = mt_lo + per;
-        lse_writer = (j == 0);
-        if (tq < TQ) {
-          float M0 = NEG_INF, M1 = NEG_INF;
-          for (int jj = 0; jj < p.nsub; ++jj) {
-            const float* sl = merge + (((jj * hkv + h) * TQ + tq) * 8 + g) * 36;
-            M0 = fmaxf(M0, sl[0]);
-            M1 = fmaxf(M1, sl[1]);
-          }
-          float S0 = 0.f, S1 = 0.f;
+        writer = (j == 0);
+        if (writer) {
+          if (!mbar_wait(mg_full, par, p.err, LA_DEVERR_WAIT_TIMEOUT)) return;
+          if (tq < TQ) {
+            for (int jj = 1; jj < p.nsub; ++jj) {
+              const float* sl = merge + (((jj * hkv + h) * TQ + tq) * 8 + g) * 36;
+              const float om0 = sl[0], om1 = sl[1], oL0 = sl[2], oL1 = sl[3];
+              const float n0 = fmaxf(m0, om0), n1 = fmaxf(m1, om1);
+              // a side with no keys (m = -inf) contributes nothing
+              const float a0 = (m0 == NEG_INF) ? 0.f : ex2(m0 - n0), b0 = (om0 == NEG_INF) ? 0.f : ex2(om0 - n0);
+              const float a1 = (m1 == NEG_INF) ? 0.f : ex2(m1 - n1), b1 = (om1 == NEG_INF) ? 0.f : ex2(om1 - n1);
 #pragma unroll
-          for (int mt = 0; mt < 8; ++mt)
-            if (mt >= mt_lo && mt < mt_hi) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-          for (int jj = 0; jj < p.nsub; ++jj) {
-            const float* sl = merge + (((jj * hkv + h) * TQ + tq) * 8 + g) * 36;
-            // a sub-chunk with no keys (m = -inf) contributes nothing
-            const float a0 = (sl[0] == NEG_INF) ? 0.f : ex2(sl[0] - M0);
-            const float a1 = (sl[1] == NEG_INF) ? 0.f : ex2(sl[1] - M1);
-            S0 += sl[2] * a0;
-            S1 += sl[3] * a1;
-#pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-              if (mt >= mt_lo && mt < mt_hi) {
-                o[mt][0] += sl[4 + mt * 4 + 0] * a0;
-                o[mt][1] += sl[4 + mt * 4 + 1] * a1;
-                o[mt][2] += sl[4 + mt * 4 + 2] * a0;
-                o[mt][3] += sl[4 + mt * 4 + 3] * a1;
+              for (int mt = 0; mt < 8; ++mt) {
+                o[mt][0] = o[mt][0] * a0 + sl[4 + mt * 4 + 0] * b0;
+                o[mt][1] = o[mt][1] * a1 + sl[4 + mt * 4 + 1] * b1;
+                o[mt][2] = o[mt][2] * a0 + sl[4 + mt * 4 + 2] * b0;
+                o[mt][3] = o[mt][3] * a1 + sl[4 + mt * 4 + 3] * b1;
               }
+              L0 = L0 * a0 + oL0 * b0;
+              L1 = L1 * a1 + oL1 * b1;
+              m0 = n0;
+              m1 = n1;
             }
           }
-          m0 = M0;
-          m1 = M1;
-          L0 = S0;
-          L1 = S1;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(mg_empty);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(mg_empty);
         ++seg_ends;
       }
-      if (d.flags & kFlagWhole) {
+      if (writer && (d.flags & kFlagWhole)) {
         const float i0 = L0 > 0.f ? 1.f / L0 : 0.f;
         const float i1 = L1 > 0.f ? 1.f / L1 : 0.f;
         {
           __nv_bfloat16* ob = p.out + static_cast<long long>(d.b) * p.out_b_stride;
 #pragma unroll
           for (int mt = 0; mt < 8; ++mt) {
-            if (mt < mt_lo || mt >= mt_hi) continue;
             const int d0 = mt * 16 + g;
             if (c0 < G) {
               __nv_bfloat16* oh = ob + static_cast<long long>(h * G + c0) * p.out_h_stride;
@@ -620,18 +603,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (lse_writer && p.lse_out && g == 0) {
+        if (p.lse_out && g == 0) {
           const float ln2 = 0.6931471805599453f;
           if (c0 < G) p.lse_out[static_cast<long long>(d.b) * p.hq + h * G + c0] = L0 > 0.f ? (m0 + __log2f(L0)) * ln2 : NEG_INF;
           if (c1 < G) p.lse_out[static_cast<long long>(d.b) * p.hq + h * G + c1] = L1 > 0.f ? (m1 + __log2f(L1)) * ln2 : NEG_INF;
         }
-      } else {
+      } else if (writer) {
         float* po = p.part_o + static_cast<long long>(d.slot) * p.hq * kD;
         const float i0 = L0 > 0.f ? 1.f / L0 : 0.f;
         const float i1 = L1 > 0.f ? 1.f / L1 : 0.f;
 #pragma unroll
         for (int mt = 0; mt < 8; ++mt) {
-          if (mt < mt_lo || mt >= mt_hi) continue;
           const int d0 = mt * 16 + g;
           if (c0 < G) {
             float* oh = po + (h * G + c0) * kD;
@@ -644,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             oh[d0 + 8] = o[mt][3] * i1;
           }
         }
-        if (lse_writer && g == 0) {
+        if (g == 0) {
           float* pl = p.part_lse + static_cast<long long>(d.slot) * p.hq;
           if (c0 < G) pl[h * G + c0] = L0 > 0.f ? m0 + __log2f(L0) : NEG_INF;
           if (c1 < G) pl[h * G + c1] = L1 > 0.f ? m1 + __log2f(L1) : NEG_INF;
@@ -657,13 +639,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------------ combine
 // Grid (batch, Hq), one warp per (sequence, query head); lane l owns dims
 // 4l..4l+3. Sequences whose key range lies inside one CTA's range were
-// written directly by the decode kernel and are skipped. The others merge
-// their partials: up to 32 slots per round, one per lane (each lane finds
+// written directly by the decode kernel and are skipped. Rows over a few
+// CTAs (at most kCombineFew) merge their slots one after another. The others
+// merge their partials: up to 32 slots per round, one per lane (each lane finds
 // its CTA's slot with its own two divisions and loads that slot's lse, so a
 // round costs one division latency whatever the slot count); the round's
 // max and weight sum are warp reductions, then the O rows are read 8 at a
 // time with independent loads.
 constexpr int kCombineBatch = 8;
+constexpr int kCombineFew = 4;  // rows over at most this many CTAs take the sequential merge
 
 __device__ __forceinline__ float warp_max_all(float v) {
 #pragma unroll
@@ -718,6 +702,45 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
         for (int r = 0; r < p.nouts; ++r)
           if (p.outs[r] != p.out) *reinterpret_cast<uint2*>(p.outs[r] + oofs) = v;
       }
+    } else if (cl - cf < kCombineFew) {
+      // A few slots (rows split across two to four CTAs, the usual case at
+      // large batches): merge them one after another, all loads issued first.
+      float m = NEG_INF, l = 0.f;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      float ls[kCombineFew];
+      float4 ov[kCombineFew];
+#pragma unroll
+      for (int u = 0; u < kCombineFew; ++u) {
+        const long long c = cf + u;
+        ls[u] = NEG_INF;
+        if (c <= cl) {
+          const long long s0 = cta_start(c, T, Gl);
+          if (s0 != cta_start(c + 1, T, Gl)) {  // an empty range (T < G) wrote nothing
+            const long long slot = 2 * c + (s0 >= Pb ? 0 : 1);
+            ls[u] = p.part_lse[slot * p.hq + hh];
+            ov[u] = *reinterpret_cast<const float4*>(p.part_o + (slot * p.hq + hh) * kD + lane * 4);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kCombineFew; ++u) {
+        if (ls[u] != NEG_INF) {
+          const float mn = fmaxf(m, ls[u]);
+          const float a = ex2(m - mn), w = ex2(ls[u] - mn);
+          acc[0] = acc[0] * a + w * ov[u].x;
+          acc[1] = acc[1] * a + w * ov[u].y;
+          acc[2] = acc[2] * a + w * ov[u].z;
+          acc[3] = acc[3] * a + w * ov[u].w;
+          l = l * a + w;
+          m = mn;
+        }
+      }
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint2 v;
+      v.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+      v.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+      for (int r = 0; r < p.nouts; ++r) *reinterpret_cast<uint2*>(p.outs[r] + oofs) = v;
+      if (lse && lane == 0) *lse = l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
     } else {
       float m = NEG_INF, l = 0.f;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};

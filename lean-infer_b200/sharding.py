@@ -231,6 +231,7 @@ class NVLinkAllGatherDecode:
         if out is None:
             out = torch.empty(B, N, dtype=torch.bfloat16, device=gathered.device)
         dev = gathered.device.index
+        fai.ensure_init(dev)
         stream = ct.c_void_p(torch.cuda.current_stream(gathered.device).cuda_stream)
         lib.call("la_o_proj_gathered", ct.c_void_p(a.data_ptr()), a.stride(0), ct.c_void_p(weight.data_ptr()),
                  weight.stride(0), ct.c_void_p(out.data_ptr()), out.stride(0), B, N, K,

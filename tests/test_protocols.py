@@ -467,11 +467,10 @@ class DecodeModel:
     warp waits a stage's empty barrier (one arrival per consumer warp), writes
     the stage descriptor into shared memory and starts its copies; consumer
     warps wait the full barrier, read descriptor and tiles, release the stage;
-    at each segment end every warp leaves its softmax state in a merge slot
-    (after the previous merge was read: mg_empty, one arrival per warp) and,
-    once all warps have written (mg_full, one arrival per warp), every warp
-    reads the slots of all sub-chunk warps of its kv head (each merges its
-    own slices of the head's dims)."""
+    at each segment end the warps of sub-chunks j > 0 leave their softmax
+    state in a merge slot (after the previous merge was read: mg_empty, one
+    arrival per kv head) and warp j = 0 of each kv head reads them once all
+    warps have written (mg_full, one arrival per warp)."""
 
     STAGES = 3
 
@@ -480,7 +479,7 @@ class DecodeModel:
         self.rng, self.plant = rng, plant
         self.full = [Bar(f"full{i}", 1) for i in range(self.STAGES)]
         self.empty = [Bar(f"empty{i}", warps) for i in range(self.STAGES)]
-        self.mg_full, self.mg_empty = Bar("mg_full", warps), Bar("mg_empty", warps)
+        self.mg_full, self.mg_empty = Bar("mg_full", warps), Bar("mg_empty", hkv)
         self.mem, self.tma, self.tc = {}, [], []
 
     read = Model.read
@@ -513,16 +512,17 @@ class DecodeModel:
                 self.write(f"M{w}", seg)
                 self.mg_full.arrive()
                 yield ("step",)
-                yield ("wait", self.mg_full, seg & 1)
-                if self.plant == "release_before_read":
-                    self.mg_empty.arrive()
+                if j == 0:
+                    yield ("wait", self.mg_full, seg & 1)
+                    if self.plant == "release_before_read":
+                        self.mg_empty.arrive()
+                        yield ("step",)
+                    for jj in range(1, nsub):
+                        self.read(f"M{jj * self.hkv + h}", seg)
+                        yield ("step",)
+                    if self.plant != "release_before_read":
+                        self.mg_empty.arrive()
                     yield ("step",)
-                for jj in range(nsub):
-                    self.read(f"M{jj * self.hkv + h}", seg)
-                    yield ("step",)
-                if self.plant != "release_before_read":
-                    self.mg_empty.arrive()
-                yield ("step",)
                 seg += 1
 
     def run(self):
