@@ -181,8 +181,20 @@ struct Walker {
   int count;       // items at `level`
 };
 
-__device__ __forceinline__ int q_start(const Params& p, int s) { return p.cu ? p.cu[s] : s * p.q_len; }
-__device__ __forceinline__ int q_count(const Params& p, int s) { return p.cu ? p.cu[s + 1] - p.cu[s] : p.q_len; }
+// kRo: read cu_seqlens through the read-only data cache (they are constant
+// for the kernel's lifetime), where the few lines that every role of the
+// pair instance walks at each item boundary stay resident; the split
+// instance walks its shared-memory table and keeps plain loads.
+template <bool kRo = false>
+__device__ __forceinline__ int q_start(const Params& p, int s) {
+  if (!p.cu) return s * p.q_len;
+  return kRo ? __ldg(p.cu + s) : p.cu[s];
+}
+template <bool kRo = false>
+__device__ __forceinline__ int q_count(const Params& p, int s) {
+  if (!p.cu) return p.q_len;
+  return kRo ? __ldg(p.cu + s + 1) - __ldg(p.cu + s) : p.cu[s + 1] - p.cu[s];
+}
 
 // The walk table, built once per CTA after the dependency wait: lv[s] = the
 // number of levels of sequence s (its query tiles, or tile pairs, capped at
@@ -213,8 +225,9 @@ __device__ __forceinline__ int levels_of(const Params& p, int s) {
 // CTAs hold one item each, most at high levels, so the walk down to the end
 // dominated its tail); otherwise from cu_seqlens (the pair instance, whose
 // hot loops measured slower with the table's code in the kernel).
+template <bool kRo>
 __device__ __forceinline__ bool seq_has_pair(const Params& p, int s, int q0) {
-  return s < p.num_seqs && q_count(p, s) > q0;
+  return s < p.num_seqs && q_count<kRo>(p, s) > q0;
 }
 
 // Whether sequence s has an item at `level` (its query tiles, or pairs, reach it).
@@ -223,7 +236,7 @@ __device__ __forceinline__ bool seq_at_level(const Params& p, const WalkTable& t
   if constexpr (kTable) {
     if (t.cached()) return s < p.num_seqs && static_cast<int>(t.lv(s)) > level;
   }
-  return seq_has_pair(p, s, level * p.pair * p.tq);
+  return seq_has_pair<!kTable>(p, s, level * p.pair * p.tq);
 }
 
 // Items at one level (warp-collective).
@@ -284,9 +297,9 @@ __device__ __forceinline__ bool walker_next(const Params& p, const WalkTable& t,
   }
   it.s = s;
   it.h = idx - ord * p.hkv;
-  it.seq0 = q_start(p, s);
-  it.L = q_count(p, s);
-  it.K = p.paged ? max(p.k_lens[s], 0) : it.L;
+  it.seq0 = q_start<!kTable>(p, s);
+  it.L = q_count<!kTable>(p, s);
+  it.K = p.paged ? max(kTable ? p.k_lens[s] : __ldg(p.k_lens + s), 0) : it.L;
   it.off = it.K - it.L;
   it.q0 = q0;
   it.has1 = p.pair == 2 && it.L > q0 + p.tq;
