@@ -95,6 +95,11 @@ struct Params {
   int q_half_bytes; // stride between the two Q halves (1024-byte aligned)
   int stage_bytes;
   int big_box;      // 1: K/V maps are [D, BS, Hkv, NB] with box (64, 16, Hkv, 1)
+  // 1: one or two kv heads over blocks of a multiple of tc tokens: the K/V
+  // maps are 5-D [D, 16 tokens, Hkv, BS / 16, NB] with box
+  // (64, 16, Hkv, nsub, 1), whose rows land in the stage's order [sub-chunk
+  // j][kv head][16 tokens]: a whole unit per half per tensor in one box.
+  int unit_box;
 };
 
 // Number of stage units of a sequence, with the same clamping everywhere.
@@ -366,7 +371,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         descs[s] = d;
         // Q is read only on a sequence's first unit (kFlagFirst): load it there.
         const bool first = (flags & kFlagFirst) != 0;
-        const uint32_t bytes = static_cast<uint32_t>(__popc(act)) * (2 * kWarpBytes) + (first ? p.q_bytes : 0u);
+        const uint32_t boxes = p.unit_box ? static_cast<uint32_t>(kCWarps) : static_cast<uint32_t>(__popc(act));
+        const uint32_t bytes = boxes * (2 * kWarpBytes) + (first ? p.q_bytes : 0u);
         mbar_arrive_expect_tx(&full[s], bytes);
         if (first) {
           uint8_t* qs = st + 2 * kKVBytes;
@@ -376,7 +382,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (phys < 0) phys = -1;  // outside the pool: TMA fills zeros
-      if (p.big_box) {
+      if (p.unit_box) {
+        // Lane 0's sub-chunk 0 starts the unit, inside one block. Rows past
+        // ctx are loaded too: block data that the consumers mask (inside the
+        // last active sub-chunk) or skip (whole sub-chunks past ctx).
+        if (lane == 0) {
+          const int grp = off / kSub;
+          tma_load_5d(st, &tm_k, &full[s], 0, 0, 0, grp, phys);
+          tma_load_5d(st + kKVHalf, &tm_k, &full[s], 64, 0, 0, grp, phys);
+          tma_load_5d(st + kKVBytes, &tm_v, &full[s], 0, 0, 0, grp, phys);
+          tma_load_5d(st + kKVBytes + kKVHalf, &tm_v, &full[s], 64, 0, 0, grp, phys);
+        }
+      } else if (p.big_box) {
         if (active && head == 0) {  // one lane per sub-chunk: all kv heads in one box per half
           uint8_t* kd = st + lane * kTileBytes;
           uint8_t* vd = st + kKVBytes + lane * kTileBytes;
@@ -922,9 +939,29 @@ static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_he
     if ((st = encode_tensor_map_bf16(&tq, q, 3, dims, strides, box, true)) != LA_OK) return st;
   }
   int big_box = 0;
-  {
-    // Preferred: token axis before the head axis, so one box covers all kv
-    // heads of 16 tokens (strides need not grow with the dimension index).
+  const int nsub = 8 / num_kv_heads;
+  if (nsub >= 4 && block_size % (kSub * nsub) == 0) {
+    // A whole unit (tc = 16 * nsub tokens of every kv head) per box: the
+    // 16-token groups of a block as their own axis, after the heads, so the
+    // box's rows come in the stage's order [group][head][token]. With one
+    // kv head this replaces 32 boxes of 2 KB per stage by 4 of 16 KB (the
+    // 8-GPU KV-head-sharded rank: 109 -> 89 us per layer at B = 1024), with
+    // two 16 boxes of 4 KB (even); with four it measured slower than a box
+    // per sub-chunk.
+    const uint64_t dims[5] = {128, static_cast<uint64_t>(kSub), static_cast<uint64_t>(num_kv_heads),
+                              static_cast<uint64_t>(block_size / kSub), static_cast<uint64_t>(num_blocks)};
+    const uint64_t strides[4] = {static_cast<uint64_t>(kv_token_stride) * 2, static_cast<uint64_t>(kv_head_stride) * 2,
+                                 static_cast<uint64_t>(kv_token_stride) * 2 * kSub,
+                                 static_cast<uint64_t>(kv_block_stride) * 2};
+    const uint32_t box[5] = {64, static_cast<uint32_t>(kSub), static_cast<uint32_t>(num_kv_heads),
+                             static_cast<uint32_t>(nsub), 1};
+    if (encode_tensor_map_bf16(&tk, k_cache, 5, dims, strides, box, true) == LA_OK &&
+        encode_tensor_map_bf16(&tv, v_cache, 5, dims, strides, box, true) == LA_OK)
+      big_box = 2;
+  }
+  if (!big_box) {
+    // Token axis before the head axis, so one box covers all kv heads of 16
+    // tokens (strides need not grow with the dimension index).
     const uint64_t dims[4] = {128, static_cast<uint64_t>(block_size), static_cast<uint64_t>(num_kv_heads),
                               static_cast<uint64_t>(num_blocks)};
     const uint64_t strides[3] = {static_cast<uint64_t>(kv_token_stride) * 2, static_cast<uint64_t>(kv_head_stride) * 2,
@@ -980,7 +1017,8 @@ static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_he
   p.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + o_bytes);
   p.err = dev_error;
   // Each Q half tile starts on a 1024-byte boundary (the 128-byte swizzle atom).
-  p.big_box = big_box;
+  p.big_box = big_box == 1;
+  p.unit_box = big_box == 2;
   p.q_half_bytes = (num_q_heads * 128 + 1023) & ~1023;
   p.q_bytes = 2 * num_q_heads * 128;
   size_t smem = 0;

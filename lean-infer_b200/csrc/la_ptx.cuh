@@ -110,6 +110,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* desc, uint64_
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_5d(void* dst, const void* desc, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- PDL
 // Programmatic dependent launch: wait for the upstream grid's memory to be
 // visible (no-op when the kernel was launched without the PDL attribute).
