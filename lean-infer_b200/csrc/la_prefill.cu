@@ -353,9 +353,52 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int wg = warp >> 2;
   const float NEG_INF = -__int_as_float(0x7f800000);
 
-  grid_dependency_wait();
+  // Barriers and TMEM: they read nothing that a previous kernel writes.
+  auto setup = [&]() {
+    if (threadIdx.x == 0) {
+      mbar_init(q_full, 1);
+      mbar_init(q_empty, 1);
+      for (int i = 0; i < kStages; ++i) {
+        mbar_init(&kv_full[i], 1);
+        mbar_init(&kv_empty[i], 1);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&s_full[i], 1);
+        mbar_init(&s_free[i], 1);
+        mbar_init(&p_full[i], 128);
+        mbar_init(&o_empty[i], 128);
+        mbar_init(&st_full[i], kSplit && i == 0 ? 256 : 128);
+        if (kSplit) {
+          if (i == 0) mbar_init(o_full, 1);
+          mbar_init(&x_full[i], 128);
+          mbar_init(&x_full[i + 2], 128);
+          mbar_init(&ph_full[i], 128);
+          mbar_init(&ph_full[i + 2], 128);
+        }
+        mbar_init(&st_empty[i], 128);
+      }
+      fence_barrier_init();
+    }
+    if (warp == 12) {
+      tmem_alloc(tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+  };
   const WalkTable wt{smem};
-  if (kSplit) {
+  if constexpr (kSplit) {
+    // The split instance (a grid of fewer CTAs than SMs) sets up before the
+    // dependency wait, so with programmatic dependent launch that overlaps
+    // the previous kernel's tail; once the previous kernel's memory is
+    // visible it lets the next kernel launch: its CTAs take the idle SMs and
+    // those this grid's CTAs leave, and wait for this grid's completion
+    // before touching memory. (The pair instance, a full grid, measured
+    // slower both ways.)
+    setup();
+    grid_dependency_wait();
+    grid_launch_dependents();
     uint16_t* lv = reinterpret_cast<uint16_t*>(smem + kOffWalk + 16);
     long long* total = reinterpret_cast<long long*>(smem + kOffWalk);
     const bool cached = p.num_seqs <= kMaxSeqs && p.n_qp <= 65535;
@@ -374,46 +417,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) *total = tot * p.hkv;
     }
     __syncthreads();
-    // a CTA without work (its first item's rank is blockIdx.x) leaves before
-    // touching barriers or TMEM
-    if (static_cast<long long>(blockIdx.x) >= wt.total()) return;
-  } else {  // the same exit from one walk
+    // a CTA without work (its first item's rank is blockIdx.x) frees its
+    // TMEM and leaves
+    if (static_cast<long long>(blockIdx.x) >= wt.total()) {
+      if (warp == 12) tmem_dealloc(*tmem_slot, kTmemCols);
+      return;
+    }
+  } else {
+    grid_dependency_wait();
+    // a CTA without work (no first item) leaves before touching barriers or TMEM
     Walker w;
     walker_init<false>(p, wt, w);
     Item it;
     if (!walker_next<false>(p, wt, w, it)) return;
+    setup();
   }
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 1);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&o_empty[i], 128);
-      mbar_init(&st_full[i], kSplit && i == 0 ? 256 : 128);
-      if (kSplit) {
-        if (i == 0) mbar_init(o_full, 1);
-        mbar_init(&x_full[i], 128);
-        mbar_init(&x_full[i + 2], 128);
-        mbar_init(&ph_full[i], 128);
-        mbar_init(&ph_full[i + 2], 128);
-      }
-      mbar_init(&st_empty[i], 128);
-    }
-    fence_barrier_init();
-  }
-  if (warp == 12) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
   auto wait_all = [&](uint64_t* bar, uint32_t parity) -> bool {
