@@ -256,7 +256,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Everything below may read data written by the previous kernel in the stream.
   grid_dependency_wait();
 
+  // Producer: when the speculative split stands, its first sequence's length
+  // (from the registers) and the block ids of its first stage, loaded
+  // together with the re-read that checks the split (one round trip instead
+  // of three dependent ones before the first copy is issued).
+  bool have_first = false;
+  int ctx_first = 0, bt_first = -1;
   if (warp == kCWarps) {
+    int spec_ctx = 0, spec_bt = -1;
+    if (spec && su1 > su0) {
+      int c = 0;
+#pragma unroll
+      for (int i = 0; i < kChunks; ++i) {  // a shuffle per chunk keeps raw[] in registers
+        const int v = __shfl_sync(0xffffffffu, raw[i], sb0 & 31);
+        if (i == (sb0 >> 5)) c = v;
+      }
+      const long long cap = static_cast<long long>(p.max_blocks) * p.block_size;
+      spec_ctx = c < 0 ? 0 : (c > cap ? static_cast<int>(cap) : c);
+      const int t = static_cast<int>(su0 - spb0) * p.tc + kSub * (lane / p.hkv);
+      if (lane < kCWarps && t < spec_ctx) {
+        const int lb = t / p.block_size;
+        if (lb < p.max_blocks) spec_bt = p.block_table[static_cast<long long>(sb0) * p.bt_stride + lb];
+      }
+    }
     bool same = spec;
     if (spec) {
 #pragma unroll
@@ -303,6 +325,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       sched[2] = b0;
       sched[3] = pb0;
     }
+    if (same && su1 > su0) {
+      have_first = true;
+      ctx_first = spec_ctx;
+      bt_first = spec_bt;
+    }
   }
   __syncthreads();
   // The next kernel (the combine pass) may start its launch now; it waits for
@@ -317,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     int b = static_cast<int>(sched[2]);
     long long pb = sched[3];
-    int ctx = (n_units > 0) ? seq_ctx(p, b) : 0;
+    int ctx = (n_units > 0) ? (have_first ? ctx_first : seq_ctx(p, b)) : 0;
     int nb = units_of(ctx, p.tc);
     long long k = 0;
     for (; k < n_units; ++k) {
@@ -348,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int lb = t / p.block_size;
           off = t - lb * p.block_size;
           if (lb < p.max_blocks) {
-            phys = p.block_table[static_cast<long long>(b) * p.bt_stride + lb];
+            phys = (k == 0 && have_first) ? bt_first : p.block_table[static_cast<long long>(b) * p.bt_stride + lb];
             // Out-of-pool ids are reported; TMA zero-fills the box for them.
             if ((phys < 0 || phys >= p.num_blocks) && p.err) atomicCAS(p.err, 0, LA_DEVERR_BLOCK_ID);
           } else if (p.err) {
@@ -705,14 +732,28 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
   const long long oofs = static_cast<long long>(b) * p.out_b_stride + static_cast<long long>(hh) * p.out_h_stride +
                          lane * 4;
   float* lse = p.lse_out ? p.lse_out + static_cast<long long>(b) * p.hq + hh : nullptr;
+  // The row's CTAs cf..cl and the partial slots they wrote, also from the
+  // lengths alone (64-bit divisions), so after the wait only the loads and
+  // the merge remain: for rows over a few CTAs every slot, for the others
+  // this lane's slot of the first round of 32 (-1: no slot, or an empty
+  // range, T < G, that wrote nothing).
+  const long long cf = nb > 0 ? cta_of(Pb, T, Gl) : 0;
+  const long long cl = nb > 0 ? cta_of(Pb + nb - 1, T, Gl) : -1;
+  auto slot_of = [&](long long c) -> int {
+    const long long s0 = cta_start(c, T, Gl);
+    return s0 != cta_start(c + 1, T, Gl) ? 2 * static_cast<int>(c) + (s0 >= Pb ? 0 : 1) : -1;
+  };
+  int few[kCombineFew];
+#pragma unroll
+  for (int u = 0; u < kCombineFew; ++u)
+    few[u] = (cf < cl && cl - cf < kCombineFew && cf + u <= cl) ? slot_of(cf + u) : -1;
+  const int first_round = (cl - cf >= kCombineFew && cf + lane <= cl) ? slot_of(cf + lane) : -1;
   grid_dependency_wait();
 
   if (nb == 0) {
     for (int r = 0; r < p.nouts; ++r) *reinterpret_cast<uint2*>(p.outs[r] + oofs) = make_uint2(0u, 0u);
     if (lse && lane == 0) *lse = NEG_INF;
   } else {
-    const long long cf = cta_of(Pb, T, Gl);
-    const long long cl = cta_of(Pb + nb - 1, T, Gl);
     if (cf == cl) {  // written by the decode pass; forward it to the peers
       if (p.peer_stores) {
         const uint2 v = *reinterpret_cast<const uint2*>(p.out + oofs);
@@ -728,15 +769,11 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
       float4 ov[kCombineFew];
 #pragma unroll
       for (int u = 0; u < kCombineFew; ++u) {
-        const long long c = cf + u;
         ls[u] = NEG_INF;
-        if (c <= cl) {
-          const long long s0 = cta_start(c, T, Gl);
-          if (s0 != cta_start(c + 1, T, Gl)) {  // an empty range (T < G) wrote nothing
-            const long long slot = 2 * c + (s0 >= Pb ? 0 : 1);
-            ls[u] = p.part_lse[slot * p.hq + hh];
-            ov[u] = *reinterpret_cast<const float4*>(p.part_o + (slot * p.hq + hh) * kD + lane * 4);
-          }
+        if (few[u] >= 0) {
+          const long long slot = few[u];
+          ls[u] = p.part_lse[slot * p.hq + hh];
+          ov[u] = *reinterpret_cast<const float4*>(p.part_o + (slot * p.hq + hh) * kD + lane * 4);
         }
       }
 #pragma unroll
@@ -763,15 +800,8 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
       for (long long c0 = cf; c0 <= cl; c0 += 32) {
         const long long c = c0 + lane;
-        int slot = -1;
-        float ls = NEG_INF;
-        if (c <= cl) {
-          const long long s0 = cta_start(c, T, Gl);
-          if (s0 != cta_start(c + 1, T, Gl)) {  // an empty range (T < G) wrote nothing
-            slot = 2 * static_cast<int>(c) + (s0 >= Pb ? 0 : 1);
-            ls = p.part_lse[static_cast<long long>(slot) * p.hq + hh];
-          }
-        }
+        const int slot = c0 == cf ? first_round : (c <= cl ? slot_of(c) : -1);
+        const float ls = slot >= 0 ? p.part_lse[static_cast<long long>(slot) * p.hq + hh] : NEG_INF;
         const float mr = warp_max_all(ls);
         if (mr == NEG_INF) continue;  // warp-uniform: no keys in this round
         const float mn = fmaxf(m, mr);
