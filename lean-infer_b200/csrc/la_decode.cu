@@ -19,8 +19,8 @@
 // (written as fp32 (O, lse) partials to the workspace and merged by the
 // combine kernel).
 //
-// CTA: warp 8 is the producer (partition walk, block-table lookups, TMA
-// issue); warps 0-7 consume. Consumer warp w handles kv head w % Hkv and the
+// CTA: warps 8 and 9 are the producers (partition walk, block-table lookups,
+// TMA issue), taking even and odd units in turn; warps 0-7 consume. Consumer warp w handles kv head w % Hkv and the
 // 16-token sub-chunk w / Hkv of each stage: S^T = K Q^T and O^T += V^T P^T on
 // mma.m16n8k16 (bf16 in, fp32 accumulate) with K/V fragments read by ldmatrix
 // from 128-byte-swizzled TMA tiles, online softmax in fp32 with warp-shuffle
@@ -40,7 +40,8 @@ namespace decode {
 constexpr int kD = 128;
 constexpr int kSub = 16;                 // tokens per consumer warp per stage (MMA M)
 constexpr int kCWarps = 8;               // consumer warps
-constexpr int kThreads = (kCWarps + 1) * 32;
+constexpr int kMaxProducers = 2;  // producer warps (units alternate between them); the launch picks 1 or 2
+constexpr int kThreads = (kCWarps + kMaxProducers) * 32;
 constexpr int kTileBytes = kSub * 128;   // 16 rows x 64 dims bf16 (one swizzle-128B tile)
 constexpr int kWarpBytes = 2 * kTileBytes;
 constexpr int kKVHalf = kCWarps * kTileBytes;   // one 64-dim half of all warps' tiles: 16 KB
@@ -72,6 +73,8 @@ struct Params {
   int batch;
   int hq, hkv, group, nsub;  // nsub = 8 / hkv consumer warps per kv head
   int block_size;
+  int bs_shift;              // log2(block_size) when it is a power of two, else -1
+  int tc_shift;              // log2(tc)
   long long num_blocks;
   int tc;                    // tokens per stage
   float scale_log2;
@@ -114,6 +117,13 @@ __device__ __forceinline__ int seq_ctx(const Params& p, int b) {
   return c;
 }
 __device__ __forceinline__ int units_of(int ctx, int tc) { return (ctx + tc - 1) / tc; }
+// Division by the block size and the unit size on the producer's per-unit
+// path: shifts (a division by a run-time value is a dependent chain of about
+// twenty instructions, and the producer paced the pipeline at one kv head).
+__device__ __forceinline__ int div_bs(const Params& p, int x) {
+  return p.bs_shift >= 0 ? (x >> p.bs_shift) : (x / p.block_size);
+}
+__device__ __forceinline__ int units_p(const Params& p, int ctx) { return (ctx + p.tc - 1) >> p.tc_shift; }
 
 __device__ __forceinline__ float warp_max_g(float v) {
   // max over the 8 lanes that share lane % 4
@@ -142,51 +152,75 @@ __device__ long long total_units(const Params& p, int lane) {
   return tot;
 }
 
-// The split for up to 32 x kChunks sequences from their lengths held in registers
-// (lane l holds sequences 32 i + l): total units T, this CTA's range [u0, u1),
-// the sequence b0 it starts in and that sequence's first unit pb0.
+// The split for up to 32 x kChunks sequences from their lengths held in
+// registers, lane l holding the kChunks consecutive sequences l * kChunks + i:
+// total units T, this CTA's range [u0, u1), the sequence b0 it starts in and
+// that sequence's first unit pb0. Each lane sums its own sequences, one warp
+// scan orders the lanes, and the lane whose sequences hold unit u0 walks its
+// registers (a scan per 32 sequences, one after another, took 18k clocks at
+// 1024 sequences before the first copy could be issued).
 __device__ __forceinline__ long long cta_start(long long c, long long T, long long G);
 template <int kChunks>
 __device__ __forceinline__ void split_from_regs(const Params& p, int lane, const int (&un)[kChunks], long long& T,
                                                 long long& u0, long long& u1, int& b0, long long& pb0) {
-  const int chunks = (p.batch + 31) >> 5;
-  T = 0;
+  long long own = 0;
 #pragma unroll
-  for (int i = 0; i < kChunks; ++i) {
-    if (i < chunks) {
-      int n = un[i];
+  for (int i = 0; i < kChunks; ++i) own += un[i];
+  long long incl = own;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
-      T += n;
-    }
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
   }
+  const long long excl = incl - own;
+  T = __shfl_sync(0xffffffffu, incl, 31);
   const long long G = gridDim.x;
   u0 = cta_start(blockIdx.x, T, G);
   u1 = cta_start(blockIdx.x + 1, T, G);
   b0 = p.batch;
   pb0 = T;
   if (u1 <= u0) return;
-  long long acc = 0;
+  const unsigned hit = __ballot_sync(0xffffffffu, excl <= u0 && u0 < incl);
+  const int src = __ffs(hit) - 1;  // u0 < T, so exactly one lane holds it
+  int bl = 0;
+  long long pbl = 0;
+  if (lane == src) {
+    long long acc = excl;
+    bool found = false;
 #pragma unroll
-  for (int i = 0; i < kChunks; ++i) {
-    if (i < chunks) {
-      const int b = i * 32 + lane;
-      const int n = un[i];
-      int incl = n;
+    for (int i = 0; i < kChunks; ++i) {
+      if (!found && u0 < acc + un[i]) {
+        found = true;
+        bl = lane * kChunks + i;
+        pbl = acc;
+      }
+      acc += un[i];
+    }
+  }
+  b0 = __shfl_sync(0xffffffffu, bl, src);
+  pb0 = __shfl_sync(0xffffffffu, pbl, src);
+}
+
+// The lengths of sequences lane * kChunks + i (0 past the batch), read
+// through L2 only; 16-byte loads where the run is aligned and inside the
+// batch.
+template <int kChunks>
+__device__ __forceinline__ void load_lens(const Params& p, int lane, int (&raw)[kChunks]) {
+  static_assert(kChunks % 4 == 0, "lengths are loaded four at a time");
+  const int b0 = lane * kChunks;
+  const bool vec = (reinterpret_cast<uintptr_t>(p.seqlens) & 15) == 0;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const long long end = acc + incl;
-      const unsigned hit = __ballot_sync(0xffffffffu, b < p.batch && end > u0);
-      if (hit) {
-        const int src = __ffs(hit) - 1;
-        b0 = i * 32 + src;
-        pb0 = acc + __shfl_sync(0xffffffffu, incl, src) - __shfl_sync(0xffffffffu, n, src);
-        return;
-      }
-      acc += __shfl_sync(0xffffffffu, incl, 31);
+  for (int v = 0; v < kChunks / 4; ++v) {
+    const int b = b0 + 4 * v;
+    if (vec && b + 3 < p.batch) {
+      const int4 x = __ldcg(reinterpret_cast<const int4*>(p.seqlens + b));
+      raw[4 * v] = x.x;
+      raw[4 * v + 1] = x.y;
+      raw[4 * v + 2] = x.z;
+      raw[4 * v + 3] = x.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) raw[4 * v + e] = (b + e < p.batch) ? __ldcg(p.seqlens + b + e) : 0;
     }
   }
 }
@@ -202,7 +236,8 @@ __device__ __forceinline__ long long cta_of(long long x, long long T, long long 
 template <int kStages, int kChunks>
 __global__ void __launch_bounds__(kThreads, 1)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                        const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_k1,
+                        const __grid_constant__ CUtensorMap tm_v1, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ctrl = smem + kStages * p.stage_bytes;
@@ -241,13 +276,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   int raw[kChunks];
   long long sT = 0, su0 = 0, su1 = 0, spb0 = 0;
   int sb0 = 0;
-  if (warp == kCWarps && spec) {
+  if (warp >= kCWarps && spec) {
     int un[kChunks];
     const long long cap = static_cast<long long>(p.max_blocks) * p.block_size;
+    load_lens(p, lane, raw);
 #pragma unroll
     for (int i = 0; i < kChunks; ++i) {
-      const int b = i * 32 + lane;
-      raw[i] = (b < p.batch) ? __ldcg(p.seqlens + b) : 0;
       const long long c = raw[i] < 0 ? 0 : (raw[i] > cap ? cap : raw[i]);
       un[i] = units_of(static_cast<int>(c), p.tc);
     }
@@ -256,36 +290,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Everything below may read data written by the previous kernel in the stream.
   grid_dependency_wait();
 
-  // Producer: when the speculative split stands, its first sequence's length
-  // (from the registers) and the block ids of its first stage, loaded
-  // together with the re-read that checks the split (one round trip instead
-  // of three dependent ones before the first copy is issued).
-  bool have_first = false;
-  int ctx_first = 0, bt_first = -1;
-  if (warp == kCWarps) {
-    int spec_ctx = 0, spec_bt = -1;
+  // Producer lookups go through two windows held across its 32 lanes, so
+  // that a unit's copies wait on no global load in the common case: lane i
+  // holds the (clamped) length of sequence sb + i, and the raw block id of
+  // block wl + i of sequence bb. Entering a sequence also loads the first 32
+  // block ids of the next one, which are read at the next sequence change
+  // (with one kv head a sequence is ~6 units, and two dependent global round
+  // trips per unit made the producer the slowest part of the pipeline). The
+  // windows of the first sequence are loaded with the speculative split,
+  // together with the re-read that checks it.
+  int sb = 0, swin = 0, bb = -1, wl = 0, bwin = -1;
+  auto load_swin = [&](int base) {
+    sb = base;
+    swin = (sb + lane < p.batch) ? seq_ctx(p, sb + lane) : 0;
+  };
+  auto load_bwin = [&](int seq, int first) {
+    bb = seq;
+    wl = first;
+    bwin = (seq < p.batch && wl + lane < p.max_blocks)
+               ? p.block_table[static_cast<long long>(seq) * p.bt_stride + wl + lane]
+               : -1;
+  };
+  if (warp >= kCWarps) {
     if (spec && su1 > su0) {
-      int c = 0;
-#pragma unroll
-      for (int i = 0; i < kChunks; ++i) {  // a shuffle per chunk keeps raw[] in registers
-        const int v = __shfl_sync(0xffffffffu, raw[i], sb0 & 31);
-        if (i == (sb0 >> 5)) c = v;
-      }
-      const long long cap = static_cast<long long>(p.max_blocks) * p.block_size;
-      spec_ctx = c < 0 ? 0 : (c > cap ? static_cast<int>(cap) : c);
-      const int t = static_cast<int>(su0 - spb0) * p.tc + kSub * (lane / p.hkv);
-      if (lane < kCWarps && t < spec_ctx) {
-        const int lb = t / p.block_size;
-        if (lb < p.max_blocks) spec_bt = p.block_table[static_cast<long long>(sb0) * p.bt_stride + lb];
-      }
+      load_swin(sb0);
+      load_bwin(sb0, static_cast<int>((su0 - spb0) * p.tc / p.block_size));
     }
     bool same = spec;
     if (spec) {
+      int now[kChunks];
+      load_lens(p, lane, now);
 #pragma unroll
-      for (int i = 0; i < kChunks; ++i) {
-        const int b = i * 32 + lane;
-        if (b < p.batch && __ldcg(p.seqlens + b) != raw[i]) same = false;
-      }
+      for (int i = 0; i < kChunks; ++i)
+        if (now[i] != raw[i]) same = false;
       same = __all_sync(0xffffffffu, same);
     }
     // Partition: this CTA's unit range and the sequence it starts in.
@@ -318,17 +355,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         acc += __shfl_sync(0xffffffffu, incl, 31);
       }
+      if (u1 > u0 && b0 < p.batch) {
+        load_swin(b0);
+        load_bwin(b0, static_cast<int>((u0 - pb0) * p.tc / p.block_size));
+      }
     }
-    if (lane == 0) {
+    if (warp == kCWarps && lane == 0) {
       sched[0] = u0;
       sched[1] = (u1 > u0) ? u1 : u0;
       sched[2] = b0;
       sched[3] = pb0;
-    }
-    if (same && su1 > su0) {
-      have_first = true;
-      ctx_first = spec_ctx;
-      bt_first = spec_bt;
     }
   }
   __syncthreads();
@@ -340,47 +376,83 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long n_units = sched[1] - sched[0];
   const int hkv = p.hkv;
 
-  if (warp == kCWarps) {
-    // ------------------------------------------------------------ producer
+  if (warp >= kCWarps) {
+    // ------------------------------------------------------------ producers
+    // Producer pid issues units k = pid, pid + nprod, ...; every producer
+    // walks every unit to follow the sequences. One warp's per-unit path
+    // (stage wait, descriptor, four TMA boxes whose issue alone takes ~650
+    // clocks) paced the pipeline when sequences are short; two alternate.
+    const int pid = warp - kCWarps;
+    const int nprod = static_cast<int>(blockDim.x >> 5) - kCWarps;
+    const int nu = static_cast<int>(n_units);
     int b = static_cast<int>(sched[2]);
-    long long pb = sched[3];
-    int ctx = (n_units > 0) ? (have_first ? ctx_first : seq_ctx(p, b)) : 0;
-    int nb = units_of(ctx, p.tc);
-    long long k = 0;
-    for (; k < n_units; ++k) {
-      const long long u = u0 + k;
-      while (u >= pb + nb && b + 1 < p.batch) {
-        pb += nb;
+    int uis = static_cast<int>(u0 - sched[3]);  // unit of the current sequence at k
+    int seq_k0 = -uis;                          // k of the current sequence's unit 0
+    int ctx = (nu > 0) ? __shfl_sync(0xffffffffu, swin, 0) : 0;
+    int nb = units_p(p, ctx);
+    int nbb = -1, nbwin = -1;  // the next sequence's first block ids
+    // This lane's warp slot (lanes 0..7): sub-chunk jl, kv head hl.
+    const int jl = (lane < kCWarps) ? lane / hkv : 0;
+    const int hl = (lane < kCWarps) ? lane - jl * hkv : 0;
+    int k = 0;
+    for (; k < nu; ++k, ++uis) {
+      while (uis >= nb && b + 1 < p.batch) {
         ++b;
-        ctx = seq_ctx(p, b);
-        nb = units_of(ctx, p.tc);
+        uis = 0;
+        seq_k0 = k;
+        if (b - sb >= 32) load_swin(b);
+        ctx = __shfl_sync(0xffffffffu, swin, b - sb);
+        nb = units_p(p, ctx);
       }
-      if (u >= pb + nb) break;  // seqlens changed under the kernel: stop issuing
-      const int s = static_cast<int>(k % kStages);
+      if (uis >= nb) break;  // seqlens changed under the kernel: stop issuing
+      if (k % nprod != pid) continue;
+      const int tok0 = uis * p.tc;
+      {
+        // Blocks of this unit's sub-chunks that hold keys: [lbf, lbl].
+        const int lbf = div_bs(p, tok0);
+        const int lbl = div_bs(p, min(tok0 + p.tc, ctx) - 1);
+        if (bb != b || lbf < wl || lbl >= wl + 32) {
+          if (b == nbb && lbf == 0 && lbl < 32) {
+            bb = b;
+            wl = 0;
+            bwin = nbwin;
+          } else {
+            load_bwin(b, lbf);
+          }
+        }
+        if (nbb <= b) {  // read at the next sequence change, not before
+          nbb = b + 1;
+          nbwin = (nbb < p.batch && lane < p.max_blocks)
+                      ? p.block_table[static_cast<long long>(nbb) * p.bt_stride + lane]
+                      : -1;
+        }
+      }
+      const int s = k % kStages;
       const uint32_t ph = static_cast<uint32_t>((k / kStages) & 1);
       if (!mbar_wait(&empty[s], ph ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) break;
-      const int uis = static_cast<int>(u - pb);
-      const int tok0 = uis * p.tc;
       uint8_t* st = smem + s * p.stage_bytes;
 
       // Sub-chunk of warp-slot `lane` (lanes 0..7).
       bool active = false;
-      int phys = -1, off = 0, head = 0;
+      int phys = -1, off = 0, head = 0, lb = 0;
       if (lane < kCWarps) {
-        const int j = lane / hkv;
-        head = lane - j * hkv;
-        const int t = tok0 + kSub * j;
+        head = hl;
+        const int t = tok0 + kSub * jl;
         if (t < ctx) {
           active = true;
-          const int lb = t / p.block_size;
+          lb = div_bs(p, t);
           off = t - lb * p.block_size;
-          if (lb < p.max_blocks) {
-            phys = (k == 0 && have_first) ? bt_first : p.block_table[static_cast<long long>(b) * p.bt_stride + lb];
-            // Out-of-pool ids are reported; TMA zero-fills the box for them.
-            if ((phys < 0 || phys >= p.num_blocks) && p.err) atomicCAS(p.err, 0, LA_DEVERR_BLOCK_ID);
-          } else if (p.err) {
-            atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
-          }
+        }
+      }
+      // every lane takes part in the shuffle; inactive ones read lane 0
+      const int id = __shfl_sync(0xffffffffu, bwin, active ? lb - wl : 0);
+      if (active) {
+        if (lb < p.max_blocks) {
+          phys = id;
+          // Out-of-pool ids are reported; TMA zero-fills the box for them.
+          if ((phys < 0 || phys >= p.num_blocks) && p.err) atomicCAS(p.err, 0, LA_DEVERR_BLOCK_ID);
+        } else if (p.err) {
+          atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);
         }
       }
       const unsigned act = __ballot_sync(0xffffffffu, active);
@@ -391,14 +463,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         d.ctx = ctx;
         int flags = 0;
         if (k == 0 || uis == 0) flags |= kFlagFirst;
-        if (k == n_units - 1 || uis == nb - 1) flags |= kFlagLast;
-        if (pb >= u0 && pb + nb <= u0 + n_units) flags |= kFlagWhole;
+        if (k == nu - 1 || uis == nb - 1) flags |= kFlagLast;
+        if (seq_k0 >= 0 && seq_k0 + nb <= nu) flags |= kFlagWhole;
         d.flags = flags;
-        d.slot = 2 * static_cast<int>(blockIdx.x) + (pb <= u0 ? 0 : 1);
+        d.slot = 2 * static_cast<int>(blockIdx.x) + (seq_k0 <= 0 ? 0 : 1);
         descs[s] = d;
         // Q is read only on a sequence's first unit (kFlagFirst): load it there.
         const bool first = (flags & kFlagFirst) != 0;
-        const uint32_t boxes = p.unit_box ? static_cast<uint32_t>(kCWarps) : static_cast<uint32_t>(__popc(act));
+        const bool whole_unit = tok0 + p.tc <= ctx;
+        const uint32_t boxes =
+            (p.unit_box && whole_unit) ? static_cast<uint32_t>(kCWarps) : static_cast<uint32_t>(__popc(act));
         const uint32_t bytes = boxes * (2 * kWarpBytes) + (first ? p.q_bytes : 0u);
         mbar_arrive_expect_tx(&full[s], bytes);
         if (first) {
@@ -409,26 +483,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (phys < 0) phys = -1;  // outside the pool: TMA fills zeros
-      if (p.unit_box) {
-        // Lane 0's sub-chunk 0 starts the unit, inside one block. Rows past
-        // ctx are loaded too: block data that the consumers mask (inside the
-        // last active sub-chunk) or skip (whole sub-chunks past ctx).
-        if (lane == 0) {
+      // The four boxes of a sub-chunk (K and V, two 64-dim halves each) are
+      // issued by four lanes in one instruction rather than one lane in four.
+      const int piece = lane & 3;
+      const int tens = piece >> 1, half = piece & 1;
+      if (p.unit_box && tok0 + p.tc <= ctx) {
+        // Lane 0's sub-chunk 0 starts the unit, inside one block.
+        const int ph0 = __shfl_sync(0xffffffffu, phys, 0);
+        const int grp = __shfl_sync(0xffffffffu, off, 0) / kSub;
+        if (lane < 4)
+          tma_load_5d(st + tens * kKVBytes + half * kKVHalf, tens ? &tm_v : &tm_k, &full[s], half * 64, 0, 0, grp,
+                      ph0);
+      } else if (p.unit_box) {
+        // A sequence's last unit, not full: only the sub-chunks that hold
+        // keys, one box [64 dims, 16 tokens, Hkv heads] per half per tensor
+        // each (the whole-unit box would read up to 7/8 of a unit of rows
+        // past ctx: 8.5 % more bytes at one kv head over U[512, 1024]).
+        // Rows past ctx inside the last active sub-chunk are loaded and
+        // masked by its consumers; sub-chunks past ctx are neither loaded
+        // nor read.
+        if (active && head == 0) {
           const int grp = off / kSub;
-          tma_load_5d(st, &tm_k, &full[s], 0, 0, 0, grp, phys);
-          tma_load_5d(st + kKVHalf, &tm_k, &full[s], 64, 0, 0, grp, phys);
-          tma_load_5d(st + kKVBytes, &tm_v, &full[s], 0, 0, 0, grp, phys);
-          tma_load_5d(st + kKVBytes + kKVHalf, &tm_v, &full[s], 64, 0, 0, grp, phys);
-        }
-      } else if (p.big_box) {
-        if (active && head == 0) {  // one lane per sub-chunk: all kv heads in one box per half
           uint8_t* kd = st + lane * kTileBytes;
           uint8_t* vd = st + kKVBytes + lane * kTileBytes;
-          tma_load_4d(kd, &tm_k, &full[s], 0, off, 0, phys);
-          tma_load_4d(kd + kKVHalf, &tm_k, &full[s], 64, off, 0, phys);
-          tma_load_4d(vd, &tm_v, &full[s], 0, off, 0, phys);
-          tma_load_4d(vd + kKVHalf, &tm_v, &full[s], 64, off, 0, phys);
+          tma_load_5d(kd, &tm_k1, &full[s], 0, 0, 0, grp, phys);
+          tma_load_5d(kd + kKVHalf, &tm_k1, &full[s], 64, 0, 0, grp, phys);
+          tma_load_5d(vd, &tm_v1, &full[s], 0, 0, 0, grp, phys);
+          tma_load_5d(vd + kKVHalf, &tm_v1, &full[s], 64, 0, 0, grp, phys);
         }
+      } else if (p.big_box) {
+        // Sub-chunk j (all kv heads in one box per half, the lane of its head
+        // 0 holding id and offset) is issued by lanes 4j .. 4j + 3.
+        const int jj = lane >> 2;
+        const int src = (jj < p.nsub ? jj : 0) * hkv;
+        const int sph = __shfl_sync(0xffffffffu, phys, src);
+        const int sof = __shfl_sync(0xffffffffu, off, src);
+        const bool sact = __shfl_sync(0xffffffffu, active ? 1 : 0, src) != 0;
+        if (jj < p.nsub && sact)
+          tma_load_4d(st + tens * kKVBytes + half * kKVHalf + src * kTileBytes, tens ? &tm_v : &tm_k, &full[s],
+                      half * 64, sof, 0, sph);
       } else if (active) {
         uint8_t* kd = st + lane * kTileBytes;
         uint8_t* vd = st + kKVBytes + lane * kTileBytes;
@@ -438,11 +531,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(vd + kKVHalf, &tm_v, &full[s], 64, head, off, phys);
       }
     }
-    // On an early exit, let the copies already issued land before the CTA
+    // On an early exit, let the copies this warp issued land before the CTA
     // releases its shared memory (bounded).
-    if (k < n_units) {
-      for (long long kk = (k > kStages ? k - kStages : 0); kk < k; ++kk)
-        mbar_wait(&full[kk % kStages], static_cast<uint32_t>((kk / kStages) & 1), nullptr, 0);
+    if (k < nu) {
+      for (int kk = (k > kStages ? k - kStages : 0); kk < k; ++kk)
+        if (kk % nprod == pid) mbar_wait(&full[kk % kStages], static_cast<uint32_t>((kk / kStages) & 1), nullptr, 0);
     }
     return;
   }
@@ -460,10 +553,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   float o[8][4];
   float m0 = NEG_INF, m1 = NEG_INF, l0 = 0.f, l1 = 0.f;
   uint32_t qf[8][2];
-  long long seg_ends = 0;  // segment ends seen (phase of the merge barriers)
+  int seg_ends = 0;  // segment ends seen (phase of the merge barriers)
 
-  for (long long k = 0; k < n_units; ++k) {
-    const int s = static_cast<int>(k % kStages);
+  const int nu = static_cast<int>(n_units);
+  for (int k = 0; k < nu; ++k) {
+    const int s = k % kStages;
     const uint32_t ph = static_cast<uint32_t>((k / kStages) & 1);
     if (!mbar_wait(&full[s], ph, p.err, LA_DEVERR_WAIT_TIMEOUT)) return;
     const StageDesc d = descs[s];
@@ -580,10 +674,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool writer = true;
       if (p.nsub > 1) {
         // Several warps hold partial states of the same kv head (one per
-        // sub-chunk j). Merge them in shared memory into warp j = 0 so every
-        // segment leaves one state per head, as with nsub == 1.
+        // sub-chunk j). They park them in shared memory and one of them
+        // merges them, so every segment leaves one state per head, as with
+        // nsub == 1. The merging warp rotates with the segment end (j =
+        // seg_ends % nsub), so the merges of a CTA's many short sequences
+        // (the KV-head-sharded rank crosses ~7 per CTA) are shared by the
+        // warps instead of all landing on j = 0, whose lag held back every
+        // stage's release. The merger folds the states in sub-chunk order
+        // 0, 1, ..., nsub-1 whoever it is, so the result does not depend on
+        // which warp merges.
         const int TQ = (G + 1) >> 1;  // lanes (per g) that hold real columns
         const uint32_t par = static_cast<uint32_t>(seg_ends & 1);
+        const int jm = seg_ends & (p.nsub - 1);  // nsub is a power of two
         if (!mbar_wait(mg_empty, par ^ 1u, p.err, LA_DEVERR_WAIT_TIMEOUT)) return;
         if (tq < TQ) {
           float* slot = merge + ((w * TQ + tq) * 8 + g) * 36;
@@ -598,10 +700,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(mg_full);
-        writer = (j == 0);
+        writer = (j == jm);
         if (writer) {
           if (!mbar_wait(mg_full, par, p.err, LA_DEVERR_WAIT_TIMEOUT)) return;
           if (tq < TQ) {
+            if (jm != 0) {  // start from sub-chunk 0's state (this warp's own is in its slot)
+              const float* sl = merge + ((h * TQ + tq) * 8 + g) * 36;
+              m0 = sl[0];
+              m1 = sl[1];
+              L0 = sl[2];
+              L1 = sl[3];
+#pragma unroll
+              for (int mt = 0; mt < 8; ++mt)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) o[mt][r] = sl[4 + mt * 4 + r];
+            }
             for (int jj = 1; jj < p.nsub; ++jj) {
               const float* sl = merge + (((jj * hkv + h) * TQ + tq) * 8 + g) * 36;
               const float om0 = sl[0], om1 = sl[1], oL0 = sl[2], oL1 = sl[3];
@@ -713,19 +826,37 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
   // T (all units) and P_b (units before sequence b). They depend only on
   // cache_seqlens, which were final before the decode grid started (it does
   // not write them), so they are computed while that grid still runs; every
-  // CTA waits for it before touching outputs or partials.
+  // CTA waits for it before touching outputs or partials. Each lane sums its
+  // own sequences (lane + 32 i, coalesced, 16 independent loads at a time)
+  // and two warp sums finish: a round trip per 512 sequences. (A warp sum
+  // after every 32 sequences, one round trip each, took ~15 us at 1024
+  // sequences, and the combine CTAs that launch only as decode CTAs leave
+  // run it after the decode grid.)
   long long T = 0, Pb = 0;
-  for (int base = 0; base < p.batch; base += 32) {
-    const int bb = base + lane;
-    int n = (bb < p.batch) ? units_of(seq_ctx(p, bb), p.tc) : 0;
-    int nb = (bb < b) ? n : 0;
+  {
+    constexpr int kLoads = 16;
+    int own = 0, before = 0;
+    for (int base = 0; base < p.batch; base += 32 * kLoads) {
+      int n[kLoads];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      n += __shfl_xor_sync(0xffffffffu, n, o);
-      nb += __shfl_xor_sync(0xffffffffu, nb, o);
+      for (int k = 0; k < kLoads; ++k) {
+        const int bb = base + 32 * k + lane;
+        n[k] = (bb < p.batch) ? units_of(seq_ctx(p, bb), p.tc) : 0;
+      }
+#pragma unroll
+      for (int k = 0; k < kLoads; ++k) {
+        own += n[k];
+        if (base + 32 * k + lane < b) before += n[k];
+      }
     }
-    T += n;
-    Pb += nb;
+    long long o = own, bf = before;
+#pragma unroll
+    for (int x = 16; x > 0; x >>= 1) {
+      o += __shfl_xor_sync(0xffffffffu, o, x);
+      bf += __shfl_xor_sync(0xffffffffu, bf, x);
+    }
+    T = o;
+    Pb = bf;
   }
   const int nb = units_of(seq_ctx(p, b), p.tc);
   const long long Gl = grid;
@@ -961,7 +1092,7 @@ static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_he
   if (st != LA_OK) return st;
   if (!workspace || workspace_bytes < need || !aligned(workspace, 256)) return LA_ERR_WORKSPACE;
 
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, tk1, tv1;
   {
     const uint64_t dims[3] = {128, static_cast<uint64_t>(num_q_heads), static_cast<uint64_t>(batch)};
     const uint64_t strides[2] = {static_cast<uint64_t>(q_head_stride) * 2, static_cast<uint64_t>(q_batch_stride) * 2};
@@ -985,8 +1116,13 @@ static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_he
                                  static_cast<uint64_t>(kv_block_stride) * 2};
     const uint32_t box[5] = {64, static_cast<uint32_t>(kSub), static_cast<uint32_t>(num_kv_heads),
                              static_cast<uint32_t>(nsub), 1};
+    // The same layout with one 16-token group per box, for a sequence's
+    // last unit when it is not full.
+    const uint32_t box1[5] = {64, static_cast<uint32_t>(kSub), static_cast<uint32_t>(num_kv_heads), 1, 1};
     if (encode_tensor_map_bf16(&tk, k_cache, 5, dims, strides, box, true) == LA_OK &&
-        encode_tensor_map_bf16(&tv, v_cache, 5, dims, strides, box, true) == LA_OK)
+        encode_tensor_map_bf16(&tv, v_cache, 5, dims, strides, box, true) == LA_OK &&
+        encode_tensor_map_bf16(&tk1, k_cache, 5, dims, strides, box1, true) == LA_OK &&
+        encode_tensor_map_bf16(&tv1, v_cache, 5, dims, strides, box1, true) == LA_OK)
       big_box = 2;
   }
   if (!big_box) {
@@ -1010,6 +1146,10 @@ static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_he
     if ((st = encode_tensor_map_bf16(&tk, k_cache, 4, dims, strides, box, true)) != LA_OK) return st;
     if ((st = encode_tensor_map_bf16(&tv, v_cache, 4, dims, strides, box, true)) != LA_OK) return st;
   }
+  if (big_box != 2) {  // the one-group maps are read only with whole-unit boxes
+    tk1 = tk;
+    tv1 = tv;
+  }
 
   Params p;
   p.seqlens = cache_seqlens;
@@ -1022,8 +1162,10 @@ static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_he
   p.group = group;
   p.nsub = 8 / num_kv_heads;
   p.block_size = block_size;
+  p.bs_shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctz(static_cast<unsigned>(block_size)) : -1;
   p.num_blocks = num_blocks;
   p.tc = kSub * p.nsub;
+  p.tc_shift = __builtin_ctz(static_cast<unsigned>(p.tc));
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_b_stride = out_batch_stride;
@@ -1056,13 +1198,17 @@ static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_he
   const int stages = stages_for(2 * p.q_half_bytes, merge_bytes, &p.stage_bytes, &smem);
   if (stages == 0) return LA_ERR_UNSUPPORTED;
 
+  // A second producer warp pays off once units are many per CTA (at 1024
+  // one-kv-head rows it took the pipeline off the producer's path); with a
+  // few short sequences (B = 8) the extra warp measured slower.
+  const int threads = (kCWarps + (batch >= 16 ? 2 : 1)) * 32;
   cudaError_t e;
   if (stages == 3)
-    e = batch <= 256 ? launch_pdl(paged_decode_kernel<3, 8>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p)
-                     : launch_pdl(paged_decode_kernel<3, 32>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p);
+    e = batch <= 256 ? launch_pdl(paged_decode_kernel<3, 8>, dim3(grid), dim3(threads), smem, stream, tq, tk, tv, tk1, tv1, p)
+                     : launch_pdl(paged_decode_kernel<3, 32>, dim3(grid), dim3(threads), smem, stream, tq, tk, tv, tk1, tv1, p);
   else
-    e = batch <= 256 ? launch_pdl(paged_decode_kernel<2, 8>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p)
-                     : launch_pdl(paged_decode_kernel<2, 32>, dim3(grid), dim3(kThreads), smem, stream, tq, tk, tv, p);
+    e = batch <= 256 ? launch_pdl(paged_decode_kernel<2, 8>, dim3(grid), dim3(threads), smem, stream, tq, tk, tv, tk1, tv1, p)
+                     : launch_pdl(paged_decode_kernel<2, 32>, dim3(grid), dim3(threads), smem, stream, tq, tk, tv, tk1, tv1, p);
   if (e != cudaSuccess) return cuda_status(e);
   e = launch_pdl(paged_decode_combine_kernel, dim3(batch, num_q_heads), dim3(32), 0, stream, p, grid);
   return cuda_status(e);

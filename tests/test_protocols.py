@@ -463,16 +463,19 @@ def test_pair_planted_mistakes_are_caught(plant):
 
 class DecodeModel:
     """The decode kernel's stage ring and sub-chunk merge
-    (lean-infer_b200/csrc/la_decode.cu, paged_decode_kernel): the producer
-    warp waits a stage's empty barrier (one arrival per consumer warp), writes
+    (lean-infer_b200/csrc/la_decode.cu, paged_decode_kernel): two producer
+    warps take the even and the odd units; for each of its units a producer
+    waits the stage's empty barrier (one arrival per consumer warp), writes
     the stage descriptor into shared memory and starts its copies; consumer
     warps wait the full barrier, read descriptor and tiles, release the stage;
-    at each segment end the warps of sub-chunks j > 0 leave their softmax
-    state in a merge slot (after the previous merge was read: mg_empty, one
-    arrival per kv head) and warp j = 0 of each kv head reads them once all
-    warps have written (mg_full, one arrival per warp)."""
+    at each segment end every sub-chunk warp leaves its softmax state in a
+    merge slot (after the previous merge was read: mg_empty, one arrival per
+    kv head) and the merging warp of each kv head, j = (segment end) % nsub,
+    reads the slots in sub-chunk order once all warps have written (mg_full,
+    one arrival per warp)."""
 
     STAGES = 3
+    PRODUCERS = 2
 
     def __init__(self, units, seg_ends, hkv, warps, rng, plant=None):
         self.units, self.ends, self.hkv, self.warps = units, seg_ends, hkv, warps
@@ -485,8 +488,8 @@ class DecodeModel:
     read = Model.read
     write = Model.write
 
-    def producer(self):
-        for k in range(self.units):
+    def producer(self, pid=0, nprod=1):
+        for k in range(pid, self.units, nprod):
             s = k % self.STAGES
             yield ("wait", self.empty[s], ((k // self.STAGES) & 1) ^ 1)
             self.write(f"D{s}", k)
@@ -507,17 +510,18 @@ class DecodeModel:
             self.empty[s].arrive()
             yield ("step",)
             if k in self.ends and nsub > 1:
-                if not (self.plant == "no_mg_empty_wait" and j > 0):
+                jm = seg % nsub
+                if not (self.plant == "no_mg_empty_wait" and j != jm):
                     yield ("wait", self.mg_empty, (seg & 1) ^ 1)
                 self.write(f"M{w}", seg)
                 self.mg_full.arrive()
                 yield ("step",)
-                if j == 0:
+                if j == jm:
                     yield ("wait", self.mg_full, seg & 1)
                     if self.plant == "release_before_read":
                         self.mg_empty.arrive()
                         yield ("step",)
-                    for jj in range(1, nsub):
+                    for jj in range(0 if jm else 1, nsub):
                         self.read(f"M{jj * self.hkv + h}", seg)
                         yield ("step",)
                     if self.plant != "release_before_read":
@@ -526,7 +530,9 @@ class DecodeModel:
                 seg += 1
 
     def run(self):
-        run_schedule(self, [self.producer()] + [self.consumer(w) for w in range(self.warps)])
+        # two producer warps issue the even and the odd units
+        run_schedule(self, [self.producer(pid, self.PRODUCERS) for pid in range(self.PRODUCERS)] +
+                     [self.consumer(w) for w in range(self.warps)])
 
 
 @pytest.mark.parametrize("hkv,warps", [(8, 8), (4, 8), (2, 8), (1, 8)])
