@@ -236,10 +236,11 @@ int la_p2p_close(void* peer_ptr);
 int la_p2p_free(void* ptr);
 
 /* Allocation-free form of la_paged_decode, for callers that cannot allocate
- * device memory where they run decode: a C/C++ host in the middle of a
- * stream capture (cudaMalloc cannot be captured), a runtime that hands out
- * device memory only from a fixed arena, or a latency-bound loop where an
- * allocation would synchronise the device. It has no counterpart in the
+ * device memory where they run decode: a host framework that owns every
+ * device allocation (a plugin may not call cudaMalloc behind its back), a
+ * runtime that hands out device memory only from a fixed arena reserved at
+ * start-up, or a latency-bound loop where an allocation would synchronise
+ * the device. It has no counterpart in the
  * reference (flash-attn allocates its own split buffers).
  * Same arguments and results as la_paged_decode without the workspace: the
  * split-KV partials live in a fixed LA_NOALLOC_SCRATCH_BYTES array inside

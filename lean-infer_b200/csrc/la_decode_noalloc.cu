@@ -4,11 +4,15 @@
 // instead of in a caller-provided workspace.
 //
 // Why: some callers of this library cannot call cudaMalloc at the point where
-// they run decode attention — a C or C++ host that is in the middle of a
-// stream capture (cudaMalloc is not a capturable operation), a runtime whose
+// they run decode attention — a host framework that owns every device
+// allocation (a plugin may not allocate behind its back), a runtime whose
 // device memory is a fixed arena handed out at start-up, or a latency-bound
 // loop where an allocation would synchronise the device. They pass the inputs
 // and outputs only.
+//
+// Set-up: the first call on each device resolves the array's device address
+// (loading the module in that device's context); make that first call before
+// any stream capture.
 //
 // Cost and limits: the array is LA_NOALLOC_SCRATCH_BYTES (4 MiB) of device
 // memory on every GPU that loads the library, held until the process exits.

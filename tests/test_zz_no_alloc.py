@@ -2,9 +2,9 @@
 against la_paged_decode, both called through the C ABI.
 
 Some callers cannot allocate device memory where they run decode attention:
-a C/C++ host in the middle of a stream capture (cudaMalloc cannot be
-captured), a runtime that only hands out a fixed arena, or a latency-bound
-loop where an allocation would synchronise the device. The allocation-free
+a host framework that owns every device allocation, a runtime that only
+hands out a fixed arena, or a latency-bound loop where an allocation would
+synchronise the device. The allocation-free
 entry point keeps the split-KV partials in a fixed array inside the library
 instead of a caller workspace; its results must match the workspace form's.
 
