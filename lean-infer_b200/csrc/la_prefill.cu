@@ -115,6 +115,7 @@ struct Params {
   int tq;    // tokens per query tile (128 / group)
   int tq_shift;  // log2(tq)
   int hq, hkv, group;
+  int hkv_shift;  // log2(hkv) when hkv is a power of two, else -1
   int causal;
   float scale_log2;
   __nv_bfloat16* out;
@@ -281,16 +282,15 @@ __device__ __forceinline__ bool walker_next(const Params& p, const WalkTable& t,
     w.count = level_count<kTable>(p, t, w.level);
   }
   const int idx = static_cast<int>(r - w.base);
-  const int ord = idx / p.hkv;  // the ord-th sequence (index order) that has this level's pair
+  // the ord-th sequence (index order) that has this level's pair
+  const int ord = p.hkv_shift >= 0 ? (idx >> p.hkv_shift) : idx / p.hkv;
   const int q0 = w.level * p.pair * p.tq;
   int seen = 0, s = 0;
   for (int b = 0; b < p.num_seqs; b += 32) {
     const unsigned m = __ballot_sync(0xffffffffu, seq_at_level<kTable>(p, t, b + lane, w.level));
     const int c = __popc(m);
     if (ord < seen + c) {
-      unsigned mm = m;
-      for (int k = seen; k < ord; ++k) mm &= mm - 1;  // drop the lower set bits
-      s = b + __ffs(mm) - 1;
+      s = b + static_cast<int>(__fns(m, 0, ord - seen + 1));  // its (ord - seen + 1)-th set bit
       break;
     }
     seen += c;
@@ -1104,6 +1104,7 @@ static int common_setup(const void* q, int64_t q_token_stride, int64_t q_head_st
   p->tq_shift = __builtin_ctz(static_cast<unsigned>(tq));
   p->hq = num_q_heads;
   p->hkv = num_kv_heads;
+  p->hkv_shift = (num_kv_heads & (num_kv_heads - 1)) == 0 ? __builtin_ctz(static_cast<unsigned>(num_kv_heads)) : -1;
   p->group = group;
   p->scale_log2 = softmax_scale * 1.4426950408889634f;
   p->out = static_cast<__nv_bfloat16*>(out);
