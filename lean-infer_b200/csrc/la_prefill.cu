@@ -105,6 +105,13 @@ constexpr int kOffWalk = off_xmax<true>() + 2 * 2 * kRows * 4;
 constexpr int kMaxSeqs = 256;
 constexpr size_t kSmemBytes = kOffWalk + 16 + 2 * kMaxSeqs + 1024;  // + the run-time 1024-byte alignment
 static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+// The split instance also keeps its first item (Walker at +0, Item at +32,
+// found flag at +80) and a copy of cu_seqlens [kMaxSeqs + 1], read before its
+// dependency wait and checked after it.
+constexpr int kOffFirst = (kOffWalk + 16 + 2 * kMaxSeqs + 15) & ~15;
+constexpr int kOffCu = kOffFirst + 96;
+constexpr size_t kSmemBytesSplit = kOffCu + 4 * (kMaxSeqs + 1) + 1024;
+static_assert(kSmemBytesSplit <= 227 * 1024, "shared memory per CTA (split instance)");
 
 struct Params {
   const int* cu;  // query starts [num_seqs + 1], or null: sequence s has q_len queries from token s * q_len
@@ -215,6 +222,8 @@ struct WalkTable {
   __device__ __forceinline__ int lv(int s) const {
     return reinterpret_cast<const uint16_t*>(smem + kOffWalk + 16)[s];
   }
+  // The split instance's copy of cu_seqlens (valid when cached()).
+  __device__ __forceinline__ int cu(int s) const { return reinterpret_cast<const int*>(smem + kOffCu)[s]; }
 };
 
 __device__ __forceinline__ int levels_of(const Params& p, int s) {
@@ -297,8 +306,18 @@ __device__ __forceinline__ bool walker_next(const Params& p, const WalkTable& t,
   }
   it.s = s;
   it.h = idx - ord * p.hkv;
-  it.seq0 = q_start<!kTable>(p, s);
-  it.L = q_count<!kTable>(p, s);
+  if constexpr (kTable) {
+    if (t.cached()) {
+      it.seq0 = t.cu(s);
+      it.L = t.cu(s + 1) - it.seq0;
+    } else {
+      it.seq0 = q_start<false>(p, s);
+      it.L = q_count<false>(p, s);
+    }
+  } else {
+    it.seq0 = q_start<true>(p, s);
+    it.L = q_count<true>(p, s);
+  }
   it.K = p.paged ? max(kTable ? p.k_lens[s] : __ldg(p.k_lens + s), 0) : it.L;
   it.off = it.K - it.L;
   it.q0 = q0;
@@ -308,6 +327,29 @@ __device__ __forceinline__ bool walker_next(const Params& p, const WalkTable& t,
   it.n = max(it.n0, it.n1);
   ++w.taken;
   return true;
+}
+
+// A role's walker: the split instance's roles take their first item (and
+// the walker state after it) from shared memory, where it was built before
+// the dependency wait; later items, and every item of the pair instance, are
+// walked by the role itself.
+template <bool kSplit>
+__device__ __forceinline__ void walker_start(const Params& p, const WalkTable& t, Walker& w) {
+  if constexpr (kSplit)
+    w.taken = 0;
+  else
+    walker_init<kSplit>(p, t, w);
+}
+template <bool kSplit>
+__device__ __forceinline__ bool walker_step(const Params& p, const WalkTable& t, Walker& w, Item& it) {
+  if constexpr (kSplit) {
+    if (w.taken == 0) {
+      w = *reinterpret_cast<const Walker*>(t.smem + kOffFirst);
+      it = *reinterpret_cast<const Item*>(t.smem + kOffFirst + 32);
+      return *reinterpret_cast<const int*>(t.smem + kOffFirst + 80) != 0;
+    }
+  }
+  return walker_next<kSplit>(p, t, w, it);
 }
 
 // kSplit (items of single query tiles): both softmax warpgroups work on tile
@@ -397,26 +439,71 @@ __global__ void __launch_bounds__(kThreads, 1)
     // before touching memory. (The pair instance, a full grid, measured
     // slower both ways.)
     setup();
-    grid_dependency_wait();
-    grid_launch_dependents();
+    // The walk table and the CTA's first item are built before the
+    // dependency wait, from cu_seqlens read through L2 only (so no stale line
+    // stays in L1), while the previous kernel still runs: measured inside a
+    // CUDA graph of one-prompt calls, building them after the wait (a cold
+    // first pass through this code on every SM) took 3.3-4.5 us before the
+    // first Q tile landed. After the wait cu_seqlens are read again; if any
+    // value changed (the previous kernel wrote them), everything is rebuilt.
+    // Paged keys (k_lens, maybe written by the previous kernel) and more
+    // than kMaxSeqs sequences build after the wait.
     uint16_t* lv = reinterpret_cast<uint16_t*>(smem + kOffWalk + 16);
     long long* total = reinterpret_cast<long long*>(smem + kOffWalk);
+    int* cuc = reinterpret_cast<int*>(smem + kOffCu);
     const bool cached = p.num_seqs <= kMaxSeqs && p.n_qp <= 65535;
-    if (threadIdx.x == 0) *reinterpret_cast<int*>(smem + kOffWalk + 8) = cached ? 1 : 0;
-    if (cached)
-      for (int s = threadIdx.x; s < p.num_seqs; s += kThreads) lv[s] = static_cast<uint16_t>(levels_of(p, s));
-    __syncthreads();
-    if (warp == 0) {
-      long long tot = 0;
-      for (int b = 0; b < p.num_seqs; b += 32) {
-        int n = (b + lane < p.num_seqs) ? (cached ? static_cast<int>(lv[b + lane]) : levels_of(p, b + lane)) : 0;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
-        tot += n;
+    auto build = [&]() {
+      if (threadIdx.x == 0) *reinterpret_cast<int*>(smem + kOffWalk + 8) = cached ? 1 : 0;
+      if (cached) {
+        for (int x = threadIdx.x; x <= p.num_seqs; x += kThreads) cuc[x] = p.cu ? __ldcg(p.cu + x) : x * p.q_len;
+        __syncthreads();
+        const int per = p.pair * p.tq;
+        for (int x = threadIdx.x; x < p.num_seqs; x += kThreads)
+          lv[x] = static_cast<uint16_t>(min((cuc[x + 1] - cuc[x] + per - 1) / per, p.n_qp));
       }
-      if (lane == 0) *total = tot * p.hkv;
+      __syncthreads();
+      if (warp == 0) {
+        long long tot = 0;
+        for (int b = 0; b < p.num_seqs; b += 32) {
+          int n = (b + lane < p.num_seqs) ? (cached ? static_cast<int>(lv[b + lane]) : levels_of(p, b + lane)) : 0;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+          tot += n;
+        }
+        if (lane == 0) *total = tot * p.hkv;
+        __syncwarp();
+        // the CTA's first item, for every role
+        Walker w;
+        walker_init<true>(p, wt, w);
+        Item it;
+        const bool have = walker_next<true>(p, wt, w, it);
+        if (lane == 0) {
+          *reinterpret_cast<Walker*>(smem + kOffFirst) = w;
+          *reinterpret_cast<Item*>(smem + kOffFirst + 32) = it;
+          *reinterpret_cast<int*>(smem + kOffFirst + 80) = have ? 1 : 0;
+        }
+      }
+      __syncthreads();
+    };
+    const bool early = cached && !p.paged;
+    if (early) {
+      if (warp == 13 && lane == 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_k);
+        tma_prefetch_desc(&tm_v);
+      }
+      build();
     }
-    __syncthreads();
+    grid_dependency_wait();
+    if (early) {
+      bool changed = false;
+      if (p.cu)
+        for (int x = threadIdx.x; x <= p.num_seqs; x += kThreads) changed |= __ldcg(p.cu + x) != cuc[x];
+      if (__syncthreads_or(changed)) build();
+    } else {
+      build();
+    }
+    grid_launch_dependents();
     // a CTA without work (its first item's rank is blockIdx.x) frees its
     // TMEM and leaves
     if (static_cast<long long>(blockIdx.x) >= wt.total()) {
@@ -449,11 +536,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* xmax = reinterpret_cast<float*>(smem + off_xmax<kSplit>());  // [step % 2][half][row]
     Walker& w = *reinterpret_cast<Walker*>(smem + off_state<kSplit>() + warp * 128);
     Item& it = *reinterpret_cast<Item*>(smem + off_state<kSplit>() + warp * 128 + 32);
-    walker_init<kSplit>(p, wt, w);
+    walker_start<kSplit>(p, wt, w);
     uint32_t t = 0;    // S_0 tiles seen
     uint32_t nst = 0;  // items whose statistics were written
     bool ok = true;
-    while (ok && walker_next<kSplit>(p, wt, w, it)) {
+    while (ok && walker_step<kSplit>(p, wt, w, it)) {
       const int ni = it.n0;
       const int tok = it.q0 + (row & (p.tq - 1));
       const int lim = p.causal ? min(max(tok + 1 + it.off, 0), it.K) : it.K;
@@ -683,12 +770,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     uint8_t* stage = smem + kOffStage + quarter * kStageBytes;
     Walker w;
-    walker_init<kSplit>(p, wt, w);
+    walker_start<kSplit>(p, wt, w);
     Item it;
     uint32_t cp[2] = {0, 0};       // PV_i so far (through this item)
     uint32_t items_i[2] = {0, 0};  // items in which tile i ran
     bool ok = true;
-    while (ok && walker_next<kSplit>(p, wt, w, it)) {
+    while (ok && walker_step<kSplit>(p, wt, w, it)) {
       for (int i = 0; i < 2 && ok; ++i) {
         const int ni = i ? it.n1 : it.n0;
         if (ni == 0) continue;
@@ -795,12 +882,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       Walker w;
-      walker_init<kSplit>(p, wt, w);
+      walker_start<kSplit>(p, wt, w);
       Item it;
       int kq = 0;
       long long nld = 0;  // K/V tiles loaded
       bool ok = true;
-      while (ok && walker_next<kSplit>(p, wt, w, it)) {
+      while (ok && walker_step<kSplit>(p, wt, w, it)) {
         if (lane == 0 && it.q0 + p.pair * p.tq >= p.n_qp * p.pair * p.tq && it.L > p.n_qp * p.pair * p.tq && p.err)
           atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);  // longer than max_seqlen: the tail is not computed
         if (!(ok = wait_all(q_empty, (kq & 1) ^ 1u))) break;
@@ -838,7 +925,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // which reads P(j) from the same columns (the tensor core executes this
       // thread's MMAs in order), while the softmax works on S(j+1).
       Walker w;
-      walker_init<kSplit>(p, wt, w);
+      walker_start<kSplit>(p, wt, w);
       Item it;
       int kq = 0;
       long long nld = 0;  // K/V ring position of the item's K(0)
@@ -870,7 +957,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++sc;
         return true;
       };
-      while (ok && walker_next<kSplit>(p, wt, w, it)) {
+      while (ok && walker_step<kSplit>(p, wt, w, it)) {
         if (!(ok = wait_all(q_full, kq & 1))) break;
         ++kq;
         const int n = it.n0;
@@ -1043,7 +1130,7 @@ int prefill_init(int device) {
                                        static_cast<int>(prefill::kSmemBytes));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(prefill::prefill_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(prefill::kSmemBytes));
+                             static_cast<int>(prefill::kSmemBytesSplit));
   return cuda_status(e);
 }
 
@@ -1072,7 +1159,7 @@ static int launch(const CUtensorMap& tq_map, const CUtensorMap& tk_map, const CU
   if (items > 0x7fffffffLL) return LA_ERR_UNSUPPORTED;
   const long long ctas = sms;  // one persistent CTA per SM (all of its TMEM and most of its shared memory)
   const dim3 grid(static_cast<unsigned>(items < ctas ? items : ctas));
-  return cuda_status(p.pair == 1 ? launch_pdl(prefill_kernel<true>, grid, dim3(kThreads), kSmemBytes, stream, tq_map,
+  return cuda_status(p.pair == 1 ? launch_pdl(prefill_kernel<true>, grid, dim3(kThreads), kSmemBytesSplit, stream, tq_map,
                                                tk_map, tv_map, p)
                                  : launch_pdl(prefill_kernel<false>, grid, dim3(kThreads), kSmemBytes, stream, tq_map,
                                               tk_map, tv_map, p));
