@@ -495,12 +495,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       build();
     }
     grid_dependency_wait();
+    int* pre = reinterpret_cast<int*>(smem + kOffFirst + 84);  // Q, K(0), V(0) already issued
     if (early) {
+      // The first item's Q, K(0) and V(0) are requested right away, while
+      // cu_seqlens are checked and the roles start (~2 us before the
+      // producer would reach them); if the check fails they are drained
+      // and their barriers initialised again.
+      const Item& f = *reinterpret_cast<const Item*>(smem + kOffFirst + 32);
+      const bool have = *reinterpret_cast<const int*>(smem + kOffFirst + 80) != 0;
+      if (warp == 13 && lane == 0) {
+        *pre = have ? 1 : 0;
+        if (have) {
+          mbar_arrive_expect_tx(q_full, kQTile);
+          for (int g = 0; g < p.group; ++g)
+            for (int half = 0; half < 2; ++half)
+              tma_load_3d(sQ + half * kQHalf + g * p.tq * 128, &tm_q, q_full, half * 64, f.h * p.group + g,
+                          f.seq0 + f.q0);
+          for (int kv = 0; kv < 2; ++kv) {
+            mbar_arrive_expect_tx(&kv_full[kv], kKVTile);
+            for (int half = 0; half < 2; ++half)
+              tma_load_3d(sKV + kv * kKVTile + half * kKVHalf, kv ? &tm_v : &tm_k, &kv_full[kv], half * 64, f.h,
+                          f.seq0);
+          }
+        }
+      }
       bool changed = false;
       if (p.cu)
         for (int x = threadIdx.x; x <= p.num_seqs; x += kThreads) changed |= __ldcg(p.cu + x) != cuc[x];
-      if (__syncthreads_or(changed)) build();
+      if (__syncthreads_or(changed)) {
+        if (threadIdx.x == 0 && *pre) {
+          mbar_wait(q_full, 0, nullptr, 0);
+          mbar_wait(&kv_full[0], 0, nullptr, 0);
+          mbar_wait(&kv_full[1], 0, nullptr, 0);
+          mbar_init(q_full, 1);
+          mbar_init(&kv_full[0], 1);
+          mbar_init(&kv_full[1], 1);
+          fence_barrier_init();
+          *pre = 0;
+        }
+        __syncthreads();
+        build();
+      }
     } else {
+      if (threadIdx.x == 0) *pre = 0;
       build();
     }
     grid_launch_dependents();
@@ -890,8 +927,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (ok && walker_step<kSplit>(p, wt, w, it)) {
         if (lane == 0 && it.q0 + p.pair * p.tq >= p.n_qp * p.pair * p.tq && it.L > p.n_qp * p.pair * p.tq && p.err)
           atomicCAS(p.err, 0, LA_DEVERR_SEQLEN);  // longer than max_seqlen: the tail is not computed
-        if (!(ok = wait_all(q_empty, (kq & 1) ^ 1u))) break;
-        if (lane == 0) {
+        // the split instance may have requested its first item's Q, K(0)
+        // and V(0) before the roles started
+        const bool pre0 = kSplit && kq == 0 && *reinterpret_cast<const int*>(smem + kOffFirst + 84) != 0;
+        if (!pre0 && !(ok = wait_all(q_empty, (kq & 1) ^ 1u))) break;
+        if (lane == 0 && !pre0) {
           mbar_arrive_expect_tx(q_full, (it.has1 ? 2 : 1) * kQTile);
           for (int t = 0; t < 1 + it.has1; ++t)
             for (int g = 0; g < p.group; ++g)
@@ -902,6 +942,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++kq;
         for (int j = 0; j < it.n && ok; ++j) {
           for (int kv = 0; kv < 2; ++kv, ++nld) {
+            if (pre0 && j == 0) continue;  // issued before the roles started
             const int st = static_cast<int>(nld % kStages);
             const uint32_t use = static_cast<uint32_t>(nld / kStages);
             if (!(ok = wait_all(&kv_empty[st], (use & 1) ^ 1u))) break;
