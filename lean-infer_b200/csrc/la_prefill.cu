@@ -55,6 +55,7 @@ constexpr int kQTile = 2 * kQHalf;     // 32 KB
 constexpr int kKVHalf = kKeys * 128;   // one 64-dim half of a K or V tile: 16 KB
 constexpr int kKVTile = 2 * kKVHalf;   // 32 KB
 constexpr int kStages = 4;             // K/V ring (K(j) and V(j) take one stage each)
+static_assert(kStages >= 4, "the split instance requests its first two K/V tiles into stages 0..3 at once");
 constexpr int kThreads = 512;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;        // O_i at kColO + 128 i; S_i at 128 i
@@ -497,10 +498,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     grid_dependency_wait();
     int* pre = reinterpret_cast<int*>(smem + kOffFirst + 84);  // Q, K(0), V(0) already issued
     if (early) {
-      // The first item's Q, K(0) and V(0) are requested right away, while
-      // cu_seqlens are checked and the roles start (~2 us before the
-      // producer would reach them); if the check fails they are drained
-      // and their barriers initialised again.
+      // The first item's Q and its first two K/V tiles (the whole 4-stage
+      // ring) are requested right away, while cu_seqlens are checked and the
+      // roles start (~2 us before the producer would reach them); if the
+      // check fails they are drained and their barriers initialised again.
       const Item& f = *reinterpret_cast<const Item*>(smem + kOffFirst + 32);
       const bool have = *reinterpret_cast<const int*>(smem + kOffFirst + 80) != 0;
       if (warp == 13 && lane == 0) {
@@ -511,11 +512,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int half = 0; half < 2; ++half)
               tma_load_3d(sQ + half * kQHalf + g * p.tq * 128, &tm_q, q_full, half * 64, f.h * p.group + g,
                           f.seq0 + f.q0);
-          for (int kv = 0; kv < 2; ++kv) {
-            mbar_arrive_expect_tx(&kv_full[kv], kKVTile);
+          for (int x = 0; x < 2 * min(f.n, 2); ++x) {  // K(0), V(0), K(1), V(1): ring stage x
+            mbar_arrive_expect_tx(&kv_full[x], kKVTile);
             for (int half = 0; half < 2; ++half)
-              tma_load_3d(sKV + kv * kKVTile + half * kKVHalf, kv ? &tm_v : &tm_k, &kv_full[kv], half * 64, f.h,
-                          f.seq0);
+              tma_load_3d(sKV + x * kKVTile + half * kKVHalf, (x & 1) ? &tm_v : &tm_k, &kv_full[x], half * 64, f.h,
+                          f.seq0 + (x >> 1) * kKeys);
           }
         }
       }
@@ -525,11 +526,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__syncthreads_or(changed)) {
         if (threadIdx.x == 0 && *pre) {
           mbar_wait(q_full, 0, nullptr, 0);
-          mbar_wait(&kv_full[0], 0, nullptr, 0);
-          mbar_wait(&kv_full[1], 0, nullptr, 0);
           mbar_init(q_full, 1);
-          mbar_init(&kv_full[0], 1);
-          mbar_init(&kv_full[1], 1);
+          for (int x = 0; x < 2 * min(f.n, 2); ++x) {
+            mbar_wait(&kv_full[x], 0, nullptr, 0);
+            mbar_init(&kv_full[x], 1);
+          }
           fence_barrier_init();
           *pre = 0;
         }
@@ -942,7 +943,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++kq;
         for (int j = 0; j < it.n && ok; ++j) {
           for (int kv = 0; kv < 2; ++kv, ++nld) {
-            if (pre0 && j == 0) continue;  // issued before the roles started
+            if (pre0 && j < 2) continue;  // issued before the roles started
             const int st = static_cast<int>(nld % kStages);
             const uint32_t use = static_cast<uint32_t>(nld / kStages);
             if (!(ok = wait_all(&kv_empty[st], (use & 1) ^ 1u))) break;
