@@ -345,6 +345,10 @@ template <bool kSplit>
 __device__ __forceinline__ bool walker_step(const Params& p, const WalkTable& t, Walker& w, Item& it) {
   if constexpr (kSplit) {
     if (w.taken == 0) {
+      // checked against cu_seqlens after the dependency wait (v_bar, at the
+      // barrier area's word 41)
+      uint64_t* v_bar = reinterpret_cast<uint64_t*>(const_cast<uint8_t*>(t.smem) + kOffBar) + 41;
+      if (!__all_sync(0xffffffffu, mbar_wait(v_bar, 0, p.err, LA_DEVERR_WAIT_TIMEOUT))) return false;
       w = *reinterpret_cast<const Walker*>(t.smem + kOffFirst);
       it = *reinterpret_cast<const Item*>(t.smem + kOffFirst + 32);
       return *reinterpret_cast<const int*>(t.smem + kOffFirst + 80) != 0;
@@ -390,6 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // before the next S, so s_free may lag the epilogue by more than one phase
   // and its parity cannot name the item's last PV.
   uint64_t* o_full = bars + 40;
+  // kSplit: the first item (built before the dependency wait) checked
+  // against cu_seqlens read after it; every role waits here before using it.
+  uint64_t* v_bar = bars + 41;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -412,7 +419,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(&o_empty[i], 128);
         mbar_init(&st_full[i], kSplit && i == 0 ? 256 : 128);
         if (kSplit) {
-          if (i == 0) mbar_init(o_full, 1);
+          if (i == 0) {
+            mbar_init(o_full, 1);
+            mbar_init(v_bar, 1);
+          }
           mbar_init(&x_full[i], 128);
           mbar_init(&x_full[i + 2], 128);
           mbar_init(&ph_full[i], 128);
@@ -495,13 +505,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       build();
     }
+    // whether this CTA has no item, decided from the table every thread saw
+    // (warp 14 may rewrite it after the wait)
+    bool nowork = early && static_cast<long long>(blockIdx.x) >= wt.total();
     grid_dependency_wait();
-    int* pre = reinterpret_cast<int*>(smem + kOffFirst + 84);  // Q, K(0), V(0) already issued
+    int* pre = reinterpret_cast<int*>(smem + kOffFirst + 84);  // Q and the first K/V tiles already issued
     if (early) {
       // The first item's Q and its first two K/V tiles (the whole 4-stage
-      // ring) are requested right away, while cu_seqlens are checked and the
-      // roles start (~2 us before the producer would reach them); if the
-      // check fails they are drained and their barriers initialised again.
+      // ring) are requested right away. Warp 14 (idle otherwise) reads
+      // cu_seqlens again while the roles start, and releases them through
+      // v_bar: each role waits there before its first item. If a value
+      // changed, warp 14 alone drains the early copies, initialises their
+      // barriers again and rebuilds the table and the first item.
       const Item& f = *reinterpret_cast<const Item*>(smem + kOffFirst + 32);
       const bool have = *reinterpret_cast<const int*>(smem + kOffFirst + 80) != 0;
       if (warp == 13 && lane == 0) {
@@ -520,33 +535,67 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      bool changed = false;
-      if (p.cu)
-        for (int x = threadIdx.x; x <= p.num_seqs; x += kThreads) changed |= __ldcg(p.cu + x) != cuc[x];
-      if (__syncthreads_or(changed)) {
-        if (threadIdx.x == 0 && *pre) {
-          mbar_wait(q_full, 0, nullptr, 0);
-          mbar_init(q_full, 1);
-          for (int x = 0; x < 2 * min(f.n, 2); ++x) {
-            mbar_wait(&kv_full[x], 0, nullptr, 0);
-            mbar_init(&kv_full[x], 1);
+      if (warp == 14) {
+        bool changed = false;
+        if (p.cu)
+          for (int x = lane; x <= p.num_seqs; x += 32) changed |= __ldcg(p.cu + x) != cuc[x];
+        if (__any_sync(0xffffffffu, changed)) {
+          if (lane == 0 && have) {  // the copies warp 13 requested (it set *pre before them)
+            const int nkv = 2 * min(f.n, 2);
+            mbar_wait(q_full, 0, nullptr, 0);
+            mbar_init(q_full, 1);
+            for (int x = 0; x < nkv; ++x) {
+              mbar_wait(&kv_full[x], 0, nullptr, 0);
+              mbar_init(&kv_full[x], 1);
+            }
+            fence_barrier_init();
+            *pre = 0;
           }
-          fence_barrier_init();
-          *pre = 0;
+          __syncwarp();
+          for (int x = lane; x <= p.num_seqs; x += 32) cuc[x] = p.cu ? __ldcg(p.cu + x) : x * p.q_len;
+          __syncwarp();
+          const int per = p.pair * p.tq;
+          for (int x = lane; x < p.num_seqs; x += 32)
+            lv[x] = static_cast<uint16_t>(min((cuc[x + 1] - cuc[x] + per - 1) / per, p.n_qp));
+          __syncwarp();
+          long long tot = 0;
+          for (int b = 0; b < p.num_seqs; b += 32) {
+            int n = (b + lane < p.num_seqs) ? static_cast<int>(lv[b + lane]) : 0;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) n += __shfl_xor_sync(0xffffffffu, n, o);
+            tot += n;
+          }
+          if (lane == 0) *total = tot * p.hkv;
+          __syncwarp();
+          Walker w;
+          walker_init<true>(p, wt, w);
+          Item it;
+          const bool h2 = walker_next<true>(p, wt, w, it);
+          if (lane == 0) {
+            *reinterpret_cast<Walker*>(smem + kOffFirst) = w;
+            *reinterpret_cast<Item*>(smem + kOffFirst + 32) = it;
+            *reinterpret_cast<int*>(smem + kOffFirst + 80) = h2 ? 1 : 0;
+          }
         }
-        __syncthreads();
-        build();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(v_bar);  // release semantics: the writes above are visible to its waiters
       }
     } else {
       if (threadIdx.x == 0) *pre = 0;
       build();
+      if (threadIdx.x == 0) mbar_arrive(v_bar);
+      nowork = static_cast<long long>(blockIdx.x) >= wt.total();
     }
     grid_launch_dependents();
     // a CTA without work (its first item's rank is blockIdx.x) frees its
-    // TMEM and leaves
-    if (static_cast<long long>(blockIdx.x) >= wt.total()) {
-      if (warp == 12) tmem_dealloc(*tmem_slot, kTmemCols);
-      return;
+    // TMEM and leaves, once the item count is checked; a CTA that turns out
+    // to have none after the check runs its roles, which find no item
+    if (nowork) {
+      mbar_wait(v_bar, 0, p.err, LA_DEVERR_WAIT_TIMEOUT);
+      if (static_cast<long long>(blockIdx.x) >= wt.total()) {
+        if (warp == 12) tmem_dealloc(*tmem_slot, kTmemCols);
+        return;
+      }
     }
   } else {
     grid_dependency_wait();

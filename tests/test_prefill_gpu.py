@@ -182,3 +182,35 @@ def test_sdpa_single_prompt_strided_views(pkg, cuda_dev):
     torch.cuda.synchronize()
     ref = opa.varlen_causal_prefill(q, k, v, cu)
     assert (out[0].transpose(0, 1).cpu().float() - ref).abs().max().item() <= TOL
+
+
+def test_cu_seqlens_rewritten_on_the_stream_between_calls(pkg, cuda_dev):
+    """The one-prompt kernel instance reads cu_seqlens before its dependency
+    wait (to walk to its first item early) and checks them again after it.
+    Here the same cu_seqlens tensor is overwritten on the stream right before
+    each call, with different lengths each time, and no synchronisation in
+    between: every call must see its own lengths (against the oracle)."""
+    lens_list = [[300, 200], [100, 700], [640], [2, 511, 64], [129, 127]]
+    cases = [_case(l, seed=40 + i) for i, l in enumerate(lens_list)]
+    T = max(int(c[3][-1]) for c in cases)
+    q_d = torch.zeros(T, 16, 128, dtype=torch.bfloat16, device=cuda_dev)
+    k_d = torch.zeros(T, 8, 128, dtype=torch.bfloat16, device=cuda_dev)
+    v_d = torch.zeros(T, 8, 128, dtype=torch.bfloat16, device=cuda_dev)
+    cu_d = torch.zeros(4, dtype=torch.int32, device=cuda_dev)
+    staged = [(c[0].to(cuda_dev), c[1].to(cuda_dev), c[2].to(cuda_dev), c[3].to(cuda_dev)) for c in cases]
+    outs = []
+    torch.cuda.synchronize()
+    for (q, k, v, cu), (_, _, _, cu_h, mx) in zip(staged, cases):
+        n = q.shape[0]
+        q_d[:n].copy_(q)
+        k_d[:n].copy_(k)
+        v_d[:n].copy_(v)
+        cu_view = cu_d[: cu.numel()]
+        cu_view.copy_(cu)  # a device copy on the stream, just before the kernel
+        out = pkg.flash_attn_varlen_func(q_d[:n], k_d[:n], v_d[:n], cu_view, cu_view, mx, mx, causal=True)
+        outs.append(out[:n].clone())
+    torch.cuda.synchronize()
+    pkg.check_device_errors(cuda_dev.index)
+    for (q, k, v, cu, _), out in zip(cases, outs):
+        ref = opa.varlen_causal_prefill(q, k, v, cu)
+        assert (out.cpu().float() - ref).abs().max().item() <= TOL
