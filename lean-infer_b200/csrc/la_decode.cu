@@ -794,8 +794,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ combine
-// Grid (batch, Hq), one warp per (sequence, query head); lane l owns dims
-// 4l..4l+3. Sequences whose key range lies inside one CTA's range were
+// Grid (batch, Hq / warps per CTA), one warp per (sequence, query head) (a
+// CTA is one warp, or up to kCombinePeerWarps with peer stores); lane l owns
+// dims 4l..4l+3. Sequences whose key range lies inside one CTA's range were
 // written directly by the decode kernel and are skipped. Rows over a few
 // CTAs (at most kCombineFew) merge their slots one after another. The others
 // merge their partials: up to 32 slots per round, one per lane (each lane finds
@@ -817,10 +818,16 @@ __device__ __forceinline__ float warp_sum_all(float v) {
   return v;
 }
 
-__global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p, int grid) {
+// With peer stores (the KV-head-sharded all-gather) a CTA holds kCombinePeerWarps
+// warps, one query head each, so that it ends with one system-scope fence for
+// all of them: one fence per one-warp CTA, 2048 of them at 256 rows x 8 heads,
+// cost 6.4 us per layer on one GPU. Otherwise a CTA is one warp.
+constexpr int kCombinePeerWarps = 4;
+
+__global__ void __launch_bounds__(32 * kCombinePeerWarps, 1) paged_decode_combine_kernel(const Params p, int grid) {
   const int b = blockIdx.x;
-  const int hh = blockIdx.y;
-  const int lane = threadIdx.x;
+  const int hh = blockIdx.y * static_cast<int>(blockDim.x >> 5) + static_cast<int>(threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   const float NEG_INF = -__int_as_float(0x7f800000);
 
   // T (all units) and P_b (units before sequence b). They depend only on
@@ -983,12 +990,12 @@ __global__ void __launch_bounds__(32) paged_decode_combine_kernel(const Params p
     }
   }
   if (p.peer_stores) {
-    // One system-scope fence per CTA: __syncwarp orders every lane's peer
-    // stores before lane 0's fence, which is cumulative over them, so the
-    // epoch the barrier kernel publishes next on this stream (a release at
-    // system scope, after this grid completes) orders after all of them.
-    __syncwarp();
-    if (lane == 0) __threadfence_system();
+    // One system-scope fence per CTA: __syncthreads orders every thread's
+    // peer stores before thread 0's fence, which is cumulative over them, so
+    // the epoch the barrier kernel publishes next on this stream (a release
+    // at system scope, after this grid completes) orders after all of them.
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
   }
 }
 
@@ -1210,7 +1217,15 @@ static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_he
     e = batch <= 256 ? launch_pdl(paged_decode_kernel<2, 8>, dim3(grid), dim3(threads), smem, stream, tq, tk, tv, tk1, tv1, p)
                      : launch_pdl(paged_decode_kernel<2, 32>, dim3(grid), dim3(threads), smem, stream, tq, tk, tv, tk1, tv1, p);
   if (e != cudaSuccess) return cuda_status(e);
-  e = launch_pdl(paged_decode_combine_kernel, dim3(batch, num_q_heads), dim3(32), 0, stream, p, grid);
+  // peer stores: kCombinePeerWarps heads per CTA (fewer when they do not divide the heads)
+  int wpc = 1;
+  if (peers)
+    for (int c = kCombinePeerWarps; c > 1; c >>= 1)
+      if (num_q_heads % c == 0) {
+        wpc = c;
+        break;
+      }
+  e = launch_pdl(paged_decode_combine_kernel, dim3(batch, num_q_heads / wpc), dim3(32 * wpc), 0, stream, p, grid);
   return cuda_status(e);
 }
 
