@@ -824,6 +824,17 @@ __device__ __forceinline__ float warp_sum_all(float v) {
 // cost 6.4 us per layer on one GPU. Otherwise a CTA is one warp.
 constexpr int kCombinePeerWarps = 4;
 
+// kMany: the instance for small batches, whose rows are split over many
+// CTAs (one round of up to 32 slots): the round's first kManyBatch O rows
+// are loaded together with its lse values, so a row over up to 16 CTAs is
+// merged after one load round trip (the general path loads the lse, then the
+// O rows of the slots that hold keys 8 at a time: four dependent round trips
+// for a row over 18 CTAs). Slots are read whether or not they hold keys;
+// those without are skipped by a warp-uniform test, never weighted by zero,
+// so whatever they hold does not reach the sum.
+constexpr int kManyBatch = 16;
+
+template <bool kMany>
 __global__ void __launch_bounds__(32 * kCombinePeerWarps, 1) paged_decode_combine_kernel(const Params p, int grid) {
   const int b = blockIdx.x;
   const int hh = blockIdx.y * static_cast<int>(blockDim.x >> 5) + static_cast<int>(threadIdx.x >> 5);
@@ -933,6 +944,71 @@ __global__ void __launch_bounds__(32 * kCombinePeerWarps, 1) paged_decode_combin
       v.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
       for (int r = 0; r < p.nouts; ++r) *reinterpret_cast<uint2*>(p.outs[r] + oofs) = v;
       if (lse && lane == 0) *lse = l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
+    } else if constexpr (kMany) {
+      float m = NEG_INF, l = 0.f;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (long long c0 = cf; c0 <= cl; c0 += 32) {
+        const long long c = c0 + lane;
+        const int slot = c0 == cf ? first_round : (c <= cl ? slot_of(c) : -1);
+        const int nr = static_cast<int>(cl - c0 + 1 < 32 ? cl - c0 + 1 : 32);  // lanes of this round
+        const float ls = slot >= 0 ? p.part_lse[static_cast<long long>(slot) * p.hq + hh] : NEG_INF;
+        int su[kManyBatch];
+        float4 ov[kManyBatch];
+#pragma unroll
+        for (int k = 0; k < kManyBatch; ++k) su[k] = __shfl_sync(0xffffffffu, slot, k);
+#pragma unroll
+        for (int k = 0; k < kManyBatch; ++k)
+          ov[k] = (k < nr && su[k] >= 0) ? *reinterpret_cast<const float4*>(
+                                               p.part_o + (static_cast<long long>(su[k]) * p.hq + hh) * kD + lane * 4)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float mr = warp_max_all(ls);
+        if (mr == NEG_INF) continue;  // warp-uniform: no keys in this round
+        const float mn = fmaxf(m, mr);
+        const float a = ex2(m - mn);  // 0 while m is -inf
+        const bool use = slot >= 0 && ls != NEG_INF;
+        const float wl = use ? ex2(ls - mn) : 0.f;
+        l = l * a + warp_sum_all(wl);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[k] *= a;
+        m = mn;
+        const unsigned usem = __ballot_sync(0xffffffffu, use);
+#pragma unroll
+        for (int k = 0; k < kManyBatch; ++k) {
+          const float w = __shfl_sync(0xffffffffu, wl, k);
+          if ((usem >> k) & 1u) {
+            acc[0] += w * ov[k].x;
+            acc[1] += w * ov[k].y;
+            acc[2] += w * ov[k].z;
+            acc[3] += w * ov[k].w;
+          }
+        }
+        for (int j0 = kManyBatch; j0 < nr; j0 += kManyBatch) {
+#pragma unroll
+          for (int k = 0; k < kManyBatch; ++k) su[k] = __shfl_sync(0xffffffffu, slot, (j0 + k) & 31);
+#pragma unroll
+          for (int k = 0; k < kManyBatch; ++k)
+            ov[k] = (j0 + k < nr && ((usem >> ((j0 + k) & 31)) & 1u))
+                        ? *reinterpret_cast<const float4*>(p.part_o + (static_cast<long long>(su[k]) * p.hq + hh) * kD +
+                                                           lane * 4)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int k = 0; k < kManyBatch; ++k) {
+            const float w = __shfl_sync(0xffffffffu, wl, (j0 + k) & 31);
+            if (j0 + k < nr && ((usem >> ((j0 + k) & 31)) & 1u)) {
+              acc[0] += w * ov[k].x;
+              acc[1] += w * ov[k].y;
+              acc[2] += w * ov[k].z;
+              acc[3] += w * ov[k].w;
+            }
+          }
+        }
+      }
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint2 v;
+      v.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+      v.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+      for (int r = 0; r < p.nouts; ++r) *reinterpret_cast<uint2*>(p.outs[r] + oofs) = v;
+      if (lse && lane == 0) *lse = l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : NEG_INF;
     } else {
       float m = NEG_INF, l = 0.f;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1031,7 +1107,8 @@ int decode_init(int device) {
     e = cudaFuncSetAttribute(decode::paged_decode_kernel<2, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
   if (e == cudaSuccess) {
     cudaFuncAttributes a;
-    e = cudaFuncGetAttributes(&a, decode::paged_decode_combine_kernel);
+    e = cudaFuncGetAttributes(&a, decode::paged_decode_combine_kernel<false>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a, decode::paged_decode_combine_kernel<true>);
   }
   return cuda_status(e);
 }
@@ -1225,7 +1302,12 @@ static int paged_decode_impl(const void* q, int64_t q_batch_stride, int64_t q_he
         wpc = c;
         break;
       }
-  e = launch_pdl(paged_decode_combine_kernel, dim3(batch, num_q_heads / wpc), dim3(32 * wpc), 0, stream, p, grid);
+  // Rows over more than kCombineFew CTAs on average (batch * kCombineFew <
+  // grid) take the many-slot instance.
+  const dim3 cgrid(batch, num_q_heads / wpc), cblock(32 * wpc);
+  e = static_cast<long long>(batch) * kCombineFew < grid
+          ? launch_pdl(paged_decode_combine_kernel<true>, cgrid, cblock, 0, stream, p, grid)
+          : launch_pdl(paged_decode_combine_kernel<false>, cgrid, cblock, 0, stream, p, grid);
   return cuda_status(e);
 }
 
